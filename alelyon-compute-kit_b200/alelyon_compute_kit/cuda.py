@@ -1,0 +1,163 @@
+"""vq4 operations on device-resident PyTorch tensors.
+
+The same kernels, plans and admission as `VQDevice`, reached through the C
+ABI's device-pointer entry `ack_vq_launch`: operands are CUDA tensors (code
+words as int32 bit patterns), work is enqueued on the current PyTorch stream
+of the tensors' device, nothing is copied to or from the host and nothing
+synchronises unless asked (`check`). PyTorch supplies device memory,
+streams and `torch.distributed`; the arithmetic is the library's.
+
+Every function refuses, by raising, when the library is missing or a tensor
+is not on a CUDA device: there is no CPU path here.
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+
+import torch
+
+from . import ack
+
+ENTRIES = 16
+OP_ENCODE1, OP_DECODE1, OP_MATMUL1, OP_ADAMW1 = 0, 1, 2, 3
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE = range(16, 23)
+
+
+def words_for(count: int, group: int) -> int:
+    """u32 words of the packed image of `count` values."""
+    return ((count + group - 1) // group + 7) // 8
+
+
+def plan1(op, m, n, k, group, flags=0) -> bytes:
+    return struct.pack("<8I", op, m, n, k, group, ENTRIES, flags, 0)
+
+
+def plan2(op, m, n, k, group, flags=0, batch=1, aux0=0, aux1=0, aux2=0) -> bytes:
+    return struct.pack("<16I", op, m, n, k, group, ENTRIES, flags, 0, batch, aux0, aux1, aux2, 0, 0, 0, 0)
+
+
+def _nbytes(t: torch.Tensor | None) -> int:
+    return 0 if t is None else t.numel() * t.element_size()
+
+
+def launch(plan: bytes, slots, stream: torch.cuda.Stream | None = None) -> None:
+    """Enqueue one plan. `slots` lists the operand tensors in the plan's slot
+    order (6 for a 32-byte plan, 8 for a 64-byte plan); None = unused."""
+    lib = ack._lib()
+    ops = ack.AckVqOperands()
+    ops.size = ctypes.sizeof(ops)
+    ops.nslots = len(slots)
+    device = None
+    for i, t in enumerate(slots):
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ack.AckError(f"vq operand {i} is not a CUDA tensor")
+        if not t.is_contiguous():
+            raise ack.AckError(f"vq operand {i} is not contiguous")
+        device = device or t.device
+        if t.device != device:
+            raise ack.AckError("vq operands live on different devices")
+        ops.ptr[i] = t.data_ptr()
+        ops.bytes[i] = _nbytes(t)
+    if device is None:
+        raise ack.AckError("vq launch without operands")
+    with torch.cuda.device(device):
+        s = stream if stream is not None else torch.cuda.current_stream(device)
+        rc = lib.cdll.ack_vq_launch(plan, len(plan), ctypes.byref(ops), ctypes.c_void_p(s.cuda_stream))
+    if rc != ack.ACK_OK:
+        raise ack._kit_error("vq", rc, lib.last_error())
+
+
+def status_word(device) -> torch.Tensor:
+    """A cleared status word (the caller clears it, vq4.comp:5-8)."""
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check(status: torch.Tensor) -> None:
+    """Synchronise on the status word and raise on any set bit."""
+    flags = int(status.item()) & 0xFFFFFFFF
+    if flags:
+        raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+
+
+def decode(codes, book, count: int, group: int, *, out=None, status=None):
+    """Dense float32 values of a packed image (64-bit count)."""
+    out = torch.empty(count, dtype=torch.float32, device=codes.device) if out is None else out
+    status = status_word(codes.device) if status is None else status
+    launch(plan2(OP_DECODE, count & 0xFFFFFFFF, 1, 1, group, aux0=count >> 32),
+           [codes, book, None, None, None, out, None, status])
+    return out, status
+
+
+def encode(x, book, group: int, *, out=None, status=None):
+    """Packed image of a float32 tensor; the reference CPU encoder's bytes."""
+    count = x.numel()
+    out = torch.empty(words_for(count, group), dtype=torch.int32, device=x.device) if out is None else out
+    status = status_word(x.device) if status is None else status
+    launch(plan2(OP_ENCODE, count & 0xFFFFFFFF, 1, 1, group, aux0=count >> 32),
+           [x, book, None, None, None, out, None, status])
+    return out, status
+
+
+def dense(x, codes, books, n: int, group: int, *, transpose_b: bool = True, out=None, status=None):
+    """Y[e] = X[e] @ decode(W[e]).T (W[e] stored n x k) for e < E, one launch.
+    `x` (E, M, K) float32; `codes` (E, words) int32; `books` (E, 16, group)."""
+    e, m, k = x.shape
+    out = torch.empty((e, m, n), dtype=torch.float32, device=x.device) if out is None else out
+    status = status_word(x.device) if status is None else status
+    launch(plan2(OP_DENSE, m, n, k, group, flags=2 if transpose_b else 0, batch=e),
+           [x, codes, books, None, None, out, None, status])
+    return out, status
+
+
+def coded(a_codes, a_book, b_codes, b_book, m: int, n: int, k: int, group: int, *, flags: int = 2,
+          out=None, status=None):
+    """C = op(decode A) @ op(decode B); flags bit 0: A stored K x M, bit 1: B stored N x K."""
+    out = torch.empty((m, n), dtype=torch.float32, device=a_codes.device) if out is None else out
+    status = status_word(a_codes.device) if status is None else status
+    launch(plan2(OP_CODED, m, n, k, group, flags=flags), [a_codes, a_book, b_codes, b_book, None, out, None, status])
+    return out, status
+
+
+def matmul_exact(a_codes, a_book, b_codes, b_book, m: int, n: int, k: int, group: int, *, flags: int = 0,
+                 out=None, status=None):
+    """The reference's bounded packed-pair product (schema-1 op 2)."""
+    out = torch.empty((m, n), dtype=torch.float32, device=a_codes.device) if out is None else out
+    status = status_word(a_codes.device) if status is None else status
+    launch(plan1(OP_MATMUL1, m, n, k, group, flags), [a_codes, a_book, b_codes, b_book, out, status])
+    return out, status
+
+
+def adamw_sample(codes, books, coefs, positions, count: int, group: int, *, batch: int = 1, out=None, status=None):
+    """AdamW values of the sample vectors `positions` for each expert: (E, 3, S, group)."""
+    s = positions.numel()
+    out = torch.empty((batch, 3, s, group), dtype=torch.float32, device=codes.device) if out is None else out
+    status = status_word(codes.device) if status is None else status
+    launch(plan2(OP_ADAMW_SAMPLE, count, 1, 1, group, batch=batch, aux0=s),
+           [codes, books, coefs, positions, None, out, None, status])
+    return out, status
+
+
+def adamw_usage(codes, books, coefs, trial, count: int, group: int, state: int, expert: int = 0, *, batch: int = 1,
+                out=None, status=None):
+    """How many complete vectors of one updated state each entry of `trial` wins."""
+    out = torch.empty(ENTRIES, dtype=torch.int32, device=codes.device) if out is None else out
+    status = status_word(codes.device) if status is None else status
+    launch(plan2(OP_ADAMW_USAGE, count, 1, 1, group, batch=batch, aux0=state, aux1=expert),
+           [codes, books, coefs, trial, None, out, None, status])
+    return out, status
+
+
+def adamw_encode(codes, books, coefs, new_books, count: int, group: int, *, batch: int = 1, out=None, changed=None,
+                 status=None):
+    """Decode, update and re-encode W, M, V of each expert: codes (E, 3, words), changed (E,)."""
+    words = words_for(count, group)
+    dev = codes.device
+    out = torch.empty((batch, 3, words), dtype=torch.int32, device=dev) if out is None else out
+    changed = torch.empty(batch, dtype=torch.int32, device=dev) if changed is None else changed
+    status = status_word(dev) if status is None else status
+    launch(plan2(OP_ADAMW_ENCODE, count, 1, 1, group, batch=batch),
+           [codes, books, coefs, new_books, None, out, changed, status])
+    return out, changed, status

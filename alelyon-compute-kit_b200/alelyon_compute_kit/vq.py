@@ -1,0 +1,682 @@
+"""Vector-coded tensors (vq4/v1) and their B200 operations.
+
+Drop-in for the reference's `vq` module (`src/alelyon_compute_kit/_kit/python/
+vq.py`): the same format and public names (`storage_layout`, `VQArray`,
+`encode`, `fit_codebook`, `VQDevice`, `VQAdamW`), the same validation and
+refusal messages, the same bounds on the schema-1 device calls.
+
+Each 4-bit index selects one of 16 FP32 code vectors of 8, 16 or 32 values;
+one codebook per tensor; eight indices per little-endian u32 word.
+
+CPU work, as in the reference: `fit_codebook` (Lloyd iterations on a strided
+calibration sample) and the module-level `encode`, which `fit_codebook` uses
+on that sample. Device work goes through `VQDevice` and the C ABI; there is
+no CPU fallback on that path.
+
+Additions, all on `VQDevice` and none changing an existing signature:
+`matmul_dense` / `matmul_dense_grouped` (FP32 activations times coded
+weights), `matmul_coded` (both operands coded, no MAC bound),
+`encode_large` / `decode_large` (64-bit value counts), and `adamw_fused`,
+which `VQAdamW.step` uses to update, refit and re-encode all three states
+with one device round trip per phase instead of seven.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import operator
+import struct
+from contextlib import ExitStack
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import ack
+
+SCHEMA = 1
+GROUPS = (8, 16, 32)
+ENTRIES = 16
+MAX_ELEMENTS = 268_435_456
+MAX_MATMUL_MACS = 268_435_456
+_HEADER = struct.Struct("<8sIIIIQQ")
+_MAGIC = b"ACKVQ4\0\0"
+
+# schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE = range(16, 23)
+
+
+def _integer(value, name: str, minimum: int, maximum: int) -> int:
+    if isinstance(value, (bool, np.bool_)):
+        raise ValueError(f"{name} must be an integer")
+    try:
+        result = operator.index(value)
+    except TypeError as exc:
+        raise ValueError(f"{name} must be an integer") from exc
+    if not minimum <= result <= maximum:
+        raise ValueError(f"{name} must be in {minimum}..{maximum}")
+    return result
+
+
+def _shape(shape) -> tuple[int, ...]:
+    result = tuple(_integer(x, "dimension", 1, MAX_ELEMENTS) for x in shape)
+    if not 1 <= len(result) <= 6 or math.prod(result) > MAX_ELEMENTS:
+        raise ValueError("vq shape requires rank 1..6 and a bounded element count")
+    return result
+
+
+def _group(group) -> int:
+    group = _integer(group, "group", 8, 32)
+    if group not in GROUPS:
+        raise ValueError("vq group must be 8, 16 or 32")
+    return group
+
+
+def _float_array(value, name: str) -> np.ndarray:
+    result = np.asarray(value)
+    if result.dtype != np.dtype("float32") or not np.isfinite(result).all():
+        raise ValueError(f"{name} must contain finite float32 values")
+    return np.ascontiguousarray(result)
+
+
+def _book(value, group: int) -> np.ndarray:
+    result = _float_array(value, "codebook")
+    if result.shape != (ENTRIES, group):
+        raise ValueError(f"codebook must have shape (16, {group})")
+    return result
+
+
+def storage_layout(shape, group: int = 16) -> dict:
+    """Byte accounting of one coded tensor, padding and codebook included."""
+    shape, group = _shape(shape), _group(group)
+    elements = math.prod(shape)
+    vectors = (elements + group - 1) // group
+    codes = ((vectors + 7) // 8) * 4
+    book = ENTRIES * group * 4
+    metadata = _HEADER.size + 8 * len(shape)
+    total = codes + book + metadata
+    return {"elements": elements, "vectors": vectors, "code_bytes": codes,
+            "codebook_bytes": book, "metadata_bytes": metadata,
+            "serialized_bytes": total, "payload_bytes": codes + book,
+            "bits_per_value": 8 * total / elements,
+            "sub_bit": 8 * total < elements}
+
+
+def _indices(codes: np.ndarray, vectors: int) -> np.ndarray:
+    pos = np.arange(vectors, dtype=np.int64)
+    return (codes[pos // 8] >> ((pos % 8) * 4).astype(np.uint32)) & np.uint32(15)
+
+
+def _pack(chosen: np.ndarray) -> np.ndarray:
+    words = np.zeros((chosen.size + 7) // 8, dtype=np.uint32)
+    for lane in range(8):
+        part = chosen[lane::8]
+        words[:part.size] |= part.astype(np.uint32) << np.uint32(4 * lane)
+    return words
+
+
+@dataclass(frozen=True, init=False)
+class VQArray:
+    """Owned CPU wire image: shape, group, packed codes, codebook."""
+
+    shape: tuple[int, ...]
+    group: int
+    codes: np.ndarray
+    codebook: np.ndarray
+
+    def __init__(self, shape, group, codes, codebook):
+        shape, group = _shape(shape), _group(group)
+        layout = storage_layout(shape, group)
+        raw = np.asarray(codes)
+        if raw.dtype != np.dtype("uint32") or raw.shape != (layout["code_bytes"] // 4,):
+            raise ValueError("vq codes must be the exact uint32 word image")
+        book = _book(codebook, group)
+        tail = layout["vectors"] % 8
+        if tail and int(raw[-1]) >> (4 * tail):
+            raise ValueError("vq unused codeword bits must be zero")
+        owned_codes, owned_book = raw.copy(), book.copy()
+        owned_codes.flags.writeable = False
+        owned_book.flags.writeable = False
+        object.__setattr__(self, "shape", shape)
+        object.__setattr__(self, "group", group)
+        object.__setattr__(self, "codes", owned_codes)
+        object.__setattr__(self, "codebook", owned_book)
+
+    @property
+    def layout(self) -> dict:
+        return storage_layout(self.shape, self.group)
+
+    def decode(self) -> np.ndarray:
+        layout = self.layout
+        idx = _indices(self.codes, layout["vectors"])
+        return self.codebook[idx].reshape(-1)[:layout["elements"]].copy().reshape(self.shape)
+
+    def to_bytes(self) -> bytes:
+        layout = self.layout
+        header = _HEADER.pack(_MAGIC, SCHEMA, self.group, len(self.shape), 0,
+                              layout["elements"], layout["code_bytes"])
+        dims = struct.pack("<" + "Q" * len(self.shape), *self.shape)
+        return header + dims + self.codebook.astype("<f4").tobytes() + self.codes.astype("<u4").tobytes()
+
+    @classmethod
+    def from_bytes(cls, data, *, max_bytes: int = 128 * 1024 * 1024) -> "VQArray":
+        limit = _integer(max_bytes, "max_bytes", _HEADER.size, 1 << 32)
+        view = memoryview(data).cast("B")
+        if not _HEADER.size <= view.nbytes <= limit:
+            raise ValueError("vq artifact byte limit or truncated header")
+        magic, schema, group, rank, reserved, elements, code_bytes = _HEADER.unpack_from(view)
+        if magic != _MAGIC or schema != SCHEMA or reserved or not 1 <= rank <= 6:
+            raise ValueError("unsupported vq artifact header")
+        dims_end = _HEADER.size + rank * 8
+        if view.nbytes < dims_end:
+            raise ValueError("truncated vq dimensions")
+        shape = struct.unpack_from("<" + "Q" * rank, view, _HEADER.size)
+        layout = storage_layout(shape, group)
+        if elements != layout["elements"] or code_bytes != layout["code_bytes"]:
+            raise ValueError("vq header disagrees with its dimensions")
+        if view.nbytes != layout["serialized_bytes"]:
+            raise ValueError("vq artifact length mismatch")
+        book_end = dims_end + layout["codebook_bytes"]
+        book = np.frombuffer(view[dims_end:book_end], dtype="<f4").reshape(ENTRIES, group)
+        codes = np.frombuffer(view[book_end:], dtype="<u4")
+        return cls(shape, group, codes.astype(np.uint32), book.astype(np.float32))
+
+
+def _nearest(vectors: np.ndarray, book: np.ndarray, valid_last: int | None = None) -> np.ndarray:
+    """float64 nearest entry per row, components summed in order, lowest
+    index on ties; `valid_last` limits the last row to its valid components."""
+    group = book.shape[1]
+    b = book.astype(np.float64)
+    chosen = np.empty(len(vectors), dtype=np.uint32)
+    step = 16384
+    for start in range(0, len(vectors), step):
+        v = vectors[start:start + step].astype(np.float64)
+        distances = np.zeros((len(v), ENTRIES), dtype=np.float64)
+        last = start + len(v) == len(vectors)
+        for j in range(group):
+            delta = v[:, j, None] - b[None, :, j]
+            if last and valid_last is not None and j >= valid_last:
+                delta[-1] = 0
+            distances += delta * delta
+        chosen[start:start + len(v)] = np.argmin(distances, axis=1).astype(np.uint32)
+    return chosen
+
+
+def encode(values, codebook, *, group: int = 16) -> VQArray:
+    """CPU encoder: nearest code vector in float64, lowest index on ties.
+
+    The reference's CPU encoder (its results define the device encoder's:
+    `VQDevice.encode` returns the same bytes). `fit_codebook` uses it on its
+    calibration sample; device-sized work belongs on `VQDevice`."""
+    group = _group(group)
+    x = _float_array(values, "values")
+    shape = _shape(x.shape)
+    book = _book(codebook, group)
+    layout = storage_layout(shape, group)
+    padded = np.zeros(layout["vectors"] * group, dtype=np.float32)
+    padded[:x.size] = x.reshape(-1)
+    tail = x.size % group
+    chosen = _nearest(padded.reshape(-1, group), book, tail if tail else None)
+    return VQArray(shape, group, _pack(chosen), book)
+
+
+def _reseed(sample: np.ndarray, book: np.ndarray) -> np.ndarray:
+    """The sample vector the current book serves worst (farthest point)."""
+    gap = ((sample.astype(np.float64)[:, None, :] - book.astype(np.float64)[None, :, :]) ** 2).sum(-1).min(1)
+    return sample[int(gap.argmax())]
+
+
+def _sample_positions(complete: int, sample_vectors: int) -> np.ndarray:
+    return np.linspace(0, complete - 1, min(complete, sample_vectors), dtype=np.int64)
+
+
+def _fit(sample: np.ndarray, complete: int, group: int, iterations: int, init, whole_usage) -> np.ndarray:
+    """Lloyd iterations on the calibration sample. `whole_usage(book)` returns
+    the entries the whole tensor selects; it is asked only on a warm start
+    whose sample is smaller than the tensor and leaves empty an entry no lower
+    row duplicates (the kept-entry rule of the reference fit)."""
+    if init is None:
+        book = sample[np.linspace(0, len(sample) - 1, ENTRIES, dtype=np.int64)].copy()
+    else:
+        book = _book(init, group).copy()
+    for _ in range(iterations):
+        _book(book, group)
+        idx = _nearest(sample, book)
+        kept = set()
+        empty = set(range(ENTRIES)) - set(np.unique(idx).tolist())
+        reachable = [e for e in empty if not any(np.array_equal(book[e], book[j]) for j in range(e))]
+        if init is not None and len(sample) < complete and reachable:
+            kept = set(whole_usage(book))
+        for entry in range(ENTRIES):
+            selected = sample[idx == entry]
+            if len(selected):
+                book[entry] = selected.mean(axis=0, dtype=np.float64).astype(np.float32)
+            elif entry not in kept:
+                book[entry] = _reseed(sample, book)
+    return book
+
+
+def fit_codebook(values, *, group: int = 16, iterations: int = 4,
+                 sample_vectors: int = 4096, init=None) -> np.ndarray:
+    """Bounded deterministic calibration on the CPU; does not establish task quality.
+
+    Lloyd iterations on a strided sample of at most `sample_vectors`
+    complete vectors; an entry a iteration leaves empty is reseeded with the
+    sample vector the book serves worst, unless (warm start from `init`, the
+    sample smaller than the tensor) the whole tensor still selects it."""
+    group = _group(group)
+    iterations = _integer(iterations, "iterations", 0, 32)
+    sample_vectors = _integer(sample_vectors, "sample_vectors", ENTRIES, 65536)
+    x = _float_array(values, "values").reshape(-1)
+    if x.size < group:
+        raise ValueError("codebook calibration needs at least one complete vector")
+    complete = x[:x.size // group * group].reshape(-1, group)
+    sample = complete[_sample_positions(len(complete), sample_vectors)]
+
+    def whole_usage(book):
+        return np.unique(_nearest(complete, book)).tolist()
+
+    return _fit(sample, len(complete), group, iterations, init, whole_usage)
+
+
+@dataclass(frozen=True, init=False)
+class VQStack:
+    """E coded matrices of one shape and group, stored contiguously: codes
+    (E, words) and books (E, 16, group). The operand of the grouped product;
+    build it once for weights that are used many times."""
+
+    shape: tuple[int, ...]
+    group: int
+    codes: np.ndarray
+    books: np.ndarray
+
+    def __init__(self, shape, group, codes, books):
+        shape, group = _shape(shape), _group(group)
+        layout = storage_layout(shape, group)
+        codes = np.asarray(codes)
+        books = np.asarray(books)
+        if codes.dtype != np.uint32 or codes.ndim != 2 or codes.shape[1] != layout["code_bytes"] // 4:
+            raise ValueError("stacked codes must be a (count, words) uint32 array")
+        if books.dtype != np.float32 or books.shape != (codes.shape[0], ENTRIES, group):
+            raise ValueError(f"stacked books must be a (count, 16, {group}) float32 array")
+        if not codes.flags.c_contiguous or not books.flags.c_contiguous:
+            raise ValueError("stacked codes and books must be C-contiguous")
+        object.__setattr__(self, "shape", shape)
+        object.__setattr__(self, "group", group)
+        object.__setattr__(self, "codes", codes)
+        object.__setattr__(self, "books", books)
+
+    @classmethod
+    def from_arrays(cls, arrays) -> "VQStack":
+        arrays = list(arrays)
+        if not arrays or any(a.shape != arrays[0].shape or a.group != arrays[0].group for a in arrays):
+            raise ValueError("a stack needs one or more VQArrays of one shape and group")
+        return cls(arrays[0].shape, arrays[0].group, np.stack([a.codes for a in arrays]),
+                   np.stack([a.codebook for a in arrays]))
+
+    def __len__(self) -> int:
+        return self.codes.shape[0]
+
+    def __getitem__(self, i) -> VQArray:
+        return VQArray(self.shape, self.group, self.codes[i], self.books[i])
+
+
+class VQDevice:
+    """Synchronous, status-checked vq4 operations on an open `ack.Device`.
+
+    Each call allocates its device buffers, uploads its inputs, enqueues the
+    kernel, reads the status word and then the output, and frees the buffers
+    -- the reference's `VQDevice._run` contract (vq.py:283-308)."""
+
+    def __init__(self, device: ack.Device):
+        self.device = device
+        with device._lock:
+            device._require_open()
+            lib = device._lib.cdll
+            try:
+                schema = lib.ack_vq_schema
+                self._call = lib.ack_vq
+                self._call2 = lib.ack_vq2
+            except AttributeError as exc:
+                raise ack.AckUnavailable("library lacks the optional vq4/v1 extension") from exc
+            if schema() != SCHEMA:
+                raise ack.AckUnavailable("incompatible vq4 extension schema")
+
+    # -- transport ------------------------------------------------------------------
+
+    def _run(self, words, inputs, output_bytes: int, dtype):
+        device = self.device
+        with device._lock, ExitStack() as cleanup:
+            device._require_open()
+            buffers = []
+            for array in inputs:
+                b = device.buffer(array.nbytes)
+                cleanup.callback(b.free)
+                b.upload(array)
+                buffers.append(b)
+            out = device.buffer(output_bytes)
+            cleanup.callback(out.free)
+            status = device.buffer(4)
+            cleanup.callback(status.free)
+            status.upload(np.zeros(1, dtype=np.uint32))
+            while len(buffers) < 4:
+                buffers.append(buffers[0])  # unread slots still hold a live input
+            plan = struct.pack("<8I", *words)
+            rc = self._call(device._handle, *(b._handle for b in buffers), out._handle, status._handle,
+                            plan, len(plan))
+            if rc != ack.ACK_OK:
+                raise ack._kit_error("vq", rc, device._lib.last_error())
+            flags = int(status.download(np.uint32)[0])
+            if flags:
+                raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            return out.download(dtype)
+
+    def _launch2(self, plan_words, slots) -> None:
+        """Enqueue one schema-2 operation on live buffers (slot order
+        in0..in4, out0, out1, status; None for an unused slot)."""
+        device = self.device
+        plan = struct.pack("<16I", *plan_words)
+        handles = (ctypes.c_void_p * 8)(*[(b._handle if b is not None else None) for b in slots])
+        rc = self._call2(device._handle, handles, 8, plan, len(plan))
+        if rc != ack.ACK_OK:
+            raise ack._kit_error("vq2", rc, device._lib.last_error())
+
+    @staticmethod
+    def _plan2(op, m, n, k, group, flags=0, batch=1, aux0=0, aux1=0, aux2=0):
+        return (op, m, n, k, group, ENTRIES, flags, 0, batch, aux0, aux1, aux2, 0, 0, 0, 0)
+
+    def _run2(self, plan_words, inputs, outputs):
+        """Upload `inputs` (up to five arrays; None skips a slot), run, check
+        status, download `outputs` [(nbytes, dtype), ...] (up to two)."""
+        device = self.device
+        with device._lock, ExitStack() as cleanup:
+            device._require_open()
+            slots = [None] * 8
+            for i, array in enumerate(inputs):
+                if array is None:
+                    continue
+                b = device.buffer(array.nbytes)
+                cleanup.callback(b.free)
+                b.upload(array)
+                slots[i] = b
+            outs = []
+            for i, (nbytes, _) in enumerate(outputs):
+                b = device.buffer(nbytes)
+                cleanup.callback(b.free)
+                slots[5 + i] = b
+                outs.append(b)
+            status = device.buffer(4)
+            cleanup.callback(status.free)
+            status.upload(np.zeros(1, dtype=np.uint32))
+            slots[7] = status
+            self._launch2(plan_words, slots)
+            flags = int(status.download(np.uint32)[0])
+            if flags:
+                raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            return tuple(b.download(dtype) for b, (_, dtype) in zip(outs, outputs))
+
+    # -- the reference's operations (schema 1) ----------------------------------
+
+    def encode(self, values, codebook, *, group: int = 16) -> VQArray:
+        group = _group(group)
+        x = _float_array(values, "values")
+        layout = storage_layout(x.shape, group)
+        book = _book(codebook, group)
+        result = self._run((0, x.size, 1, 1, group, ENTRIES, 0, 0),
+                           (x, book), layout["code_bytes"], np.uint32)
+        return VQArray(x.shape, group, result, book)
+
+    def decode(self, value: VQArray) -> np.ndarray:
+        layout = value.layout
+        return self._run((1, layout["elements"], 1, 1, value.group, ENTRIES, 0, 0),
+                         (value.codes, value.codebook), layout["elements"] * 4,
+                         np.float32).reshape(value.shape)
+
+    def matmul(self, a: VQArray, b: VQArray, *, transpose_a=False, transpose_b=False) -> np.ndarray:
+        if type(transpose_a) is not bool or type(transpose_b) is not bool:
+            raise ValueError("transpose flags must be boolean")
+        if len(a.shape) != 2 or len(b.shape) != 2 or a.group != b.group:
+            raise ValueError("vq matmul requires two matrices using the same vector group")
+        m, k = a.shape[::-1] if transpose_a else a.shape
+        k2, n = b.shape[::-1] if transpose_b else b.shape
+        if k != k2 or max(m, n, k) > 65536 or m * n > MAX_ELEMENTS:
+            raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
+        if m * n * k > MAX_MATMUL_MACS:
+            raise ValueError("vq-matmul-work-limit: split the product into bounded calls")
+        flags = int(transpose_a) | (int(transpose_b) << 1)
+        return self._run((2, m, n, k, a.group, ENTRIES, flags, 0),
+                         (a.codes, a.codebook, b.codes, b.codebook), m * n * 4,
+                         np.float32).reshape(m, n)
+
+    def adamw(self, weight: VQArray, momentum: VQArray, variance: VQArray,
+              gradient: VQArray, *, lr: float, beta1: float, beta2: float,
+              eps: float, weight_decay: float, step: int) -> tuple[np.ndarray, ...]:
+        """Native update from four coded states into FP32 scratch (vq4.comp op 3)."""
+        states = (weight, momentum, variance, gradient)
+        coefficients = _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step)
+        count = weight.layout["elements"]
+        if count * 3 > MAX_ELEMENTS:
+            raise ValueError("vq AdamW active scratch exceeds element bound")
+        codes = np.concatenate([s.codes for s in states])
+        books = np.concatenate([s.codebook.reshape(-1) for s in states])
+        result = self._run((3, count, 1, 1, weight.group, ENTRIES, 0, 0),
+                           (codes, books, coefficients), count * 3 * 4, np.float32)
+        return tuple(x.reshape(weight.shape) for x in np.split(result, 3))
+
+    # -- B200 extension operations (schema 2) ----------------------------------
+
+    def encode_large(self, values, codebook, *, group: int = 16) -> np.ndarray:
+        """Packed code words of a 1-D float32 array of any length (beyond the
+        2^28-value bound of `encode`); returns the uint32 word image."""
+        group = _group(group)
+        x = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+        if not x.size:
+            raise ValueError("nothing to encode")
+        book = _book(codebook, group)
+        words = ((x.size + group - 1) // group + 7) // 8
+        plan = self._plan2(OP_ENCODE, x.size & 0xFFFFFFFF, 1, 1, group, aux0=x.size >> 32)
+        (codes,) = self._run2(plan, (x, book), [(words * 4, np.uint32)])
+        return codes
+
+    def decode_large(self, codes, codebook, count: int, *, group: int = 16) -> np.ndarray:
+        group = _group(group)
+        count = _integer(count, "count", 1, 1 << 36)
+        book = _book(codebook, group)
+        words = ((count + group - 1) // group + 7) // 8
+        codes = np.ascontiguousarray(codes, dtype=np.uint32).reshape(-1)
+        if codes.size != words:
+            raise ValueError("code image does not match the value count")
+        plan = self._plan2(OP_DECODE, count & 0xFFFFFFFF, 1, 1, group, aux0=count >> 32)
+        (out,) = self._run2(plan, (codes, book), [(count * 4, np.float32)])
+        return out
+
+    def matmul_dense(self, x, w: VQArray, *, transpose_b: bool = True) -> np.ndarray:
+        """FP32 activations times coded weights.
+
+        `transpose_b=True`: `w` is stored (N, K) with its vectors along K and
+        the result is `x @ decode(w).T`; `False`: `w` is stored (K, N) and the
+        result is `x @ decode(w)`. `x` is (M, K) float32."""
+        return self.matmul_dense_grouped(np.asarray(x)[None], VQStack.from_arrays([w]),
+                                         transpose_b=transpose_b)[0]
+
+    def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True) -> np.ndarray:
+        """E independent products in one launch: `xs` is (E, M, K) float32
+        (or a sequence of (M, K)), `ws` a `VQStack` (or a sequence of
+        VQArray) of E matrices of one shape and group. Returns (E, M, N)."""
+        if type(transpose_b) is not bool:
+            raise ValueError("transpose flags must be boolean")
+        stack = ws if isinstance(ws, VQStack) else VQStack.from_arrays(ws)
+        if len(stack.shape) != 2:
+            raise ValueError("vq matmul requires matrices")
+        x = np.asarray(xs) if not isinstance(xs, (list, tuple)) else np.stack([np.asarray(v) for v in xs])
+        x = _float_array(x, "activations")
+        if x.ndim != 3 or x.shape[0] != len(stack):
+            raise ValueError("activations must be (count, M, K) with one matrix per coded weight")
+        e, m, k = x.shape
+        n, k2 = stack.shape if transpose_b else stack.shape[::-1]
+        if k != k2:
+            raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
+        plan = self._plan2(OP_DENSE, m, n, k, stack.group, flags=2 if transpose_b else 0, batch=e)
+        (y,) = self._run2(plan, (x, stack.codes, stack.books), [(e * m * n * 4, np.float32)])
+        return y.reshape(e, m, n)
+
+    def matmul_coded(self, a: VQArray, b: VQArray, *, transpose_a=False, transpose_b=False) -> np.ndarray:
+        """`op(decode a) @ op(decode b)` without the 2^28-MAC bound of `matmul`.
+
+        With `a` stored (M, K) and `b` stored (N, K) (`transpose_b=True`) and
+        K a multiple of the group, each group's dot product is a lookup in the
+        16x16 table of codebook inner products."""
+        if type(transpose_a) is not bool or type(transpose_b) is not bool:
+            raise ValueError("transpose flags must be boolean")
+        if len(a.shape) != 2 or len(b.shape) != 2 or a.group != b.group:
+            raise ValueError("vq matmul requires two matrices using the same vector group")
+        m, k = a.shape[::-1] if transpose_a else a.shape
+        k2, n = b.shape[::-1] if transpose_b else b.shape
+        if k != k2:
+            raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
+        flags = int(transpose_a) | (int(transpose_b) << 1)
+        plan = self._plan2(OP_CODED, m, n, k, a.group, flags=flags)
+        (y,) = self._run2(plan, (a.codes, a.codebook, b.codes, b.codebook), [(m * n * 4, np.float32)])
+        return y.reshape(m, n)
+
+    def adamw_fused(self, weight: VQArray, momentum: VQArray, variance: VQArray, gradient: VQArray, *,
+                    lr: float, beta1: float, beta2: float, eps: float, weight_decay: float, step: int,
+                    sample_vectors: int = 4096, iterations: int = 4):
+        """One VQAdamW step without FP32 scratch: the device computes the
+        AdamW values of the calibration sample (the same values op 3 would
+        produce), `fit_codebook`'s Lloyd iterations run on the CPU with the
+        whole-tensor entry check answered by the device, then one device pass
+        decodes, updates and re-encodes W, M and V with the fitted books.
+
+        Returns ((W', M', V') as VQArrays, changed weight values, bytes the
+        device produced)."""
+        states = (weight, momentum, variance, gradient)
+        coefficients = _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step)
+        group = weight.group
+        count = weight.layout["elements"]
+        complete = count // group
+        if complete < 1:
+            raise ValueError("codebook calibration needs at least one complete vector")
+        positions = _sample_positions(complete, sample_vectors)
+        s = len(positions)
+        codes = np.concatenate([st.codes for st in states])
+        books = np.concatenate([st.codebook.reshape(-1) for st in states])
+        words = weight.codes.size
+        device = self.device
+        with device._lock, ExitStack() as cleanup:
+            device._require_open()
+
+            def buffer_of(array):
+                b = device.buffer(array.nbytes)
+                cleanup.callback(b.free)
+                b.upload(array)
+                return b
+
+            b_codes, b_books, b_coefs = buffer_of(codes), buffer_of(books), buffer_of(coefficients)
+            b_pos = buffer_of(positions.astype(np.uint32))
+            status = buffer_of(np.zeros(1, dtype=np.uint32))
+
+            def check():
+                flags = int(status.download(np.uint32)[0])
+                if flags:
+                    raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+
+            sample_out = device.buffer(3 * s * group * 4)
+            cleanup.callback(sample_out.free)
+            self._launch2(self._plan2(OP_ADAMW_SAMPLE, count, 1, 1, group, batch=1, aux0=s),
+                          [b_codes, b_books, b_coefs, b_pos, None, sample_out, None, status])
+            check()
+            samples = sample_out.download(np.float32).reshape(3, s, group)
+
+            trial = device.buffer(ENTRIES * group * 4)
+            cleanup.callback(trial.free)
+            usage_out = device.buffer(ENTRIES * 4)
+            cleanup.callback(usage_out.free)
+            fitted = []
+            for which, state in enumerate((weight, momentum, variance)):
+                def whole_usage(book, which=which):
+                    trial.upload(np.ascontiguousarray(book, dtype=np.float32))
+                    self._launch2(self._plan2(OP_ADAMW_USAGE, count, 1, 1, group, batch=1, aux0=which, aux1=0),
+                                  [b_codes, b_books, b_coefs, trial, None, usage_out, None, status])
+                    check()
+                    return np.nonzero(usage_out.download(np.uint32))[0].tolist()
+
+                fitted.append(_fit(samples[which], complete, group, iterations, state.codebook, whole_usage))
+            new_books = np.ascontiguousarray(np.stack(fitted), dtype=np.float32)
+            b_new = buffer_of(new_books)
+            out_codes = device.buffer(3 * words * 4)
+            cleanup.callback(out_codes.free)
+            changed = device.buffer(4)
+            cleanup.callback(changed.free)
+            self._launch2(self._plan2(OP_ADAMW_ENCODE, count, 1, 1, group, batch=1),
+                          [b_codes, b_books, b_coefs, b_new, None, out_codes, changed, status])
+            check()
+            image = out_codes.download(np.uint32).reshape(3, words)
+            n_changed = int(changed.download(np.uint32)[0])
+        encoded = tuple(VQArray(weight.shape, group, image[i], new_books[i]) for i in range(3))
+        return encoded, n_changed, samples.nbytes + image.nbytes
+
+
+def _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step) -> np.ndarray:
+    """The reference's argument checks and its seven FP32 coefficients (vq.py:345-360)."""
+    weight = states[0]
+    if any(s.shape != weight.shape or s.group != weight.group for s in states):
+        raise ValueError("vq AdamW states must have identical shapes and groups")
+    step = _integer(step, "step", 1, 1 << 53)
+    values = (lr, beta1, beta2, eps, weight_decay)
+    if any(isinstance(x, (bool, np.bool_)) or not math.isfinite(float(x)) for x in values):
+        raise ValueError("vq AdamW coefficients must be finite numbers")
+    if lr < 0 or not 0 <= beta1 < 1 or not 0 <= beta2 < 1 or eps <= 0 or weight_decay < 0:
+        raise ValueError("vq AdamW coefficients outside their domains")
+    coefficients = np.array([lr, beta1, beta2, eps, weight_decay,
+                             1 - beta1 ** step, 1 - beta2 ** step], dtype=np.float32)
+    if not np.isfinite(coefficients).all() or coefficients[3] <= 0 or (coefficients[5:] <= 0).any():
+        raise ValueError("vq AdamW coefficients are not representable in float32")
+    return coefficients
+
+
+class VQAdamW:
+    """Optimizer with coded persistent weights and both moments.
+
+    The AdamW arithmetic is FP32 in the reference shader's order; codebooks
+    are refitted on the CPU; re-encoding is lossy. A failed step leaves the
+    three state images and the step counter unchanged."""
+
+    def __init__(self, backend, weight: VQArray, *, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0):
+        self.backend = backend
+        self.weight = weight
+        zeros = np.zeros_like(weight.codes)
+        zero_book = np.zeros((ENTRIES, weight.group), dtype=np.float32)
+        self.momentum = VQArray(weight.shape, weight.group, zeros, zero_book)
+        self.variance = VQArray(weight.shape, weight.group, zeros, zero_book)
+        self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
+        self.steps = 0
+
+    def step(self, gradient: VQArray) -> dict:
+        next_step = self.steps + 1
+        fused = getattr(self.backend, "adamw_fused", None)
+        if fused is not None:
+            encoded, changed, produced = fused(
+                self.weight, self.momentum, self.variance, gradient, lr=self.lr, beta1=self.betas[0],
+                beta2=self.betas[1], eps=self.eps, weight_decay=self.weight_decay, step=next_step)
+            encoded = list(encoded)
+        else:
+            scratch = self.backend.adamw(self.weight, self.momentum, self.variance, gradient,
+                                         lr=self.lr, beta1=self.betas[0], beta2=self.betas[1],
+                                         eps=self.eps, weight_decay=self.weight_decay, step=next_step)
+            # each array warm-starts from its own state's codebook: the pairing must be exact
+            if len(scratch) != 3:
+                raise ValueError(f"vq AdamW update returned {len(scratch)} arrays, not 3")
+            encoded = []
+            for value, state in zip(scratch, (self.weight, self.momentum, self.variance)):
+                book = fit_codebook(value, group=self.weight.group, init=state.codebook)
+                encoded.append(self.backend.encode(value, book, group=self.weight.group))
+            changed = int(np.count_nonzero(encoded[0].decode() != self.weight.decode()))
+            produced = sum(s.nbytes for s in scratch)
+        self.weight, self.momentum, self.variance = encoded
+        self.steps = next_step
+        return {"step": self.steps, "changed_weight_values": changed,
+                "persistent_state_bytes": sum(s.layout["serialized_bytes"] for s in encoded),
+                "gradient_bytes": gradient.layout["serialized_bytes"],
+                "native_update_output_bytes": produced,
+                "calibration": "CPU float32/float64 temporary arrays",
+                "model_quality_validated": False}

@@ -1,0 +1,776 @@
+// The C ABI of libalelyon_compute_kit.so over the CUDA runtime.
+//
+// Restates the contract of the reference's Rust C ABI (ffi.rs) for the core
+// device entries and the vq4 extension, B200-first:
+//   * a device is one CUDA device with one non-blocking stream; operator
+//     entries enqueue on it and return ACK_OK (= accepted, not finished);
+//     ack_download waits for the stream, so a readback sees all earlier work
+//     (ffi.rs:48-64);
+//   * handles are ids looked up in a registry under a lock, never
+//     dereferenced (ffi.rs:10-25); a buffer handle is (device id << 32) | seq;
+//   * one mutex per device serialises calls on it (ffi.rs:27-34);
+//   * a CUDA error that leaves the context unusable (an illegal address, a
+//     launch failure) poisons the device: every later call on it refuses
+//     with ACK_ERR_POISONED, a free leaks and counts its buffer, close still
+//     succeeds (ffi.rs:16-20);
+//   * the last error message is per thread (ffi.rs:1368).
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "alelyon_compute_kit.h"
+#include "vq_kernels.hpp"
+#include "vq_plan.hpp"
+
+#define ACK_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& m) { g_last_error = m; }
+
+std::string format(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return buf;
+}
+
+struct BufferRec {
+  void* ptr = nullptr;
+  uint64_t bytes = 0;
+  uint64_t id = 0;
+};
+
+struct Device {
+  uint64_t id = 0;
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  bool closed = false;
+  bool poisoned = false;
+  std::unordered_map<uint32_t, BufferRec> buffers;
+  uint32_t next_buffer = 1;
+  uint64_t leaked = 0;
+  cudaDeviceProp prop{};
+  int inject_sync = 0;       // test-only: error reported by the next synchronisation
+  bool inject_alloc = false; // test-only: the next allocation reports failure
+};
+
+struct Registry {
+  std::mutex mu;
+  std::unordered_map<uint64_t, std::shared_ptr<Device>> devices;
+  uint64_t next_device = 1;
+};
+
+Registry& registry() {
+  static Registry* r = new Registry;  // never destroyed: no teardown-order hazards at exit
+  return *r;
+}
+
+// Make `ordinal` current for the scope and restore the caller's device after.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int ordinal) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    if (prev_ != ordinal) cudaSetDevice(ordinal);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev_ >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = -1;
+};
+
+// Errors after which the CUDA context cannot be trusted.
+bool sticky(cudaError_t e) {
+  switch (e) {
+    case cudaErrorIllegalAddress:
+    case cudaErrorLaunchFailure:
+    case cudaErrorHardwareStackError:
+    case cudaErrorIllegalInstruction:
+    case cudaErrorMisalignedAddress:
+    case cudaErrorInvalidAddressSpace:
+    case cudaErrorInvalidPc:
+    case cudaErrorAssert:
+    case cudaErrorLaunchTimeout:
+    case cudaErrorECCUncorrectable:
+    case cudaErrorContextIsDestroyed:
+    case cudaErrorDevicesUnavailable:
+    case cudaErrorUnknown:
+      return true;
+    default:
+      return false;
+  }
+}
+
+int32_t cuda_fail(Device& d, cudaError_t e, const char* what) {
+  set_error(format("%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e)));
+  if (sticky(e)) {
+    d.poisoned = true;
+    return ACK_ERR_POISONED;
+  }
+  return ACK_ERR_VULKAN;
+}
+
+int32_t lookup(const AckDevice* handle, std::shared_ptr<Device>* out) {
+  const uint64_t id = uint64_t(reinterpret_cast<uintptr_t>(handle));
+  if (!id) {
+    set_error("null device handle");
+    return ACK_ERR_NULL;
+  }
+  Registry& r = registry();
+  std::lock_guard<std::mutex> lk(r.mu);
+  auto it = r.devices.find(id);
+  if (it == r.devices.end()) {
+    set_error(format("device handle %llu is not open (closed, never opened, or not a kit handle)",
+                     (unsigned long long)id));
+    return ACK_ERR_CLOSED;
+  }
+  *out = it->second;
+  return ACK_OK;
+}
+
+// The device lock, or ACK_ERR_CLOSED once closed (ffi.rs:1906-1916).
+int32_t acquire(Device& d, std::unique_lock<std::mutex>* lk) {
+  *lk = std::unique_lock<std::mutex>(d.mu);
+  if (d.closed) {
+    set_error(format("device %llu is closed", (unsigned long long)d.id));
+    return ACK_ERR_CLOSED;
+  }
+  return ACK_OK;
+}
+
+// A buffer handle resolved against the device that must own it (ffi.rs:1919-1941).
+int32_t buffer_of(Device& d, const AckBuffer* handle, BufferRec** out) {
+  const uint64_t raw = uint64_t(reinterpret_cast<uintptr_t>(handle));
+  if (!raw) {
+    set_error("null buffer handle");
+    return ACK_ERR_NULL;
+  }
+  const uint64_t owner = raw >> 32;
+  const uint32_t seq = uint32_t(raw & 0xffffffffu);
+  if (owner != d.id) {
+    set_error(format("buffer %#llx belongs to device %llu, not device %llu", (unsigned long long)raw,
+                     (unsigned long long)owner, (unsigned long long)d.id));
+    return ACK_ERR_FOREIGN;
+  }
+  auto it = d.buffers.find(seq);
+  if (it == d.buffers.end()) {
+    set_error(format("buffer %#llx is not live on device %llu (freed, or never allocated)", (unsigned long long)raw,
+                     (unsigned long long)d.id));
+    return ACK_ERR_FREED;
+  }
+  *out = &it->second;
+  return ACK_OK;
+}
+
+int32_t refuse_poisoned(const Device& d, const char* what) {
+  if (!d.poisoned) return ACK_OK;
+  set_error(format("%s: device %llu poisoned by an earlier failed CUDA operation; close it", what,
+                   (unsigned long long)d.id));
+  return ACK_ERR_POISONED;
+}
+
+// Wait for the device stream; a test-only injected fault reports after the real wait.
+cudaError_t sync_stream(Device& d) {
+  cudaError_t e = cudaStreamSynchronize(d.stream);
+  if (e == cudaSuccess && d.inject_sync) {
+    e = cudaError_t(d.inject_sync);
+    d.inject_sync = 0;
+  }
+  return e;
+}
+
+uint64_t fnv1a(const void* data, size_t len, uint64_t h = 0xcbf29ce484222325ull) {
+  const unsigned char* p = static_cast<const unsigned char*>(data);
+  for (size_t i = 0; i < len; ++i) {
+    h ^= p[i];
+    h *= 0x100000001b3ull;
+  }
+  return h;
+}
+
+uint64_t shader_identity() {
+  const char* m = ack::kernel_manifest();
+  return fnv1a(m, strlen(m));
+}
+
+constexpr const char* kVersion = "alelyon-compute-kit-b200 0.1.0";
+
+int32_t plan_refused(const char* entry, ack::PlanError e, int schema, int slot) {
+  set_error(format("%s: plan refused: %s", entry, ack::plan_error_name(e, schema, slot).c_str()));
+  return ack::plan_error_code(e);
+}
+
+// ACK_DEVICE: "gpu", "gpu:<n>", "any", "any:<n>" choose a CUDA ordinal
+// (device_choice.rs:11-22); "cpu" is refused; unset = the current device.
+int choose_ordinal(std::string* why) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    *why = format("no CUDA device: %s", e == cudaSuccess ? "none found" : cudaGetErrorString(e));
+    return -1;
+  }
+  const char* env = getenv("ACK_DEVICE");
+  if (!env || !*env) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) cur = 0;
+    return cur;
+  }
+  std::string s(env);
+  std::string kind = s.substr(0, s.find(':'));
+  if (kind == "cpu") {
+    *why = "ACK_DEVICE=cpu: this build has no CPU device; the vq4 path runs on CUDA only";
+    return -1;
+  }
+  if (kind != "gpu" && kind != "any") {
+    *why = format("ACK_DEVICE=%s is not gpu, gpu:<n>, any or any:<n>", env);
+    return -1;
+  }
+  int n = 0;
+  if (s.find(':') != std::string::npos) {
+    char* end = nullptr;
+    long v = strtol(s.c_str() + s.find(':') + 1, &end, 10);
+    if (!end || *end || v < 0) {
+      *why = format("ACK_DEVICE=%s: the ordinal is not a number", env);
+      return -1;
+    }
+    n = int(v);
+  }
+  if (n >= count) {
+    *why = format("ACK_DEVICE=%s: only %d CUDA device(s)", env, count);
+    return -1;
+  }
+  return n;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- core entries --
+
+ACK_EXPORT int32_t ack_abi_info(AckAbiInfo* out, size_t size) {
+  if (!out) return ACK_ERR_NULL;
+  if (size < sizeof(AckAbiInfo)) {
+    set_error(format("AckAbiInfo of %zu bytes is smaller than this library's %zu", size, sizeof(AckAbiInfo)));
+    return ACK_ERR_ABI;
+  }
+  AckAbiInfo info;
+  memset(&info, 0, sizeof(info));
+  info.size = sizeof(AckAbiInfo);
+  info.version = ACK_ABI_VERSION;
+  info.operators = 0;  // none of the reference's dense operator families
+  info.shaders = shader_identity();
+  uint64_t b = fnv1a(kVersion, strlen(kVersion));
+  info.build = fnv1a(&info.shaders, sizeof(info.shaders), b);
+  memcpy(out, &info, sizeof(info));
+  return ACK_OK;
+}
+
+ACK_EXPORT AckDevice* ack_open(void) {
+  std::string why;
+  const int ordinal = choose_ordinal(&why);
+  if (ordinal < 0) {
+    set_error(why);
+    return nullptr;
+  }
+  auto dev = std::make_shared<Device>();
+  dev->ordinal = ordinal;
+  {
+    DeviceScope scope(ordinal);
+    cudaError_t e = cudaGetDeviceProperties(&dev->prop, ordinal);
+    if (e != cudaSuccess) {
+      set_error(format("ack_open: %s", cudaGetErrorString(e)));
+      return nullptr;
+    }
+    if (dev->prop.major != 10 || dev->prop.minor != 0) {
+      set_error(format("ack_open: this library is built for sm_100a (B200); CUDA device %d is sm_%d%d", ordinal,
+                       dev->prop.major, dev->prop.minor));
+      return nullptr;
+    }
+    e = cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      set_error(format("ack_open: stream: %s", cudaGetErrorString(e)));
+      return nullptr;
+    }
+  }
+  Registry& r = registry();
+  std::lock_guard<std::mutex> lk(r.mu);
+  if (r.next_device > 0xffffffffull) {
+    set_error("device handle space exhausted in this process");
+    DeviceScope scope(ordinal);
+    cudaStreamDestroy(dev->stream);
+    return nullptr;
+  }
+  dev->id = r.next_device++;
+  r.devices[dev->id] = dev;
+  return reinterpret_cast<AckDevice*>(uintptr_t(dev->id));
+}
+
+ACK_EXPORT int32_t ack_close(AckDevice* handle) {
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  {
+    std::unique_lock<std::mutex> lk;
+    rc = acquire(*dev, &lk);
+    if (rc) return rc;
+    if (!dev->buffers.empty()) {
+      set_error(format("close refused: %zu buffer(s) still allocated on this device", dev->buffers.size()));
+      return ACK_ERR_LIVE_BUFFERS;
+    }
+    if (!dev->poisoned) {
+      DeviceScope scope(dev->ordinal);
+      cudaError_t e = sync_stream(*dev);
+      if (e != cudaSuccess)
+        set_error(format("close waited for enqueued work and it failed: %s", cudaGetErrorString(e)));
+      else
+        cudaStreamDestroy(dev->stream);
+    }
+    dev->closed = true;
+  }
+  Registry& r = registry();
+  std::lock_guard<std::mutex> lk(r.mu);
+  r.devices.erase(dev->id);
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_device_info(const AckDevice* handle, AckDeviceInfo* out, size_t size) {
+  if (!out) return ACK_ERR_NULL;
+  if (size < sizeof(AckDeviceInfo)) {
+    set_error(format("AckDeviceInfo of %zu bytes is smaller than this library's %zu", size, sizeof(AckDeviceInfo)));
+    return ACK_ERR_ABI;
+  }
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  const cudaDeviceProp& p = dev->prop;
+  AckDeviceInfo info;
+  memset(&info, 0, sizeof(info));
+  info.size = sizeof(AckDeviceInfo);
+  info.version = ACK_DEVICE_INFO_VERSION;
+  int runtime = 0, driver = 0;
+  cudaRuntimeGetVersion(&runtime);
+  cudaDriverGetVersion(&driver);
+  // Vulkan-style packed version (major << 22 | minor << 12) of the CUDA runtime
+  info.api_version = (uint32_t(runtime / 1000) << 22) | (uint32_t((runtime % 1000) / 10) << 12);
+  info.driver_version_raw = uint32_t(driver);
+  info.driver_id = 0;
+  info.vendor_id = 0x10DE;
+  info.device_id = uint32_t(p.pciDeviceID);
+  info.device_type = 2;  // a discrete GPU
+  memcpy(info.device_uuid, p.uuid.bytes, 16);
+  info.features = 0;
+  info.subgroup_size = uint32_t(p.warpSize);
+  info.timestamp_valid_bits = 64;
+  info.timestamp_period_ns = 1.0f;
+  info.max_push_constant_bytes = 32764;  // kernel parameter space
+  info.device_local_bytes = p.totalGlobalMem;
+  info.max_storage_buffer_bytes = p.totalGlobalMem;
+  info.max_workgroup_invocations = uint32_t(p.maxThreadsPerBlock);
+  for (int i = 0; i < 3; ++i) {
+    info.max_workgroup_count[i] = uint32_t(p.maxGridSize[i]);
+    info.max_workgroup_size[i] = uint32_t(p.maxThreadsDim[i]);
+  }
+  uint64_t id = fnv1a(reinterpret_cast<const unsigned char*>(&info) + 8, 152);
+  uint64_t sh = shader_identity();
+  info.identity = fnv1a(&sh, sizeof(sh), id);
+  snprintf(info.device_name, sizeof(info.device_name), "%s", p.name);
+  snprintf(info.driver_name, sizeof(info.driver_name), "NVIDIA CUDA");
+  snprintf(info.driver_info, sizeof(info.driver_info), "driver API %d.%d, runtime %d.%d, sm_%d%d, %d SMs",
+           driver / 1000, (driver % 1000) / 10, runtime / 1000, (runtime % 1000) / 10, p.major, p.minor,
+           p.multiProcessorCount);
+  memcpy(out, &info, sizeof(info));
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_device_name(const AckDevice* handle, char* out, size_t len) {
+  if (!out || len == 0) return ACK_ERR_NULL;
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  const size_t n = std::min(strlen(dev->prop.name), len - 1);
+  memcpy(out, dev->prop.name, n);
+  out[n] = 0;
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_live_objects(const AckDevice* handle, int64_t* out) {
+  if (!out) return ACK_ERR_NULL;
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  *out = 1 + int64_t(dev->buffers.size()) + int64_t(dev->leaked);
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_leaked_on_poison(const AckDevice* handle, uint64_t* out) {
+  if (!out) return ACK_ERR_NULL;
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  *out = dev->leaked;
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_last_error(char* out, size_t len) {
+  if (!out || len == 0) return ACK_ERR_NULL;
+  const size_t n = std::min(g_last_error.size(), len - 1);
+  memcpy(out, g_last_error.data(), n);
+  out[n] = 0;
+  return ACK_OK;
+}
+
+ACK_EXPORT AckBuffer* ack_buffer_alloc(const AckDevice* handle, uint64_t bytes) {
+  if (bytes == 0) {
+    set_error("zero-byte buffer");
+    return nullptr;
+  }
+  std::shared_ptr<Device> dev;
+  if (lookup(handle, &dev)) return nullptr;
+  std::unique_lock<std::mutex> lk;
+  if (acquire(*dev, &lk)) return nullptr;
+  if (refuse_poisoned(*dev, "buffer alloc")) return nullptr;
+  if (dev->next_buffer == 0xffffffffu) {
+    set_error("buffer handle space exhausted on this device; close and reopen");
+    return nullptr;
+  }
+  DeviceScope scope(dev->ordinal);
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e == cudaSuccess && dev->inject_alloc) {
+    dev->inject_alloc = false;
+    cudaFree(ptr);
+    ptr = nullptr;
+    e = cudaErrorMemoryAllocation;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // an allocation failure is not sticky; clear it
+    set_error(format("buffer alloc of %llu bytes: %s (%s)", (unsigned long long)bytes, cudaGetErrorName(e),
+                     cudaGetErrorString(e)));
+    if (sticky(e)) dev->poisoned = true;
+    return nullptr;
+  }
+  const uint32_t seq = dev->next_buffer++;
+  const uint64_t h = (dev->id << 32) | seq;
+  dev->buffers[seq] = BufferRec{ptr, bytes, h};
+  return reinterpret_cast<AckBuffer*>(uintptr_t(h));
+}
+
+ACK_EXPORT int32_t ack_buffer_free(const AckDevice* handle, AckBuffer* buf) {
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  BufferRec* b = nullptr;
+  rc = buffer_of(*dev, buf, &b);
+  if (rc) return rc;
+  const uint32_t seq = uint32_t(uint64_t(reinterpret_cast<uintptr_t>(buf)) & 0xffffffffu);
+  void* ptr = b->ptr;
+  dev->buffers.erase(seq);
+  if (dev->poisoned) {
+    // the handle is consumed; the allocation is left alone and counted
+    dev->leaked += 1;
+    set_error("buffer leaked, not freed: the device is poisoned");
+    return ACK_ERR_POISONED;
+  }
+  DeviceScope scope(dev->ordinal);
+  cudaError_t e = cudaFree(ptr);  // waits for enqueued work that may still use it
+  if (e != cudaSuccess) return cuda_fail(*dev, e, "buffer free");
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_upload(const AckDevice* handle, const AckBuffer* buf, const void* data, size_t len) {
+  if (!data) return ACK_ERR_NULL;
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  BufferRec* b = nullptr;
+  rc = buffer_of(*dev, buf, &b);
+  if (rc) return rc;
+  if (uint64_t(len) != b->bytes) {
+    set_error(format("upload of %zu bytes into a %llu-byte buffer", len, (unsigned long long)b->bytes));
+    return ACK_ERR_SIZE;
+  }
+  rc = refuse_poisoned(*dev, "upload");
+  if (rc) return rc;
+  DeviceScope scope(dev->ordinal);
+  cudaError_t e = cudaMemcpyAsync(b->ptr, data, len, cudaMemcpyHostToDevice, dev->stream);
+  if (e == cudaSuccess) e = sync_stream(*dev);  // the caller's bytes may go away on return
+  if (e != cudaSuccess) return cuda_fail(*dev, e, "upload");
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_download(const AckDevice* handle, const AckBuffer* buf, void* data, size_t len) {
+  if (!data) return ACK_ERR_NULL;
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  BufferRec* b = nullptr;
+  rc = buffer_of(*dev, buf, &b);
+  if (rc) return rc;
+  if (uint64_t(len) != b->bytes) {
+    set_error(format("download of %zu bytes from a %llu-byte buffer", len, (unsigned long long)b->bytes));
+    return ACK_ERR_SIZE;
+  }
+  rc = refuse_poisoned(*dev, "download");
+  if (rc) return rc;
+  DeviceScope scope(dev->ordinal);
+  cudaError_t e = cudaMemcpyAsync(data, b->ptr, len, cudaMemcpyDeviceToHost, dev->stream);
+  if (e == cudaSuccess) e = sync_stream(*dev);
+  if (e != cudaSuccess) return cuda_fail(*dev, e, "download");
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_inject_fault(const AckDevice* handle, int32_t kind, int32_t code) {
+  const char* env = getenv("ACK_FAULT_INJECTION");
+  if (!env || strcmp(env, "1") != 0) {
+    set_error("ack_inject_fault: fault injection is disabled in this process (set ACK_FAULT_INJECTION=1)");
+    return ACK_ERR_UNSUPPORTED_OP;
+  }
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  if (kind == 0 && code != 0) {
+    dev->inject_sync = code;
+  } else if (kind == 1) {
+    dev->inject_alloc = true;
+  } else {
+    set_error(format("ack_inject_fault: kind %d is not 0 (synchronisation, nonzero code) or 1 (allocation)", kind));
+    return ACK_ERR_SHAPE;
+  }
+  return ACK_OK;
+}
+
+// ------------------------------------------------------------ vq4 entries --
+
+ACK_EXPORT uint32_t ack_vq_schema(void) { return ACK_VQ_SCHEMA; }
+ACK_EXPORT uint32_t ack_vq2_schema(void) { return ACK_VQ2_SCHEMA; }
+
+namespace {
+
+// Admission against live registry buffers, then enqueue. `handles` is in the
+// plan's slot order (6 or 8 entries).
+int32_t run_handles(const char* entry, const AckDevice* handle, const AckBuffer* const* handles,
+                    const ack::Plan& plan) {
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  if (dev->poisoned) {
+    set_error(format("%s: device poisoned by an earlier failed CUDA operation", entry));
+    return ACK_ERR_POISONED;
+  }
+  const int n = plan.nslots();
+  uint64_t caps[ack::kSlots] = {0}, ids[ack::kSlots] = {0};
+  void* ptr[ack::kSlots] = {nullptr};
+  for (int i = 0; i < n; ++i) {
+    if (plan.schema == 2 && !handles[i] && !plan.required[i]) continue;  // an unused schema-2 slot
+    BufferRec* b = nullptr;
+    rc = buffer_of(*dev, handles[i], &b);
+    if (rc) return rc;
+    caps[i] = b->bytes;
+    ids[i] = b->id;
+    ptr[i] = b->ptr;
+  }
+  int slot = 0;
+  ack::PlanError e = ack::validate_buffers(plan, caps, ids, &slot);
+  if (e == ack::PlanError::None) {
+    const std::array<uint32_t, 3> limits = {uint32_t(dev->prop.maxGridSize[0]), uint32_t(dev->prop.maxGridSize[1]),
+                                            uint32_t(dev->prop.maxGridSize[2])};
+    e = ack::validate_dispatch(plan, limits);
+  }
+  if (e != ack::PlanError::None) return plan_refused(entry, e, plan.schema, slot);
+  DeviceScope scope(dev->ordinal);
+  cudaError_t ce = ack::launch(plan, ptr, dev->stream);
+  if (ce != cudaSuccess) return cuda_fail(*dev, ce, entry);
+  return ACK_OK;
+}
+
+}  // namespace
+
+ACK_EXPORT int32_t ack_vq(const AckDevice* dev, const AckBuffer* b0, const AckBuffer* b1, const AckBuffer* b2,
+                          const AckBuffer* b3, const AckBuffer* out, const AckBuffer* status, const uint8_t* plan,
+                          size_t plan_len) {
+  if (!plan) {
+    set_error("vq: null plan");
+    return ACK_ERR_NULL;
+  }
+  if (plan_len != ACK_VQ_PUSH_BYTES) {
+    set_error(format("vq: plan has %zu bytes, expected %u", plan_len, ACK_VQ_PUSH_BYTES));
+    return ACK_ERR_SIZE;
+  }
+  ack::Plan p;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused("vq", e, 1, 0);
+  const AckBuffer* handles[6] = {b0, b1, b2, b3, out, status};
+  return run_handles("vq", dev, handles, p);
+}
+
+ACK_EXPORT int32_t ack_vq2(const AckDevice* dev, const AckBuffer* const* slots, size_t nslots, const uint8_t* plan,
+                           size_t plan_len) {
+  if (!plan) {
+    set_error("vq2: null plan");
+    return ACK_ERR_NULL;
+  }
+  if (plan_len != ACK_VQ2_PLAN_BYTES) {
+    set_error(format("vq2: plan has %zu bytes, expected %u", plan_len, ACK_VQ2_PLAN_BYTES));
+    return ACK_ERR_SIZE;
+  }
+  if (!slots) {
+    set_error("vq2: null slot array");
+    return ACK_ERR_NULL;
+  }
+  if (nslots != ACK_VQ2_SLOTS) {
+    set_error(format("vq2: %zu slots, expected %u", nslots, ACK_VQ2_SLOTS));
+    return ACK_ERR_SIZE;
+  }
+  ack::Plan p;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused("vq2", e, 2, 0);
+  return run_handles("vq2", dev, slots, p);
+}
+
+ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops, void* stream) {
+  if (!plan || !ops) {
+    set_error(!plan ? "vq: null plan" : "vq: null operands");
+    return ACK_ERR_NULL;
+  }
+  if (ops->size < sizeof(AckVqOperands)) {
+    set_error(format("AckVqOperands of %u bytes is smaller than this library's %zu", ops->size,
+                     sizeof(AckVqOperands)));
+    return ACK_ERR_ABI;
+  }
+  if (plan_len != ACK_VQ_PUSH_BYTES && plan_len != ACK_VQ2_PLAN_BYTES) {
+    set_error(format("vq: plan has %zu bytes, expected %u or %u", plan_len, ACK_VQ_PUSH_BYTES, ACK_VQ2_PLAN_BYTES));
+    return ACK_ERR_SIZE;
+  }
+  const char* entry = plan_len == ACK_VQ_PUSH_BYTES ? "vq" : "vq2";
+  ack::Plan p;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused(entry, e, p.schema, 0);
+  const int n = p.nslots();
+  if (ops->nslots != uint32_t(n)) {
+    set_error(format("%s: %u operand slots, expected %d", entry, ops->nslots, n));
+    return ACK_ERR_SIZE;
+  }
+  uint64_t ids[ack::kSlots] = {0}, caps[ack::kSlots] = {0};
+  void* ptr[ack::kSlots] = {nullptr};
+  for (int i = 0; i < n; ++i) {
+    ptr[i] = ops->ptr[i];
+    ids[i] = uint64_t(reinterpret_cast<uintptr_t>(ops->ptr[i]));
+    caps[i] = ops->bytes[i];
+  }
+  int slot = 0;
+  e = ack::validate_buffers(p, caps, ids, &slot);
+  if (e != ack::PlanError::None) return plan_refused(entry, e, p.schema, slot);
+  // pointers: 4-byte aligned; written ranges disjoint from every other used range
+  for (int i = 0; i < n; ++i)
+    if (p.required[i] && (ids[i] & 3u)) return plan_refused(entry, ack::PlanError::Misaligned, 2, i);
+  const int first_out = p.first_output();
+  for (int o = first_out; o < n; ++o) {
+    if (!p.required[o]) continue;
+    for (int i = 0; i < n; ++i) {
+      if (i == o || !p.required[i]) continue;
+      const uint64_t a0 = ids[o], a1 = ids[o] + p.required[o], b0 = ids[i], b1 = ids[i] + p.required[i];
+      if (a0 < b1 && b0 < a1) {
+        const bool status = o == p.status_slot() || i == p.status_slot();
+        return plan_refused(entry, status ? ack::PlanError::StatusAlias : ack::PlanError::OutputAlias, p.schema, 0);
+      }
+    }
+  }
+  cudaError_t ce = ack::launch(p, ptr, static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) {
+    set_error(format("%s: launch: %s (%s)", entry, cudaGetErrorName(ce), cudaGetErrorString(ce)));
+    return ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
+// ------------------------------------------------------- planner probes --
+
+ACK_EXPORT int32_t ack_vq_plan_probe(const uint8_t* plan, size_t plan_len, uint64_t required_bytes[8],
+                                     uint32_t* work_items, uint32_t dispatch[3]) {
+  if (!plan) {
+    set_error("vq: null plan");
+    return ACK_ERR_NULL;
+  }
+  if (plan_len != ACK_VQ_PUSH_BYTES && plan_len != ACK_VQ2_PLAN_BYTES) {
+    set_error(format("vq: plan has %zu bytes, expected %u", plan_len, ACK_VQ_PUSH_BYTES));
+    return ACK_ERR_SIZE;
+  }
+  ack::Plan p;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused(p.schema == 1 ? "vq" : "vq2", e, p.schema, 0);
+  if (required_bytes)
+    for (int i = 0; i < 8; ++i) required_bytes[i] = p.required[i];
+  if (work_items) *work_items = p.work_items;
+  if (dispatch)
+    for (int i = 0; i < 3; ++i) dispatch[i] = p.dispatch[i];
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_vq_plan_validate_buffers(const uint8_t* plan, size_t plan_len, const uint64_t* capacities,
+                                                const uint64_t* ids, size_t n) {
+  if (!plan || !capacities || !ids) return ACK_ERR_NULL;
+  ack::Plan p;
+  if (plan_len != ACK_VQ_PUSH_BYTES && plan_len != ACK_VQ2_PLAN_BYTES) return ACK_ERR_SIZE;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused("vq", e, p.schema, 0);
+  if (n != size_t(p.nslots())) {
+    set_error(format("vq: %zu slots, expected %d", n, p.nslots()));
+    return ACK_ERR_SIZE;
+  }
+  int slot = 0;
+  e = ack::validate_buffers(p, capacities, ids, &slot);
+  if (e != ack::PlanError::None) return plan_refused(p.schema == 1 ? "vq" : "vq2", e, p.schema, slot);
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_vq_plan_validate_dispatch(const uint8_t* plan, size_t plan_len, const uint32_t limits[3]) {
+  if (!plan || !limits) return ACK_ERR_NULL;
+  ack::Plan p;
+  if (plan_len != ACK_VQ_PUSH_BYTES && plan_len != ACK_VQ2_PLAN_BYTES) return ACK_ERR_SIZE;
+  ack::PlanError e = ack::parse_plan(plan, plan_len, &p);
+  if (e != ack::PlanError::None) return plan_refused("vq", e, p.schema, 0);
+  e = ack::validate_dispatch(p, {limits[0], limits[1], limits[2]});
+  if (e != ack::PlanError::None) return plan_refused(p.schema == 1 ? "vq" : "vq2", e, p.schema, 0);
+  return ACK_OK;
+}

@@ -1,0 +1,256 @@
+// Device-side building blocks shared by the vq4 kernels: code access, status
+// flags, the codebook preparation and the certified nearest-entry search.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ack {
+
+constexpr uint32_t kNonfinite = 1u;   // vq4.comp:5-8 status bits
+constexpr uint32_t kLayout = 2u;
+constexpr uint32_t kOptimizer = 4u;
+
+// Index of vector `v` in a packed image: nibble v%8 of word v/8, little-endian.
+__device__ __forceinline__ uint32_t code_at(const uint32_t* __restrict__ codes, uint64_t v) {
+  return (__ldg(codes + (v >> 3)) >> (4u * uint32_t(v & 7u))) & 15u;
+}
+
+__device__ __forceinline__ bool finite32(float x) {
+  return (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u;
+}
+
+// OR `bits` into the status word once per warp. Every lane of the warp that
+// is active must call it.
+__device__ __forceinline__ void flag_warp(uint32_t* status, uint32_t bits) {
+  const uint32_t mask = __activemask();
+  const uint32_t all = __reduce_or_sync(mask, bits);
+  if (all && (threadIdx.x & 31) == (__ffs(mask) - 1)) atomicOr(status, all);
+}
+
+// A codebook prepared for the nearest-entry search, in shared memory.
+//   cT      transposed book, cT[j*4 + q] = (c[4q][j], c[4q+1][j], c[4q+2][j], c[4q+3][j])
+//   rows    the book row-major, for the exact float64 pass
+//   q       fl32(||c_e||^2), the square norm summed in float64 then rounded
+//   cmax2   max_e ||c_e||^2 rounded up
+//   uniq    bit e set when row e differs from every lower row; a duplicate
+//           row can never win because ties keep the lowest index
+//   bad     the book holds a NaN or an infinity
+template <int G>
+struct EncBook {
+  float4 cT[G * 4];
+  float rows[16 * G];
+  float q[16];
+  float cmax2;
+  uint32_t uniq;
+  uint32_t bad;
+};
+
+// Fill `eb` from a global-memory book. All threads of the block call it; it
+// ends with a barrier.
+template <int G>
+__device__ void enc_book_setup(EncBook<G>& eb, const float* __restrict__ book) {
+  float* cT = reinterpret_cast<float*>(eb.cT);
+  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) {
+    const float v = book[i];
+    eb.rows[i] = v;
+    cT[(i % G) * 16 + i / G] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int e = threadIdx.x & 15;
+    double s = 0.0;
+    bool bad = false;
+    for (int j = 0; j < G; ++j) {
+      const float c = eb.rows[e * G + j];
+      bad |= !finite32(c);
+      s = __dadd_rn(s, __dmul_rn(double(c), double(c)));
+    }
+    bool uniq = true;
+    for (int f = 0; f < e; ++f) {
+      bool same = true;
+      for (int j = 0; j < G; ++j) same &= eb.rows[f * G + j] == eb.rows[e * G + j];
+      if (same) uniq = false;
+    }
+    float up = __double2float_ru(s);
+    for (int o = 8; o; o >>= 1) up = fmaxf(up, __shfl_xor_sync(0xffffffffu, up, o));
+    const uint32_t u = __ballot_sync(0xffffffffu, uniq) & 0xffffu;
+    const uint32_t b = __ballot_sync(0xffffffffu, bad) & 0xffffu;
+    if (threadIdx.x < 16) eb.q[e] = __double2float_rn(s);
+    if (threadIdx.x == 0) {
+      eb.cmax2 = up;
+      eb.uniq = u;
+      eb.bad = b != 0;
+    }
+  }
+  __syncthreads();
+}
+
+// Exact nearest entry among the set bits of `cand`, computed the way the
+// reference CPU encoder computes it (vq.py:167-174): float64 distances
+// accumulated in component order, d += (v_j - b_j)^2 with each operation
+// rounded on its own, over the first `valid` components; the lowest index
+// wins a tie; a NaN distance wins at its first occurrence (np.argmin).
+template <int G>
+__device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, uint32_t cand,
+                                              const float* __restrict__ rows) {
+  double best = 0.0;
+  int chosen = -1;
+  bool nan_seen = false;
+  for (int e = 0; e < 16; ++e) {
+    if (!((cand >> e) & 1u)) continue;
+    double d = 0.0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      if (j < valid) {
+        const double t = __dsub_rn(double(x[j]), double(rows[e * G + j]));
+        d = __dadd_rn(d, __dmul_rn(t, t));
+      }
+    }
+    if (nan_seen) continue;
+    if (d != d) {
+      chosen = e;
+      nan_seen = true;
+    } else if (chosen < 0 || d < best) {
+      best = d;
+      chosen = e;
+    }
+  }
+  return chosen < 0 ? 0u : uint32_t(chosen);
+}
+
+// Certified nearest entry of one complete vector.
+//
+// Filter: f_e = ||c_e||^2 - 2 x.c_e in FP32 (16 fused multiply-adds per
+// component). |f_e - G_e| <= eps with G_e the exact value of the same
+// expression and eps = (G + 8) 2^-23 (||x||^2 + max ||c||^2): twice the
+// forward-error bound of the FMA chain, the rounded norms and the final FMA,
+// plus an absolute floor for subnormal products. Any entry whose f_e lies
+// within 2 eps of the minimum could be the float64 winner (the float64
+// distances differ from the exact ones by far less than eps); when that
+// candidate set holds more than one distinct row, or anything is not finite,
+// the exact float64 pass decides among the candidates. The result is
+// therefore always the reference encoder's choice, not an approximation.
+template <int G>
+__device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const EncBook<G>& eb,
+                                               bool* certified) {
+  float acc[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+  float nx2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const float4 c0 = eb.cT[j * 4 + 0], c1 = eb.cT[j * 4 + 1];
+    const float4 c2 = eb.cT[j * 4 + 2], c3 = eb.cT[j * 4 + 3];
+    const float xj = x[j];
+    acc[0] = fmaf(xj, c0.x, acc[0]);
+    acc[1] = fmaf(xj, c0.y, acc[1]);
+    acc[2] = fmaf(xj, c0.z, acc[2]);
+    acc[3] = fmaf(xj, c0.w, acc[3]);
+    acc[4] = fmaf(xj, c1.x, acc[4]);
+    acc[5] = fmaf(xj, c1.y, acc[5]);
+    acc[6] = fmaf(xj, c1.z, acc[6]);
+    acc[7] = fmaf(xj, c1.w, acc[7]);
+    acc[8] = fmaf(xj, c2.x, acc[8]);
+    acc[9] = fmaf(xj, c2.y, acc[9]);
+    acc[10] = fmaf(xj, c2.z, acc[10]);
+    acc[11] = fmaf(xj, c2.w, acc[11]);
+    acc[12] = fmaf(xj, c3.x, acc[12]);
+    acc[13] = fmaf(xj, c3.y, acc[13]);
+    acc[14] = fmaf(xj, c3.z, acc[14]);
+    acc[15] = fmaf(xj, c3.w, acc[15]);
+    nx2 = fmaf(xj, xj, nx2);
+  }
+  float f[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) f[e] = fmaf(-2.f, acc[e], eb.q[e]);
+  float fb = f[0];
+  uint32_t best = 0;
+#pragma unroll
+  for (int e = 1; e < 16; ++e)
+    if (f[e] < fb) {
+      fb = f[e];
+      best = uint32_t(e);
+    }
+  constexpr float kappa = float(G + 8) * (1.0f / 8388608.0f);
+  const float eps = fmaf(kappa, nx2 + eb.cmax2, 1e-37f);
+  const float thr = fmaf(2.f, eps, fb);
+  uint32_t cand = 0;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
+  cand &= eb.uniq;
+  const bool clean = finite32(thr) && finite32(fb) && !eb.bad;
+  if (clean && cand == (1u << best)) {
+    *certified = false;
+    return best;
+  }
+  *certified = true;
+  return enc_exact<G>(x, G, clean ? cand : 0xffffu, eb.rows);
+}
+
+// OR together the nibbles of the 8 lanes that share a word and return the
+// packed word (valid in every lane). All 32 lanes must call it.
+__device__ __forceinline__ uint32_t pack_nibbles(uint32_t idx) {
+  uint32_t w = idx << (4u * (threadIdx.x & 7u));
+  w |= __shfl_xor_sync(0xffffffffu, w, 1);
+  w |= __shfl_xor_sync(0xffffffffu, w, 2);
+  w |= __shfl_xor_sync(0xffffffffu, w, 4);
+  return w;
+}
+
+// The shader's AdamW for one value (vq4.comp:98-115), every operation
+// rounded on its own. Returns status bits; on a nonzero return from the
+// input checks the outputs are not meaningful (the shader writes nothing).
+struct AdamwCoefs {
+  float lr, beta1, beta2, eps, decay, c1, c2;
+  uint32_t status;  // nonzero: coefficients refused (vq4.comp:92-97)
+};
+
+__device__ __forceinline__ AdamwCoefs load_coefs(const float* __restrict__ c) {
+  AdamwCoefs k;
+  k.lr = c[0];
+  k.beta1 = c[1];
+  k.beta2 = c[2];
+  k.eps = c[3];
+  k.decay = c[4];
+  k.c1 = c[5];
+  k.c2 = c[6];
+  k.status = 0;
+  const float all[7] = {k.lr, k.beta1, k.beta2, k.eps, k.decay, k.c1, k.c2};
+  for (int j = 0; j < 7; ++j)
+    if (!finite32(all[j])) k.status = kNonfinite;
+  if (!k.status && (k.lr < 0.f || k.beta1 < 0.f || k.beta1 >= 1.f || k.beta2 < 0.f || k.beta2 >= 1.f ||
+                    k.eps <= 0.f || k.decay < 0.f || k.c1 <= 0.f || k.c1 > 1.f || k.c2 <= 0.f || k.c2 > 1.f))
+    k.status = kOptimizer;
+  return k;
+}
+
+// Returns 0, or the status bits of a refused input (then the outputs are
+// unspecified), or kNonfinite with outputs written for a nonfinite result.
+__device__ __forceinline__ uint32_t adamw_value(const AdamwCoefs& k, float w, float m, float v, float g,
+                                                float* nw, float* nm, float* nv, bool* skip) {
+  *skip = false;
+  if (!finite32(w) || !finite32(m) || !finite32(v) || !finite32(g)) {
+    *skip = true;
+    return kNonfinite;
+  }
+  if (v < 0.f) {
+    *skip = true;
+    return kOptimizer;
+  }
+  const float next_m = __fadd_rn(__fmul_rn(k.beta1, m), __fmul_rn(__fsub_rn(1.f, k.beta1), g));
+  const float next_v = __fadd_rn(__fmul_rn(k.beta2, v), __fmul_rn(__fsub_rn(1.f, k.beta2), __fmul_rn(g, g)));
+  const float cm = __fdiv_rn(next_m, k.c1);
+  const float cv = __fdiv_rn(next_v, k.c2);
+  const float den = __fadd_rn(__fsqrt_rn(cv), k.eps);
+  const float decayed = __fmul_rn(w, __fsub_rn(1.f, __fmul_rn(k.lr, k.decay)));
+  const float next_w = __fsub_rn(decayed, __fdiv_rn(__fmul_rn(k.lr, cm), den));
+  *nw = next_w;
+  *nm = next_m;
+  *nv = next_v;
+  const bool ok = finite32(next_m) && finite32(next_v) && finite32(cm) && finite32(cv) && finite32(den) &&
+                  finite32(decayed) && finite32(next_w);
+  return ok ? 0u : kNonfinite;
+}
+
+}  // namespace ack

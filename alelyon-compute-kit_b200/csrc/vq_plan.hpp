@@ -1,0 +1,74 @@
+// Host-side admission for the vq4 operations: the schema-1 plan of the
+// reference (vq4_ops.rs:1-243, same order of checks, same refusal names and
+// codes) and the schema-2 plan of this library's extension entry.
+#pragma once
+
+#include <array>
+#include <cstdint>
+#include <string>
+
+namespace ack {
+
+constexpr uint32_t kEntries = 16;
+constexpr uint32_t kIndicesPerWord = 8;
+constexpr uint32_t kWorkgroupSize = 64;          // vq4_ops.rs:18; names the reference grid
+constexpr uint32_t kMaxValues = 1u << 28;        // vq4_ops.rs:19
+constexpr uint32_t kMaxDim = 65536;              // vq4_ops.rs:20
+constexpr uint64_t kMaxMatmulMacs = 1ull << 28;  // vq4_ops.rs:23
+constexpr uint32_t kGridX = 65535;               // vq4_ops.rs:24
+constexpr int kSlots = 8;                        // schema 2; schema 1 uses the first 6 slot positions
+
+enum class Op : uint32_t {
+  Encode = 0, Decode = 1, Matmul = 2, AdamW = 3,
+  Dense = 16, Coded = 17, AdamwSample = 18, AdamwUsage = 19, AdamwEncode = 20,
+  EncodeLarge = 21, DecodeLarge = 22,
+};
+
+// Refusals. The schema-1 names are vq4_ops.rs:66-84; the schema-2 ones are
+// this library's and are prefixed "vq2-".
+enum class PlanError {
+  None, Operation, Group, Entries, Flags, Reserved, Geometry, AddressLimit, WorkLimit,
+  Capacity, NullIdentity, OutputAlias, StatusAlias, Dispatch,
+  // schema 2 only
+  Batch, Aux, Misaligned,
+};
+
+struct Plan {
+  int schema = 1;                 // 1: 32-byte block, 6 slots; 2: 64-byte block, 8 slots
+  std::array<uint32_t, 16> words{};
+  Op op = Op::Encode;
+  uint32_t group = 8;
+  uint64_t m = 0, n = 0, k = 0;   // m carries the 64-bit value count of ops 21/22
+  uint32_t flags = 0;
+  uint32_t batch = 1;
+  uint32_t aux0 = 0, aux1 = 0, aux2 = 0;
+  // Required byte capacity per slot. Schema 1: [b0,b1,b2,b3,out,status];
+  // schema 2: [in0,in1,in2,in3,in4,out0,out1,status].
+  std::array<uint64_t, kSlots> required{};
+  uint32_t work_items = 0;        // schema 1: the reference's dispatch accounting
+  std::array<uint32_t, 3> dispatch{{0, 0, 0}};
+  int nslots() const { return schema == 1 ? 6 : 8; }
+  int first_output() const { return schema == 1 ? 4 : 5; }
+  int status_slot() const { return schema == 1 ? 5 : 7; }
+};
+
+// Bytes of a packed code image of `values` values: ceil(ceil(values/g)/8) u32 words.
+inline uint64_t packed_bytes(uint64_t values, uint32_t group) {
+  return ((values + group - 1) / group + 7) / 8 * 4;
+}
+inline uint64_t packed_words(uint64_t values, uint32_t group) { return packed_bytes(values, group) / 4; }
+
+// Parse a plan block (32 bytes: schema 1, 64 bytes: schema 2). `slot` receives
+// the offending slot for Capacity.
+PlanError parse_plan(const uint8_t* bytes, size_t len, Plan* out);
+// vq4_ops.rs:188-209: live identities (0 = null), capacities, alias rules.
+PlanError validate_buffers(const Plan& p, const uint64_t* capacities, const uint64_t* ids, int* slot);
+// vq4_ops.rs:211-222.
+PlanError validate_dispatch(const Plan& p, const std::array<uint32_t, 3>& limits);
+
+// "vq-..." / "vq2-..." refusal name; Capacity names its slot.
+std::string plan_error_name(PlanError e, int schema, int slot);
+// ACK_ERR_SIZE for Capacity/AddressLimit/WorkLimit, ACK_ERR_SHAPE otherwise (ffi.rs:6011-6018).
+int32_t plan_error_code(PlanError e);
+
+}  // namespace ack

@@ -1,0 +1,238 @@
+/*
+ * alelyon_compute_kit.h -- the C ABI of the B200 vq4/v1 library
+ * (libalelyon_compute_kit.so, built for sm_100a).
+ *
+ * This is the drop-in boundary for the reference's `vq4/v1` extension. The
+ * first block of entries keeps the reference's C ABI (its Rust `ffi.rs`,
+ * ABI version 14) symbol for symbol, with the same argument meaning, return
+ * codes and refusal names, so that a binding written for the reference's
+ * core + vq entries binds this library unchanged. Paths in the citations are
+ * relative to the reference's `src/alelyon_compute_kit/_kit/`.
+ *
+ * Handles are ids, never addresses: a device handle is a process-wide
+ * sequence number and a buffer handle is (device id << 32) | sequence. No
+ * entry dereferences a handle; each is looked up in a registry and refused
+ * by code when closed (ACK_ERR_CLOSED), foreign (ACK_ERR_FOREIGN) or freed
+ * (ACK_ERR_FREED) -- the reference contract of ffi.rs:10-25.
+ *
+ * ACK_OK from an operator entry means the work was ENQUEUED on the device's
+ * CUDA stream, not that it finished (ffi.rs:48-64). ack_download is the
+ * synchronisation point; read the status word before trusting an output
+ * (vq4.comp:5-8).
+ */
+#ifndef ALELYON_COMPUTE_KIT_H
+#define ALELYON_COMPUTE_KIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque handle types (ffi.rs: `AckDevice`, `Buffer`). Never dereferenced. */
+typedef struct AckDevice AckDevice;
+typedef struct AckBuffer AckBuffer;
+
+/* Return codes, values of ffi.rs:726-760. */
+#define ACK_OK 0
+#define ACK_ERR_NULL (-1)
+#define ACK_ERR_VULKAN (-2)          /* a driver error; here, a CUDA runtime error */
+#define ACK_ERR_SHAPE (-3)
+#define ACK_ERR_SIZE (-4)
+#define ACK_ERR_LIVE_BUFFERS (-5)
+#define ACK_ERR_CLOSED (-6)
+#define ACK_ERR_FOREIGN (-7)
+#define ACK_ERR_FREED (-8)
+#define ACK_ERR_ABI (-9)
+#define ACK_ERR_POISONED (-10)
+#define ACK_ERR_UNSUPPORTED_OP (-11)
+#define ACK_ERR_TIMING (-12)
+
+#define ACK_ABI_VERSION 14u            /* ffi.rs:867 */
+#define ACK_DEVICE_INFO_VERSION 1u     /* ack.py ACK_DEVICE_INFO_VERSION */
+#define ACK_VQ_SCHEMA 1u               /* vq4_ops.rs:13 */
+#define ACK_VQ_PUSH_BYTES 32u          /* vq4_ops.rs:15 */
+#define ACK_VQ2_SCHEMA 1u              /* schema of the B200 extension entry ack_vq2 */
+#define ACK_VQ2_PLAN_BYTES 64u
+#define ACK_VQ2_SLOTS 8u
+
+/* Status word bits written by every vq kernel (vq4.comp:5-8). */
+#define ACK_VQ_STATUS_NONFINITE 1u
+#define ACK_VQ_STATUS_LAYOUT 2u
+#define ACK_VQ_STATUS_OPTIMIZER 4u
+
+/* What ack_abi_info reports (ffi.rs:1009-1057, 96 bytes, same layout). This
+ * library carries none of the reference's twelve dense operator families, so
+ * `operators` and every op_schema_* field are 0; the vq extension announces
+ * itself through ack_vq_schema / ack_vq2_schema, as in the reference. */
+typedef struct AckAbiInfo {
+    uint32_t size;
+    uint32_t version;
+    uint64_t operators;
+    uint64_t shaders;   /* FNV-1a over the embedded CUDA kernel manifest */
+    uint64_t build;     /* FNV-1a over the library version and `shaders` */
+    uint32_t op_schema_matmul_bf16;
+    uint32_t op_schema_cast;
+    uint32_t capability_streams;
+    uint32_t capability_rng;
+    uint32_t capability_optimizer;
+    uint32_t capability_serialization;
+    uint32_t op_schema_matmul_f32;
+    uint32_t op_schema_pointwise;
+    uint32_t op_schema_reduce;
+    uint32_t op_schema_rowwise;
+    uint32_t op_schema_loss;
+    uint32_t op_schema_embedding;
+    uint32_t op_schema_matmul_f16;
+    uint32_t op_schema_index;
+    uint32_t op_schema_convert;
+    uint32_t op_schema_intwise;
+} AckAbiInfo;
+
+/* What ack_device_info reports (ffi.rs:1223-1255, 616 bytes, same layout),
+ * filled from the CUDA device: vendor 0x10DE, the device UUID, warp size as
+ * `subgroup_size`, CUDA grid/block limits as the workgroup limits. */
+typedef struct AckDeviceInfo {
+    uint32_t size;
+    uint32_t version;
+    uint32_t api_version;
+    uint32_t driver_version_raw;
+    uint32_t driver_id;
+    uint32_t vendor_id;
+    uint32_t device_id;
+    uint32_t device_type;
+    uint8_t device_uuid[16];
+    uint8_t driver_uuid[16];
+    uint64_t features;
+    uint32_t subgroup_size;
+    uint32_t timestamp_valid_bits;
+    float timestamp_period_ns;
+    uint32_t max_push_constant_bytes;
+    uint64_t device_local_bytes;
+    uint64_t max_storage_buffer_bytes;
+    uint32_t max_workgroup_invocations;
+    uint32_t max_workgroup_count[3];
+    uint32_t max_workgroup_size[3];
+    uint32_t matmul_tile;
+    uint32_t matmul_k_multiple;
+    uint32_t matmul_layouts;
+    uint32_t matmul_operand_dtype;
+    uint32_t matmul_result_dtype;
+    uint32_t cast_modes;
+    uint32_t reserved;
+    uint64_t identity;
+    char device_name[256];
+    char driver_name[64];
+    char driver_info[128];
+} AckDeviceInfo;
+
+/* ---- core device ABI (the subset the reference binding loads, ack.py:714-739) ---- */
+
+/* ffi.rs:1981 ack_abi_info. ACK_ERR_ABI when `size` < sizeof(AckAbiInfo). */
+int32_t ack_abi_info(AckAbiInfo *out, size_t size);
+/* ffi.rs:2410 ack_device_info. */
+int32_t ack_device_info(const AckDevice *dev, AckDeviceInfo *out, size_t size);
+/* ffi.rs:2037 ack_open: opens the CUDA device ACK_DEVICE names ("gpu", "gpu:<n>",
+ * "any", "any:<n>"; device_choice.rs:11-22), else the thread's current CUDA
+ * device. Null with ack_last_error set on failure ("cpu" is refused: this
+ * build has no CPU device). */
+AckDevice *ack_open(void);
+/* ffi.rs:2365 ack_close: ACK_ERR_LIVE_BUFFERS while buffers are live. */
+int32_t ack_close(AckDevice *dev);
+/* ffi.rs:3296 ack_device_name. */
+int32_t ack_device_name(const AckDevice *dev, char *out, size_t len);
+/* ffi.rs:2741 ack_live_objects: CUDA objects this device holds (its stream,
+ * live buffers). */
+int32_t ack_live_objects(const AckDevice *dev, int64_t *out);
+/* ffi.rs:3276 ack_leaked_on_poison: buffers left allocated because the
+ * device was poisoned when they were freed. */
+int32_t ack_leaked_on_poison(const AckDevice *dev, uint64_t *out);
+/* ffi.rs:3325 ack_last_error: this thread's last message. */
+int32_t ack_last_error(char *out, size_t len);
+/* ffi.rs:3345 ack_buffer_alloc: a device buffer (cudaMalloc); null on failure. */
+AckBuffer *ack_buffer_alloc(const AckDevice *dev, uint64_t bytes);
+/* ffi.rs:3413 ack_buffer_free. */
+int32_t ack_buffer_free(const AckDevice *dev, AckBuffer *buf);
+/* ffi.rs:3477 ack_upload: `len` must equal the buffer size. */
+int32_t ack_upload(const AckDevice *dev, const AckBuffer *buf, const void *data, size_t len);
+/* ffi.rs:3525 ack_download: waits for all enqueued work, then copies. */
+int32_t ack_download(const AckDevice *dev, const AckBuffer *buf, void *data, size_t len);
+
+/* ---- vq4/v1 extension (ffi.rs:6004-6151, vq4_ops.rs) ---- */
+
+/* ffi.rs:6006 ack_vq_schema: always 1. */
+uint32_t ack_vq_schema(void);
+/* ffi.rs:6037 ack_vq: encode (op 0), decode (1), packed-pair matmul (2),
+ * decoded-state AdamW (3). `plan` is 8 little-endian u32
+ * [op, m, n, k, group, 16, flags, 0]; admission, slot sizes, refusal names
+ * and codes are those of vq4_ops.rs:111-222, including the 2^28 value and
+ * matmul-MAC bounds. Results follow vq4.comp: encode picks the float64
+ * nearest code vector with lowest-index ties (the reference CPU encoder,
+ * vq.py:154-179), decode is exact, op 2 sums fl32(a*b) in k order with
+ * separately rounded adds, op 3 is AdamW in FP32 in the shader's order. */
+int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, const AckBuffer *b2,
+               const AckBuffer *b3, const AckBuffer *out, const AckBuffer *status,
+               const uint8_t *plan, size_t plan_len);
+
+/* ---- B200 extension of vq4 (schema 2). No counterpart in the reference's
+ * C ABI; these are the north-star operations the reference lacks
+ * (dense-activation product, unbounded coded product, fused coded-state
+ * AdamW, 64-bit encode/decode). ---- */
+
+/* Plan operations of ack_vq2 / ack_vq_launch with a 64-byte plan. */
+#define ACK_VQ2_DENSE 16u        /* Y_b = X_b * op(decode W_b), batch b of independent products */
+#define ACK_VQ2_CODED 17u        /* C = op(decode A) * op(decode B), no MAC bound */
+#define ACK_VQ2_ADAMW_SAMPLE 18u /* AdamW values of the calibration sample vectors */
+#define ACK_VQ2_ADAMW_USAGE 19u  /* entries a trial book selects over one updated state */
+#define ACK_VQ2_ADAMW_ENCODE 20u /* decode -> AdamW -> encode W', M', V' in one pass */
+#define ACK_VQ2_ENCODE 21u       /* encode with a 64-bit value count */
+#define ACK_VQ2_DECODE 22u       /* decode with a 64-bit value count */
+
+uint32_t ack_vq2_schema(void);
+/* `plan` is 16 little-endian u32 [op, m, n, k, group, 16, flags, 0, batch,
+ * aux0, aux1, aux2, 0, 0, 0, 0]; `slots` is ACK_VQ2_SLOTS buffer handles
+ * [in0, in1, in2, in3, in4, out0, out1, status]; a slot the operation does
+ * not use may be null. Slot meanings per operation are listed in
+ * INTEGRATION.md; refusals are named "vq2-..." and carry the schema-1 codes. */
+int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslots,
+                const uint8_t *plan, size_t plan_len);
+
+/* Device-pointer form of both entries, for callers whose data already lives
+ * in device memory (a PyTorch tensor, an NCCL buffer): the same plan, the
+ * same admission and refusals, operands given as CUDA device pointers with
+ * their byte capacities, work enqueued on the caller's CUDA stream `stream`
+ * (a cudaStream_t; null = the legacy default stream) on the current device.
+ * A 32-byte plan uses slots [b0, b1, b2, b3, out, status]; a 64-byte plan the
+ * ack_vq2 slots. Every non-null pointer must be 16-byte aligned. */
+typedef struct AckVqOperands {
+    uint32_t size;      /* sizeof(AckVqOperands) */
+    uint32_t nslots;    /* 6 for a schema-1 plan, 8 for a schema-2 plan */
+    uint64_t bytes[8];
+    void *ptr[8];
+} AckVqOperands;
+int32_t ack_vq_launch(const uint8_t *plan, size_t plan_len, const AckVqOperands *ops, void *stream);
+
+/* ---- host-only planner introspection (the public methods of the
+ * reference's VqPlan, vq4_ops.rs:111-243, which its Rust tests call
+ * directly). No device is touched. Each returns ACK_OK or the code ack_vq
+ * would return, with the refusal name in ack_last_error. ---- */
+int32_t ack_vq_plan_probe(const uint8_t *plan, size_t plan_len, uint64_t required_bytes[8],
+                          uint32_t *work_items, uint32_t dispatch[3]);
+int32_t ack_vq_plan_validate_buffers(const uint8_t *plan, size_t plan_len,
+                                     const uint64_t *capacities, const uint64_t *ids, size_t n);
+int32_t ack_vq_plan_validate_dispatch(const uint8_t *plan, size_t plan_len, const uint32_t limits[3]);
+
+/* ---- test-only host fault injection (the reference's `ack_inject_fault`,
+ * ffi.rs:3449, behind its `fault-injection` feature). Refused unless the
+ * process environment has ACK_FAULT_INJECTION=1. kind 0: the next stream
+ * synchronisation reports `code` (a cudaError_t) after the real wait ran;
+ * kind 1: the next buffer allocation reports cudaErrorMemoryAllocation after
+ * freeing what it allocated. Nothing is injected on the GPU. ---- */
+int32_t ack_inject_fault(const AckDevice *dev, int32_t kind, int32_t code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALELYON_COMPUTE_KIT_H */

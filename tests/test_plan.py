@@ -1,0 +1,218 @@
+"""Host-only vq4 admission: the reference planner's tests
+(`_kit/tests/vq4_plan.rs`), run against this library's C planner through
+its probe entries. Same plans, same byte counts, same refusals."""
+import pytest
+
+from abi_util import MAX_DIM, MAX_VALUES, probe, refusal, required, validate_buffers, validate_dispatch
+
+SHAPE, SIZE = -3, -4
+
+
+def vector(op, n, group):
+    return [op, n, 1, 1, group, 16, 0, 0]
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_packed_cost_counts_padding_and_complete_codebooks(group):  # vq4_plan.rs:10
+    for length, words in ((1, 1), (group, 1), (group * 8, 1), (group * 8 + 1, 2)):
+        assert required(vector(0, length, group)) == [length * 4, group * 64, 0, 0, words * 4, 4]
+        assert required(vector(1, length, group)) == [words * 4, group * 64, 0, 0, length * 4, 4]
+        assert probe(vector(0, length, group))[2] == words
+        assert probe(vector(1, length, group))[2] == length
+
+
+def test_adamw_is_four_packed_states_and_three_dense_scratch_arrays():  # vq4_plan.rs:44
+    rc, req, work, disp = probe(vector(3, 129, 16))
+    assert rc == 0
+    assert req[:6] == [32, 4096, 28, 0, 1548, 4]
+    assert work == 129 and disp == [3, 1, 1]
+    assert probe([3, MAX_VALUES // 3, 1, 1, 8, 16, 0, 0])[0] == 0
+    rc, msg = refusal([3, MAX_VALUES // 3 + 1, 1, 1, 8, 16, 0, 0])
+    assert rc == SIZE and msg.endswith("vq-address-limit-exceeded")
+
+
+def test_matmul_transposes_preserve_storage_counts():  # vq4_plan.rs:58
+    for flags in range(4):
+        rc, req, work, disp = probe([2, 3, 5, 7, 8, 16, flags, 0])
+        assert rc == 0 and req[:6] == [4, 512, 4, 512, 60, 4] and work == 15 and disp == [1, 1, 1]
+
+
+def test_all_schema_words_are_closed():  # vq4_plan.rs:74
+    good = [0, 64, 1, 1, 8, 16, 0, 0]
+    for slot, value, name in ((0, 4, "vq-operation-out-of-range"), (4, 0, "vq-unsupported-group"),
+                              (4, 4, "vq-unsupported-group"), (4, 64, "vq-unsupported-group"),
+                              (5, 0, "vq-codebook-entries-not-16"), (5, 15, "vq-codebook-entries-not-16"),
+                              (5, 17, "vq-codebook-entries-not-16"), (6, 1, "vq-unsupported-flags"),
+                              (7, 1, "vq-nonzero-reserved-word")):
+        words = list(good)
+        words[slot] = value
+        rc, msg = refusal(words)
+        assert rc == SHAPE and msg.endswith(name), (slot, value, msg)
+    assert refusal([2, 1, 1, 1, 8, 16, 4, 0])[1].endswith("vq-unsupported-flags")
+    for op in (1, 3):
+        assert refusal([op, 1, 1, 1, 8, 16, 1, 0])[1].endswith("vq-unsupported-flags")
+
+
+def test_zero_mismatched_or_overflowing_geometry_refuses():  # vq4_plan.rs:101
+    for op in range(4):
+        for axis in (1, 2, 3):
+            words = [op, 1, 1, 1, 8, 16, 0, 0]
+            words[axis] = 0
+            assert refusal(words)[1].endswith("vq-invalid-geometry")
+    for op in (0, 1, 3):
+        for axis in (2, 3):
+            words = [op, 1, 1, 1, 8, 16, 0, 0]
+            words[axis] = 2
+            assert refusal(words)[1].endswith("vq-invalid-geometry")
+    assert refusal([0, 0xFFFFFFFF, 1, 1, 8, 16, 0, 0]) [1].endswith("vq-address-limit-exceeded")
+    assert refusal([1, MAX_VALUES + 1, 1, 1, 8, 16, 0, 0])[1].endswith("vq-address-limit-exceeded")
+    assert refusal([2, MAX_DIM + 1, 1, 1, 8, 16, 0, 0])[1].endswith("vq-invalid-geometry")
+    for words in ([2, MAX_DIM, MAX_DIM, 1, 8, 16, 0, 0], [2, MAX_DIM, 1, MAX_DIM, 8, 16, 0, 0],
+                  [2, 1, MAX_DIM, MAX_DIM, 8, 16, 0, 0]):
+        rc, msg = refusal(words)
+        assert rc == SIZE and msg.endswith("vq-address-limit-exceeded")
+
+
+def test_each_read_and_write_capacity_is_checked_in_bytes():  # vq4_plan.rs:138
+    for op in range(4):
+        words = [2, 11, 9, 7, 16, 16, 0, 0] if op == 2 else vector(op, 129, 16)
+        caps = required(words)
+        ids = [1, 2, 3, 4, 5, 6]
+        assert validate_buffers(words, caps, ids) == 0
+        for slot in range(6):
+            if caps[slot] == 0:
+                continue
+            short = list(caps)
+            short[slot] -= 1
+            rc = validate_buffers(words, short, ids)
+            from abi_util import last_error
+            assert rc == SIZE and last_error().endswith(f"vq-binding-{slot}-too-small")
+
+
+def test_every_output_alias_including_unread_inputs_refuses():  # vq4_plan.rs:160
+    from abi_util import last_error
+    words = vector(0, 64, 8)
+    caps = [4096] * 6
+    for inp in range(4):
+        ids = [1, 2, 3, 4, 5, 6]
+        ids[4] = ids[inp]
+        assert validate_buffers(words, caps, ids) == SHAPE and last_error().endswith("vq-output-aliases-input")
+    for operand in range(5):
+        ids = [1, 2, 3, 4, 5, 6]
+        ids[5] = ids[operand]
+        assert validate_buffers(words, caps, ids) == SHAPE and last_error().endswith("vq-status-aliases-operand")
+    assert validate_buffers(words, caps, [1, 1, 1, 1, 2, 3]) == 0
+    for slot in range(6):
+        ids = [1, 2, 3, 4, 5, 6]
+        ids[slot] = 0
+        assert validate_buffers(words, caps, ids) == SHAPE and last_error().endswith("vq-null-allocation-identity")
+
+
+def test_maximum_tensor_uses_bounded_two_dimensional_grid():  # vq4_plan.rs:182
+    from abi_util import last_error
+    words = vector(1, MAX_VALUES, 32)
+    _, _, _, (x, y, z) = probe(words)
+    assert (x, y, z) == (65535, 65, 1)
+    assert x * y * 64 >= MAX_VALUES and x * y * 64 < 2 ** 32
+    assert validate_dispatch(words, [65535] * 3) == 0
+    for axis in range(3):
+        limits = [x, y, z]
+        limits[axis] -= 1
+        assert validate_dispatch(words, limits) == SHAPE and last_error().endswith("vq-dispatch-grid-unsupported")
+
+
+def test_every_refusal_is_named_and_slot_specific():  # vq4_plan.rs:199
+    from abi_util import last_error
+    words = [2, 11, 9, 7, 16, 16, 0, 0]
+    caps = required(words)
+    for slot in range(6):
+        short = list(caps)
+        short[slot] = 0 if caps[slot] else 0
+        if caps[slot]:
+            validate_buffers(words, short, [1, 2, 3, 4, 5, 6])
+            assert last_error() == f"vq: plan refused: vq-binding-{slot}-too-small"
+
+
+def test_matmul_work_is_bounded_even_when_every_buffer_extent_fits():  # vq4_plan.rs:225
+    assert probe([2, 1024, 1024, 256, 8, 16, 0, 0])[0] == 0
+    for words in ([2, 1024, 1024, 257, 8, 16, 0, 0], [2, 4096, 4096, 4096, 8, 16, 0, 0]):
+        rc, msg = refusal(words)
+        assert rc == SIZE and msg.endswith("vq-matmul-work-limit")
+
+
+# ---- schema 2 (this library's extension plan) ----
+
+def plan2(op, m, n, k, group, flags=0, batch=1, aux0=0, aux1=0, aux2=0):
+    return [op, m, n, k, group, 16, flags, 0, batch, aux0, aux1, aux2, 0, 0, 0, 0]
+
+
+def test_schema2_dense_and_coded_slot_sizes():
+    m, n, k, g, e = 4, 11008, 4096, 16, 3
+    words = (n * k // g + 7) // 8
+    assert required(plan2(16, m, n, k, g, flags=2, batch=e)) == [
+        e * m * k * 4, e * words * 4, e * 64 * g, 0, 0, e * m * n * 4, 0, 4]
+    assert required(plan2(17, 5, 7, 64, 8, flags=2)) == [
+        (5 * 64 // 8 + 7) // 8 * 4, 512, (7 * 64 // 8 + 7) // 8 * 4, 512, 0, 140, 0, 4]
+    # the schema-1 MAC bound does not apply to schema 2
+    assert probe(plan2(17, 4096, 14336, 4096, 32, flags=2))[0] == 0
+
+
+def test_schema2_adamw_and_large_slot_sizes():
+    n, g, e, s = 4096 * 1024, 8, 8, 4096
+    words = (n // g + 7) // 8
+    assert required(plan2(18, n, 1, 1, g, batch=e, aux0=s)) == [
+        e * 4 * words * 4, e * 4 * 64 * g, e * 28, s * 4, 0, e * 3 * s * g * 4, 0, 4]
+    assert required(plan2(19, n, 1, 1, g, batch=e, aux0=2, aux1=7)) == [
+        e * 4 * words * 4, e * 4 * 64 * g, e * 28, 64 * g, 0, 64, 0, 4]
+    assert required(plan2(20, n, 1, 1, g, batch=e)) == [
+        e * 4 * words * 4, e * 4 * 64 * g, e * 28, e * 3 * 64 * g, 0, e * 3 * words * 4, e * 4, 4]
+    big = 1 << 30
+    assert required(plan2(21, big & 0xFFFFFFFF, 1, 1, 16, aux0=big >> 32)) == [
+        big * 4, 1024, 0, 0, 0, (big // 16 + 7) // 8 * 4, 0, 4]
+    assert required(plan2(22, big & 0xFFFFFFFF, 1, 1, 16, aux0=big >> 32)) == [
+        (big // 16 + 7) // 8 * 4, 1024, 0, 0, 0, big * 4, 0, 4]
+
+
+def test_schema2_refusals_are_named():
+    cases = [
+        (plan2(15, 1, 1, 1, 8), "vq2-operation-out-of-range"),
+        (plan2(16, 1, 1, 1, 12), "vq2-unsupported-group"),
+        (plan2(16, 1, 1, 1, 8, flags=1), "vq2-unsupported-flags"),
+        (plan2(16, 0, 1, 1, 8), "vq2-invalid-geometry"),
+        (plan2(16, 1, 1, 1, 8, batch=0), "vq2-invalid-batch"),
+        (plan2(17, 1, 1, 1, 8, batch=2), "vq2-invalid-batch"),
+        (plan2(18, 64, 1, 1, 8, aux0=0), "vq2-invalid-aux-word"),
+        (plan2(18, 64, 1, 1, 8, aux0=9), "vq2-invalid-aux-word"),
+        (plan2(19, 64, 1, 1, 8, aux0=3), "vq2-invalid-aux-word"),
+        (plan2(19, 64, 1, 1, 8, batch=2, aux1=2), "vq2-invalid-aux-word"),
+        (plan2(21, 0, 1, 1, 8), "vq2-invalid-geometry"),
+        (plan2(21, 1, 1, 1, 8, aux0=1 << 8), "vq2-address-limit-exceeded"),
+        (plan2(16, 1 << 21, 1, 1, 8), "vq2-invalid-geometry"),
+    ]
+    for words, name in cases:
+        rc, msg = refusal(words)
+        assert rc in (SHAPE, SIZE) and msg.endswith(name), (words, msg)
+    bad = plan2(16, 1, 1, 8, 8)
+    bad[13] = 1
+    assert refusal(bad)[1].endswith("vq2-nonzero-reserved-word")
+
+
+def test_schema2_outputs_must_not_alias_and_unused_slots_may_be_null():
+    from abi_util import last_error
+    words = plan2(20, 1000, 1, 1, 8)
+    caps = required(words)
+    ids = [1, 2, 3, 4, 0, 6, 7, 8]
+    assert validate_buffers(words, caps, ids) == 0
+    for inp in range(4):
+        bad = list(ids)
+        bad[5] = bad[inp]
+        assert validate_buffers(words, caps, bad) == SHAPE and last_error().endswith("vq2-output-aliases-input")
+    bad = list(ids)
+    bad[6] = bad[5]
+    assert validate_buffers(words, caps, bad) == SHAPE and last_error().endswith("vq2-output-aliases-input")
+    bad = list(ids)
+    bad[7] = bad[6]
+    assert validate_buffers(words, caps, bad) == SHAPE and last_error().endswith("vq2-status-aliases-operand")
+    bad = list(ids)
+    bad[3] = 0
+    assert validate_buffers(words, caps, bad) == SHAPE and last_error().endswith("vq2-null-allocation-identity")
