@@ -301,7 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_dense_lut(const float* __restri
   }
   const uint32_t r0 = blockIdx.x * rows_per_block;
   const uint32_t r1 = min(N, r0 + rows_per_block);
-  const uint32_t chunk_bytes = TC / 2;  // bytes of one row's codes in a t-chunk
 
   for (uint32_t m0 = 0; m0 < M; m0 += MC) {
     const uint32_t mc = min(uint32_t(MC), M - m0);
@@ -330,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_dense_lut(const float* __restri
       auto issue = [&](uint32_t batch, int buf) {
         const uint32_t rb = r0 + batch * kThreads;
         const uint32_t nrows = min(uint32_t(kThreads), r1 - rb);
-        const uint32_t pieces = chunk_bytes / 16;  // 16-byte pieces per row
+        const uint32_t pieces = tc / 32;  // 16-byte pieces of this chunk in one row
         for (uint32_t i = threadIdx.x; i < nrows * pieces; i += blockDim.x) {
           const uint32_t r = i / pieces, pc = i % pieces;
           const unsigned char* src = reinterpret_cast<const unsigned char*>(Cb) +
@@ -610,6 +609,7 @@ __global__ void __launch_bounds__(kThreads) k_adamw_sample(AdamwBatch a, const u
     const uint32_t s = uint32_t(i / G), j = uint32_t(i % G);
     const uint64_t v = sample[s];
     uint32_t bits = k.status;
+    if (v >= uint64_t(a.n) / G) bits |= kLayout;  // a position outside the complete vectors
     float nw = 0.f, nm = 0.f, nv = 0.f;
     if (!bits) {
       const uint32_t* base = a.codes + uint64_t(e) * 4 * a.words;

@@ -1,0 +1,317 @@
+"""CUDA parity of the vq4 path through the C ABI (`ack.Device` / `VQDevice`)
+against the CPU oracle. Bit-exact: decode, encode (the reference's float64
+choice), the shader-order packed-pair matmul (op 2) and AdamW (op 3), the
+fused VQAdamW step. Tolerance (normwise 1e-5 of sum_k |a_k b_k|): the
+north-star products, whose summation order differs from any reference."""
+import json
+
+import numpy as np
+import pytest
+
+import vq_oracle as o
+import vq_oracle_c as oc
+from alelyon_compute_kit import ack, vq
+from alelyon_compute_kit.vq import VQAdamW, VQArray
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5  # normwise relative tolerance of the FP32 products
+
+
+@pytest.fixture(scope="module")
+def device():
+    dev = ack.Device()
+    yield dev
+    dev.close()
+
+
+@pytest.fixture(scope="module")
+def backend(device):
+    return vq.VQDevice(device)
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def rand_book(rng, group, scale=1.0):
+    return (rng.standard_normal((16, group)) * scale).astype(np.float32)
+
+
+def normwise(y, y64, a, b):
+    return float(np.max(np.abs(y.astype(np.float64) - y64) / np.maximum(np.abs(a) @ np.abs(b), 1e-30)))
+
+
+def test_device_identity(device):
+    assert "B200" in device.name
+    assert device.info.vendor_id == 0x10DE and device.info.subgroup_size == 32
+    assert device.live_objects() == 1
+    record = device.capability_record()
+    json.dumps(record)
+    assert record["abi"]["version"] == 14
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_decode_is_bit_exact(backend, group):
+    rng = np.random.default_rng(group)
+    for n in (1, 3, group, 8 * group, 8 * group + 1, 4097, 100_003):
+        book = rand_book(rng, group)
+        vectors = (n + group - 1) // group
+        codes = o.pack(rng.integers(0, 16, vectors))
+        arr = VQArray((n,), group, codes, book)
+        np.testing.assert_array_equal(bits(backend.decode(arr)), bits(o.decode(codes, book, n, group)))
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_encode_matches_reference_golden_bytes(backend, golden, group):
+    g = golden("encode_decode")
+    for n in (1, group, 8 * group, 8 * group + 1, 1000, 4097, 3 * group - 5):
+        key = f"g{group}_n{n}"
+        arr = backend.encode(g[key + "_values"], g[key + "_book"], group=group)
+        assert arr.to_bytes() == g[key + "_wire"].tobytes(), key
+    t = golden("ties")
+    for suffix in ("", "_zero", "_heavy"):
+        values = t[f"g{group}{suffix}_values"]
+        book = t[f"g{group}_book"] if suffix == "" else (
+            np.zeros((16, group), np.float32) if suffix == "_zero" else t[f"g{group}_heavy_book"])
+        got = backend.encode(values, book, group=group).codes
+        np.testing.assert_array_equal(got, t[f"g{group}{suffix}_codes"], err_msg=suffix)
+
+
+def test_cfg1_on_the_device(backend, golden):
+    g = golden("cfg1")
+    w = o.gaussian((256, 256), 0.02, 7)
+    image = backend.encode(w, g["book"], group=16)
+    assert image.to_bytes() == g["wire"].tobytes() and len(image.to_bytes()) == 3128
+    np.testing.assert_array_equal(backend.decode(image), image.decode())
+    x_image = VQArray.from_bytes(g["x_wire"].tobytes())
+    y = backend.matmul(x_image, image)
+    np.testing.assert_array_equal(bits(y), bits(o.matmul_shader(x_image.codes, x_image.codebook, image.codes,
+                                                                 image.codebook, 1, 256, 256, 16, 0)))
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_encode_bit_exact_at_scale_with_near_ties_counted(backend, group):
+    """2^20 values of each cfg-5 distribution against the C oracle (float64,
+    the reference's encoder); disagreements with the FP32 shader encoder are
+    counted and must all be float64 near ties."""
+    n = 1 << 20
+    gauss = o.block_normalised(o.gaussian(n, 1.0, 10), group)
+    heavy = o.duplicate_heavy(n // group, group)
+    for values in (gauss, heavy):
+        book = vq.fit_codebook(values, group=group, sample_vectors=65536)
+        got = backend.encode_large(values, book, group=group)
+        want = oc.encode(values, book, group)
+        np.testing.assert_array_equal(got, want)
+        fp32 = o.nearest_fp32_shader(values[:1 << 16], book, group)
+        mism = np.nonzero(fp32 != o.unpack(want, (1 << 16) // group))[0]
+        ties = set(o.near_ties(values[:1 << 16], book, group, rel=1e-4).tolist())
+        assert set(mism.tolist()) <= ties, "an FP32-vs-FP64 disagreement that is not a near tie"
+
+
+def test_encode_decode_round_trip_is_idempotent(backend):
+    rng = np.random.default_rng(5)
+    for group in (8, 16, 32):
+        book = rand_book(rng, group)
+        codes = o.pack(rng.integers(0, 16, 4096 // group * 8))
+        n = codes.size * 8 * group
+        values = backend.decode_large(codes, book, n, group=group)
+        again = backend.encode_large(values, book, group=group)
+        np.testing.assert_array_equal(again, codes)
+
+
+@pytest.mark.parametrize("flags", [0, 1, 2, 3])
+def test_packed_pair_matmul_is_the_shader_bit_for_bit(backend, flags):
+    rng = np.random.default_rng(40 + flags)
+    for (m, n, k, group) in ((3, 5, 7, 8), (33, 65, 129, 16), (64, 17, 96, 32), (1, 256, 256, 16)):
+        ab, bb = rand_book(rng, group), rand_book(rng, group)
+        ac = o.pack(rng.integers(0, 16, (m * k + group - 1) // group))
+        bc = o.pack(rng.integers(0, 16, (k * n + group - 1) // group))
+        a = VQArray((k, m) if flags & 1 else (m, k), group, ac, ab)
+        b = VQArray((n, k) if flags & 2 else (k, n), group, bc, bb)
+        y = backend.matmul(a, b, transpose_a=bool(flags & 1), transpose_b=bool(flags & 2))
+        want = o.matmul_shader(ac, ab, bc, bb, m, n, k, group, flags)
+        np.testing.assert_array_equal(bits(y), bits(want), err_msg=str((m, n, k, group)))
+
+
+def test_schema1_bounds_are_the_references(backend):
+    a = VQArray((1024, 257), 8, np.zeros((1024 * 257 // 8 + 7) // 8, np.uint32), np.zeros((16, 8), np.float32))
+    b = VQArray((257, 1024), 8, np.zeros((1024 * 257 // 8 + 7) // 8, np.uint32), np.zeros((16, 8), np.float32))
+    with pytest.raises(ValueError, match="vq-matmul-work-limit"):
+        backend.matmul(a, b)
+
+
+def test_adamw_op3_is_the_shader_bit_for_bit(backend):
+    rng = np.random.default_rng(77)
+    for (n, group) in ((129, 16), (4096, 8), (50_001, 32)):
+        states = []
+        for scale in (0.02, 0.01, 1e-4, 1e-3):
+            book = rand_book(rng, group, scale)
+            if scale == 1e-4:
+                book = np.abs(book)
+            states.append(VQArray((n,), group, o.pack(rng.integers(0, 16, (n + group - 1) // group)), book))
+        for step in (1, 7):
+            got = backend.adamw(*states, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step)
+            coefs = o.adamw_coefficients(1e-3, 0.9, 0.999, 1e-8, 0.01, step)
+            want = o.adamw_shader(*(s.decode() for s in states), coefs)
+            for g_, w_ in zip(got, want):
+                np.testing.assert_array_equal(bits(g_), bits(w_))
+
+
+def test_status_bits_refuse_outputs(backend):
+    rng = np.random.default_rng(3)
+    n, group = 64, 8
+    codes = o.pack(rng.integers(0, 16, n // group))
+    negative = -np.abs(rand_book(rng, group))
+    states = np.concatenate([codes] * 4)
+    books = np.concatenate([rand_book(rng, group).reshape(-1), rand_book(rng, group).reshape(-1),
+                            negative.reshape(-1), rand_book(rng, group).reshape(-1)])
+    coefs = o.adamw_coefficients(1e-3, 0.9, 0.999, 1e-8, 0.0, 1)
+    with pytest.raises(ack.AckError, match="status=4"):   # a negative variance (vq4.comp:102)
+        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, books, coefs), n * 12, np.float32)
+    bad = coefs.copy()
+    bad[1] = 1.5                                          # beta1 outside [0, 1)
+    with pytest.raises(ack.AckError, match="status=4"):
+        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, np.abs(books), bad), n * 12, np.float32)
+    bad[1] = np.inf
+    with pytest.raises(ack.AckError, match="status=1"):
+        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, np.abs(books), bad), n * 12, np.float32)
+    nan_book = rand_book(rng, group)
+    nan_book[5, 2] = np.nan
+    with pytest.raises(ack.AckError, match="status=1"):
+        backend._run((1, n, 1, 1, group, 16, 0, 0), (codes, nan_book), n * 4, np.float32)
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_dense_activation_product_within_tolerance(backend, group):
+    rng = np.random.default_rng(100 + group)
+    for (m, n, k, e, nt) in ((1, 1000, 32 * group, 3, True), (3, 517, 64 * group, 2, True),
+                             (8, 300, 32 * group, 1, True), (16, 257, 32 * group, 2, True),
+                             (5, 129, 3 * group + 4, 2, True), (4, 200, 8 * group, 2, False),
+                             (2, 96, 40, 1, False)):
+        ws = []
+        for _ in range(e):
+            shape = (n, k) if nt else (k, n)
+            count = n * k
+            ws.append(VQArray(shape, group, o.pack(rng.integers(0, 16, (count + group - 1) // group)),
+                              rand_book(rng, group, 0.05)))
+        x = rng.standard_normal((e, m, k)).astype(np.float32)
+        y = backend.matmul_dense_grouped(x, ws, transpose_b=nt)
+        for i in range(e):
+            wd = ws[i].decode().astype(np.float64)
+            wmat = wd.T if nt else wd
+            y64 = x[i].astype(np.float64) @ wmat
+            err = normwise(y[i], y64, x[i].astype(np.float64), wmat)
+            assert err <= TOL, (m, n, k, nt, err)
+
+
+def test_dense_matches_cfg2_shapes(backend):
+    """One BASELINE config-2 matrix (11008 x 4096, g16) for M in {1, 4, 16, 64}."""
+    rng = np.random.default_rng(7)
+    n, k, group = 11008, 4096, 16
+    book = rand_book(rng, group, 0.25)
+    codes = o.pack(rng.integers(0, 16, n * k // group))
+    w = VQArray((n, k), group, codes, book)
+    for m in (1, 4, 16, 64):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y = backend.matmul_dense(x, w)
+        y64 = o.dense_nt_f64(x, codes, book, n, k, group)
+        wd = o.decode(codes, book, n * k, group).reshape(n, k).astype(np.float64)
+        assert normwise(y, y64, x.astype(np.float64), wd.T) <= TOL
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_coded_product_within_tolerance(backend, group):
+    rng = np.random.default_rng(200 + group)
+    for (m, n, k, flags) in ((70, 300, 16 * group, 2), (64, 256, 8 * group, 2), (5, 9, 3 * group, 2),
+                             (33, 40, 8 * group + 3, 2), (20, 30, 40, 0), (20, 30, 40, 1), (20, 30, 40, 3)):
+        ab, bb = rand_book(rng, group), rand_book(rng, group)
+        ac = o.pack(rng.integers(0, 16, (m * k + group - 1) // group))
+        bc = o.pack(rng.integers(0, 16, (k * n + group - 1) // group))
+        a = VQArray((k, m) if flags & 1 else (m, k), group, ac, ab)
+        b = VQArray((n, k) if flags & 2 else (k, n), group, bc, bb)
+        y = backend.matmul_coded(a, b, transpose_a=bool(flags & 1), transpose_b=bool(flags & 2))
+        da = a.decode().astype(np.float64)
+        db = b.decode().astype(np.float64)
+        A = da.T if flags & 1 else da
+        B = db.T if flags & 2 else db
+        assert normwise(y, A @ B, A, B) <= TOL, (m, n, k, flags)
+
+
+class HostShaderBackend:
+    """The reference's arithmetic on the host: the CPU encoder, the shader's
+    op 2 and op 3 restated by the oracle."""
+
+    def encode(self, values, codebook, *, group):
+        return vq.encode(values, codebook, group=group)
+
+    def decode(self, value):
+        return value.decode()
+
+    def matmul(self, a, b, *, transpose_a=False, transpose_b=False):
+        m, k = a.shape[::-1] if transpose_a else a.shape
+        _, n = b.shape[::-1] if transpose_b else b.shape
+        flags = int(transpose_a) | (int(transpose_b) << 1)
+        return o.matmul_shader(a.codes, a.codebook, b.codes, b.codebook, m, n, k, a.group, flags)
+
+    def adamw(self, weight, momentum, variance, gradient, *, lr, beta1, beta2, eps, weight_decay, step):
+        coefs = o.adamw_coefficients(lr, beta1, beta2, eps, weight_decay, step)
+        return o.adamw_shader(*(s.decode() for s in (weight, momentum, variance, gradient)), coefs)
+
+
+@pytest.mark.parametrize("shape,group", [((37, 29), 8), ((256, 256), 16), ((1024, 512), 32), ((4096, 1024), 8)])
+def test_fused_vqadamw_step_matches_the_reference_flow(backend, shape, group):
+    rng = np.random.default_rng(sum(shape) + group)
+    w = o.gaussian(shape, 0.02, 7)
+    weight = vq.encode(w, vq.fit_codebook(w, group=group), group=group)
+    dev_opt = VQAdamW(backend, weight, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    host_opt = VQAdamW(HostShaderBackend(), weight, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    for _ in range(2):
+        g = (rng.standard_normal(shape) * 1e-3).astype(np.float32)
+        gimg = vq.encode(g, vq.fit_codebook(g, group=group), group=group)
+        r_dev = dev_opt.step(gimg)
+        r_host = host_opt.step(gimg)
+        for a, b in ((dev_opt.weight, host_opt.weight), (dev_opt.momentum, host_opt.momentum),
+                     (dev_opt.variance, host_opt.variance)):
+            assert a.to_bytes() == b.to_bytes()
+        assert r_dev["changed_weight_values"] == r_host["changed_weight_values"]
+        assert r_dev["step"] == r_host["step"]
+
+
+@pytest.mark.parametrize("group,rare_at", [(8, -1), (16, -1), (32, -1), (8, 1)])
+def test_fused_zero_gradient_moves_no_weight(backend, group, rare_at):
+    """The reference audit's acceptance test on the device path; with the
+    rare entry outside the calibration sample (group 8, position 1) the
+    whole-tensor usage check runs on the device."""
+    vectors = 65536 // group
+    atoms = np.random.default_rng(1).standard_normal((16, group)).astype(np.float32)
+    index = np.insert(np.arange(vectors - 1) % 15, rare_at % vectors, 15)
+    values = atoms[index].reshape(-1)
+    weight = vq.encode(values, atoms, group=group)
+    zero = VQArray(weight.shape, group, np.zeros_like(weight.codes), np.zeros((16, group), np.float32))
+    opt = VQAdamW(backend, weight, lr=1e-3, weight_decay=0.0)
+    before = opt.weight.decode().copy()
+    report = opt.step(zero)
+    assert report["changed_weight_values"] == 0 == int((before != opt.weight.decode()).sum())
+    assert len(np.unique(opt.weight.codebook.round(6), axis=0)) == 16
+
+
+def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device):
+    from alelyon_compute_kit import expert_bank, harness
+    rng = np.random.default_rng(12)
+    roots = []
+    for name in ("dev", "host"):
+        bank = expert_bank.ExpertBank.create(tmp_path / name, expert_bank.BankConfig(1, 2, ((64, 48),) * 3, 16))
+        bank.initialize_expert(0, 1, seed=5, zero_optimizer_state=True)
+        roots.append(bank)
+    x = rng.standard_normal((8, 64)).astype(np.float32)
+    t = rng.standard_normal((8, 48)).astype(np.float32)
+    dev_h = harness.VulkanExpertHarness(roots[0], device=device)
+    host_h = harness.VulkanExpertHarness(roots[1], backend=HostShaderBackend())
+    for _ in range(2):
+        a = dev_h.train_step(x, t, expert=1, beta2=0.999)
+        b = host_h.train_step(x, t, expert=1, beta2=0.999)
+        assert a.loss == b.loss and a.gradient_norm_before_clip == b.gradient_norm_before_clip
+    for ta, tb in zip(roots[0].read_expert(0, 1), roots[1].read_expert(0, 1)):
+        assert ta.to_bytes() == tb.to_bytes()
+    np.testing.assert_array_equal(dev_h.forward(x, expert=1), host_h.forward(x, expert=1))
