@@ -30,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -67,59 +66,69 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock and throttle samples during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    50 ms during the timed region. Read-only: no setting is changed."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, local: int):
+        self.local = local
+        self.samples: list[tuple[int, int, int]] = []
+        self._stop = threading.Event()
+        self.handle = None
+        self.error = None
+
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+        for candidate in (uuid, "GPU-" + uuid):
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(candidate)
+            except pynvml.NVMLError:
+                continue
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.local)
+
+    def _run(self, nvml):
+        while not self._stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(self.handle, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(self.handle, nvml.NVML_CLOCK_SM)
+                reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((sm, mx, reasons))
+            except Exception as exc:  # noqa: BLE001
+                self.error = str(exc)
+                return
+            self._stop.wait(0.05)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            nvml, self.handle = self._open()
+            self.thread = threading.Thread(target=self._run, args=(nvml,), daemon=True)
             self.thread.start()
-        except OSError:
-            self.proc = None
+        except Exception as exc:  # noqa: BLE001
+            self.error = str(exc)
+            self.handle = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.handle is not None:
+            self.thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[4:8]):
-                if flag.lower() in ("active", "1", "yes"):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.error}
+        reasons = set()
+        for _, _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples)}
 
 
 def dist_setup(args):
@@ -185,7 +194,7 @@ def cpu_dense_sample(codes_np, books_np, x_np, budget_s: float):
         oc.dense_nt(x_np[e], codes_np[e], books_np[e], N_ROWS, GROUP)
         done += 1
         elapsed = time.perf_counter() - t0
-        if elapsed >= budget_s or done >= 64:
+        if elapsed >= budget_s or done >= 4096:
             break
     return done * (CODE_BYTES + BOOK_BYTES) / elapsed / 1e9, done, oc.threads(), elapsed
 
@@ -297,6 +306,198 @@ def run_cfg2_e2e(args, torch, vq, codes, books, x, book, local):
             "api": "VQDevice.matmul_dense_grouped (C ABI ack_vq2, host buffers)"}
 
 
+def _timed(torch, fn, steps, warmup, world, device, local):
+    """CUDA-event time of `steps` calls after `warmup`, max over ranks (ms/step)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(steps):
+            fn()
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / steps, clocks.summary()
+
+
+def _fit_from_device(vq, torch, values, group, sample_vectors=65536):
+    """fit_codebook on the CPU from the strided sample of a device tensor
+    (the sample is what fit_codebook would draw from the whole tensor)."""
+    complete = values.numel() // group
+    pos = np.linspace(0, complete - 1, min(complete, sample_vectors), dtype=np.int64)
+    sample = values[: complete * group].view(complete, group)[torch.from_numpy(pos).to(values.device)]
+    return vq.fit_codebook(sample.cpu().numpy().reshape(-1), group=group, sample_vectors=sample_vectors)
+
+
+def run_codec(args, world, rank, local, which):
+    """cfg 5: encode or decode of 2^30 FP32 values (args.dist: gauss or heavy)."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group, n = args.group, args.values
+    gen = torch.Generator(device=device)
+    gen.manual_seed(10 + rank)
+    if args.dist == "heavy":
+        atoms = torch.from_numpy(np.random.default_rng(10).standard_normal((16, group)).astype(np.float32)).to(device)
+        idx = torch.zeros(n // group, dtype=torch.int64, device=device)
+        rare = int(round(idx.numel() * 0.15))
+        idx[:rare] = 1 + torch.arange(rare, device=device) % 15
+        idx = idx[torch.randperm(idx.numel(), generator=gen, device=device)]
+        x = atoms[idx].reshape(-1)
+        del idx
+    else:
+        x = torch.randn(n, generator=gen, device=device)
+        blocks = x.view(-1, group)
+        blocks /= blocks.norm(dim=1, keepdim=True)
+    book = torch.from_numpy(_fit_from_device(vq, torch, x, group)).to(device)
+    codes, status = cuda.encode(x, book, group)
+    cuda.check(status)
+    if which == "encode":
+        fn = lambda: cuda.encode(x, book, group, out=codes, status=status)  # noqa: E731
+    else:
+        fn = lambda: cuda.decode(codes, book, n, group, out=x, status=status)  # noqa: E731
+    ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
+    cuda.check(status)
+    code_bytes = codes.numel() * 4
+    algorithmic = 4 * n + code_bytes + 64 * group
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    achieved = algorithmic / (ms / 1e3) / 1e9
+    kernel = "k_encode" if which == "encode" else "k_decode"
+    result = {
+        "metric": f"vq4 {which} Gvalues/s (cfg5, 2^30 values, g{group}, {args.dist})",
+        "value": round(world * n / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": f"synthetic ({args.dist})",
+        "config": {"workload": f"cfg5-{which}-g{group}-{args.dist}", "values_per_gpu": n, "group": group,
+                   "l2": "inputs larger than L2", "parallelism": f"range-sharded x{world}, no collective"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"{kernel}_cfg5_g{group}"),
+                     "kernel": kernel, "algorithmic_bytes_per_launch": algorithmic},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    if rank == 0 and not args.no_cpu:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import vq_oracle_c as oc
+        m = 1 << 24
+        xs, cb, bk = x[:m].cpu().numpy(), codes[: m // group // 8].cpu().numpy().view(np.uint32), book.cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < args.cpu_budget:
+            if which == "encode":
+                oc.encode(xs, bk, group)
+            else:
+                oc.decode(cb, bk, m, group)
+            reps += 1
+        el = time.perf_counter() - t0
+        result["cpu_baseline"] = {"value": round(reps * m / el / 1e9, 4), "unit": "Gvalues/s", "cores": oc.threads(),
+                                  "kind": "port", "sample": f"{reps} x 2^24 values, {el:.1f} s"}
+    return result
+
+
+def run_cfg3(args, world, rank, local):
+    """cfg 3: both operands coded, X 4096 x 4096 (g32, own book) times
+    W 14336 x 4096 (g32) transposed; the 16x16 codebook inner-product table."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    m, n, k, group = 4096, 14336, 4096, 32
+    gen = torch.Generator(device=device)
+    gen.manual_seed(8)
+    x = torch.randn(m * k, generator=gen, device=device)
+    gen.manual_seed(7)
+    w = torch.randn(n * k, generator=gen, device=device) * 0.02
+    xb = torch.from_numpy(_fit_from_device(vq, torch, x, group, 4096)).to(device)
+    wb = torch.from_numpy(_fit_from_device(vq, torch, w, group, 4096)).to(device)
+    xc, status = cuda.encode(x, xb, group)
+    wc, _ = cuda.encode(w, wb, group, status=status)
+    cuda.check(status)
+    del x, w
+    y = torch.empty((m, n), dtype=torch.float32, device=device)
+    fn = lambda: cuda.coded(xc, xb, wc, wb, m, n, k, group, flags=2, out=y, status=status)  # noqa: E731
+    ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
+    cuda.check(status)
+    flops = 2.0 * m * n * k
+    lookups = m * n * (k // group)
+    byts = xc.numel() * 4 + wc.numel() * 4 + 2 * 64 * group + 4 * m * n
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    return {
+        "metric": "vq4 both-coded GEMM effective TFLOP/s (cfg3, 4096x4096 . (14336x4096)^T, g32)",
+        "value": round(world * flops / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg3-coded-gemm", "M": m, "N": n, "K": k, "group": group,
+                   "lut_lookups_per_s": lookups / (ms / 1e3), "parallelism": f"replicated x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "k_coded_lut",
+                     "note": "the table lookups on the shared-memory pipe bound this kernel, not HBM"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
+def run_cfg4(args, world, rank, local):
+    """cfg 4: the fused coded-state AdamW pass over 8 experts per GPU, each
+    W, M, V of 4096 x 1024 g8, with fitted books (kernel-only timing)."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    experts, rows, cols, group = args.experts_cfg4, 4096, 1024, 8
+    count = rows * cols
+    words = cuda.words_for(count, group)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    codes = torch.empty((experts, 4, words), dtype=torch.int32, device=device)
+    books = torch.empty((experts, 4, 16, group), dtype=torch.float32, device=device)
+    status = cuda.status_word(device)
+    scales = (0.02, 1e-4, 1e-7, 1e-3)
+    for e in range(experts):
+        for s, scale in enumerate(scales):
+            v = torch.randn(count, generator=gen, device=device) * scale
+            if s == 2:
+                v = v.abs()
+            b = torch.from_numpy(_fit_from_device(vq, torch, v, group, 4096)).to(device)
+            books[e, s] = b
+            cuda.encode(v, b, group, out=codes[e, s], status=status)
+    coefs = torch.from_numpy(np.tile(np.array([1e-3, 0.9, 0.999, 1e-8, 0.01, 1 - 0.9 ** 2, 1 - 0.999 ** 2],
+                                              np.float32), (experts, 1))).to(device)
+    new_books = books[:, :3].contiguous()
+    out = torch.empty((experts, 3, words), dtype=torch.int32, device=device)
+    changed = torch.empty(experts, dtype=torch.int32, device=device)
+    fn = lambda: cuda.adamw_encode(codes, books, coefs, new_books, count, group, batch=experts,  # noqa: E731
+                                   out=out, changed=changed, status=status)
+    ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
+    cuda.check(status)
+    byts = codes.numel() * 4 + out.numel() * 4
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    return {
+        "metric": "vq4 fused VQAdamW update Gvalues/s (cfg4, 3 x 4096x1024 g8 per expert, kernel only)",
+        "value": round(world * experts * count / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg4-adamw-encode", "experts_per_gpu": experts, "rows": rows, "cols": cols,
+                   "group": group, "parallelism": f"expert-sharded x{world}, no collective"},
+        "roofline": {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "k_adamw_encode",
+                     "note": "compute-bound (three certified 16-entry searches per value)"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
 def run_reference(args, world, rank):
     """The reference arm: the CPU restatement of the path (decode + dot
     product with all host threads) on a bounded sample of the workload."""
@@ -348,6 +549,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--group", type=int, default=16)
+    ap.add_argument("--values", type=int, default=1 << 30)
+    ap.add_argument("--dist", choices=("gauss", "heavy"), default="gauss")
+    ap.add_argument("--experts-cfg4", type=int, default=8)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -356,6 +561,12 @@ def main():
         result = run_reference(args, world, rank)
     elif args.workload == "cfg2":
         result = run_cfg2(args, world, rank, local)
+    elif args.workload in ("encode", "decode"):
+        result = run_codec(args, world, rank, local, args.workload)
+    elif args.workload == "cfg3":
+        result = run_cfg3(args, world, rank, local)
+    elif args.workload == "cfg4":
+        result = run_cfg4(args, world, rank, local)
     else:
         raise SystemExit(f"unknown workload {args.workload!r}")
     if world > 1:
