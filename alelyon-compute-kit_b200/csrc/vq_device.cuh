@@ -1,5 +1,6 @@
 // Device-side building blocks shared by the vq4 kernels: code access, status
-// flags, the codebook preparation and the certified nearest-entry search.
+// flags, constant-bank codebook slots and the certified nearest-entry search.
+// Included by vq_kernels.cu only (it defines the constant-bank array).
 #pragma once
 
 #include <cstdint>
@@ -28,59 +29,64 @@ __device__ __forceinline__ void flag_warp(uint32_t* status, uint32_t bits) {
   if (all && (threadIdx.x & 31) == (__ffs(mask) - 1)) atomicOr(status, all);
 }
 
-// A codebook prepared for the nearest-entry search, in shared memory.
-//   cT      transposed book, cT[j*4 + q] = (c[4q][j], c[4q+1][j], c[4q+2][j], c[4q+3][j])
-//   rows    the book row-major, for the exact float64 pass
-//   q       fl32(||c_e||^2), the square norm summed in float64 then rounded
-//   cmax2   max_e ||c_e||^2 rounded up
-//   uniq    bit e set when row e differs from every lower row; a duplicate
-//           row can never win because ties keep the lowest index
-//   bad     the book holds a NaN or an infinity
-template <int G>
-struct EncBook {
-  float4 cT[G * 4];
-  float rows[16 * G];
+// Codebooks of in-flight encode launches live in the constant bank. The
+// launcher copies the caller's book into one of kBookSlots slots on the
+// launch stream (stream-ordered, device to device) and picks the kernel
+// instance compiled for that slot, so every book value the 16 x G filter
+// multiplies by is a compile-time constant-bank operand: a warp-wide
+// broadcast from the constant cache, with no shared-memory traffic. A slot
+// holds up to three books of group 32 (the fused AdamW pass re-encodes W, M
+// and V with three books).
+constexpr int kBookSlots = 8;
+constexpr int kSlotFloats = 3 * 16 * 32;
+__constant__ float c_books[kBookSlots][kSlotFloats];
+
+// Book B (0..2) of slot SLOT, row-major 16 x G.
+template <int G, int SLOT, int B>
+struct CBook {
+  static __device__ __forceinline__ float at(int e, int j) { return c_books[SLOT][B * 16 * G + e * G + j]; }
+};
+
+// Facts about a codebook the search needs, computed once per block:
+//   q      fl32(||c_e||^2), the square norm summed in float64 then rounded
+//   cmax2  max_e ||c_e||^2 rounded up
+//   uniq   bit e set when row e differs from every lower row; a duplicate
+//          row can never win because ties keep the lowest index
+//   bad    the book holds a NaN or an infinity
+struct alignas(16) BookMeta {
   float q[16];
   float cmax2;
   uint32_t uniq;
   uint32_t bad;
 };
 
-// Fill `eb` from a global-memory book. All threads of the block call it; it
-// ends with a barrier.
-template <int G>
-__device__ void enc_book_setup(EncBook<G>& eb, const float* __restrict__ book) {
-  float* cT = reinterpret_cast<float*>(eb.cT);
-  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) {
-    const float v = book[i];
-    eb.rows[i] = v;
-    cT[(i % G) * 16 + i / G] = v;
-  }
-  __syncthreads();
+// Fill `m`; every thread of the block calls it, it ends with a barrier.
+template <int G, class Book>
+__device__ void meta_setup(BookMeta& m) {
   if (threadIdx.x < 32) {
     const int e = threadIdx.x & 15;
     double s = 0.0;
     bool bad = false;
     for (int j = 0; j < G; ++j) {
-      const float c = eb.rows[e * G + j];
+      const float c = Book::at(e, j);
       bad |= !finite32(c);
       s = __dadd_rn(s, __dmul_rn(double(c), double(c)));
     }
     bool uniq = true;
     for (int f = 0; f < e; ++f) {
       bool same = true;
-      for (int j = 0; j < G; ++j) same &= eb.rows[f * G + j] == eb.rows[e * G + j];
+      for (int j = 0; j < G; ++j) same &= Book::at(f, j) == Book::at(e, j);
       if (same) uniq = false;
     }
     float up = __double2float_ru(s);
     for (int o = 8; o; o >>= 1) up = fmaxf(up, __shfl_xor_sync(0xffffffffu, up, o));
     const uint32_t u = __ballot_sync(0xffffffffu, uniq) & 0xffffu;
     const uint32_t b = __ballot_sync(0xffffffffu, bad) & 0xffffu;
-    if (threadIdx.x < 16) eb.q[e] = __double2float_rn(s);
+    if (threadIdx.x < 16) m.q[e] = __double2float_rn(s);
     if (threadIdx.x == 0) {
-      eb.cmax2 = up;
-      eb.uniq = u;
-      eb.bad = b != 0;
+      m.cmax2 = up;
+      m.uniq = u;
+      m.bad = b != 0;
     }
   }
   __syncthreads();
@@ -91,9 +97,8 @@ __device__ void enc_book_setup(EncBook<G>& eb, const float* __restrict__ book) {
 // accumulated in component order, d += (v_j - b_j)^2 with each operation
 // rounded on its own, over the first `valid` components; the lowest index
 // wins a tie; a NaN distance wins at its first occurrence (np.argmin).
-template <int G>
-__device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, uint32_t cand,
-                                              const float* __restrict__ rows) {
+template <int G, class Book>
+__device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, uint32_t cand) {
   double best = 0.0;
   int chosen = -1;
   bool nan_seen = false;
@@ -103,7 +108,7 @@ __device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, ui
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       if (j < valid) {
-        const double t = __dsub_rn(double(x[j]), double(rows[e * G + j]));
+        const double t = __dsub_rn(double(x[j]), double(Book::at(e, j)));
         d = __dadd_rn(d, __dmul_rn(t, t));
       }
     }
@@ -122,48 +127,38 @@ __device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, ui
 // Certified nearest entry of one complete vector.
 //
 // Filter: f_e = ||c_e||^2 - 2 x.c_e in FP32 (16 fused multiply-adds per
-// component). |f_e - G_e| <= eps with G_e the exact value of the same
-// expression and eps = (G + 8) 2^-23 (||x||^2 + max ||c||^2): twice the
-// forward-error bound of the FMA chain, the rounded norms and the final FMA,
-// plus an absolute floor for subnormal products. Any entry whose f_e lies
-// within 2 eps of the minimum could be the float64 winner (the float64
-// distances differ from the exact ones by far less than eps); when that
-// candidate set holds more than one distinct row, or anything is not finite,
-// the exact float64 pass decides among the candidates. The result is
-// therefore always the reference encoder's choice, not an approximation.
-template <int G>
-__device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const EncBook<G>& eb,
-                                               bool* certified) {
+// component, the book values constant-bank operands). |f_e - G_e| <= eps
+// with G_e the exact value of the same expression and
+// eps = (G + 8) 2^-23 (||x||^2 + max ||c||^2): twice the forward-error bound
+// of the FMA chain, the rounded norms and the final FMA, plus an absolute
+// floor for subnormal products. Any entry whose f_e lies within 2 eps of the
+// minimum could be the float64 winner (the float64 distances differ from the
+// exact ones by far less than eps); when that candidate set holds more than
+// one distinct row, or anything is not finite, the exact float64 pass decides
+// among the candidates. The result is always the reference encoder's choice.
+template <int G, class Book>
+__device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const BookMeta& m, bool* certified) {
   float acc[16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) acc[e] = 0.f;
   float nx2 = 0.f;
 #pragma unroll
   for (int j = 0; j < G; ++j) {
-    const float4 c0 = eb.cT[j * 4 + 0], c1 = eb.cT[j * 4 + 1];
-    const float4 c2 = eb.cT[j * 4 + 2], c3 = eb.cT[j * 4 + 3];
     const float xj = x[j];
-    acc[0] = fmaf(xj, c0.x, acc[0]);
-    acc[1] = fmaf(xj, c0.y, acc[1]);
-    acc[2] = fmaf(xj, c0.z, acc[2]);
-    acc[3] = fmaf(xj, c0.w, acc[3]);
-    acc[4] = fmaf(xj, c1.x, acc[4]);
-    acc[5] = fmaf(xj, c1.y, acc[5]);
-    acc[6] = fmaf(xj, c1.z, acc[6]);
-    acc[7] = fmaf(xj, c1.w, acc[7]);
-    acc[8] = fmaf(xj, c2.x, acc[8]);
-    acc[9] = fmaf(xj, c2.y, acc[9]);
-    acc[10] = fmaf(xj, c2.z, acc[10]);
-    acc[11] = fmaf(xj, c2.w, acc[11]);
-    acc[12] = fmaf(xj, c3.x, acc[12]);
-    acc[13] = fmaf(xj, c3.y, acc[13]);
-    acc[14] = fmaf(xj, c3.z, acc[14]);
-    acc[15] = fmaf(xj, c3.w, acc[15]);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = fmaf(xj, Book::at(e, j), acc[e]);
     nx2 = fmaf(xj, xj, nx2);
   }
   float f[16];
+  const float4* q4 = reinterpret_cast<const float4*>(m.q);
 #pragma unroll
-  for (int e = 0; e < 16; ++e) f[e] = fmaf(-2.f, acc[e], eb.q[e]);
+  for (int i = 0; i < 4; ++i) {
+    const float4 q = q4[i];
+    f[4 * i + 0] = fmaf(-2.f, acc[4 * i + 0], q.x);
+    f[4 * i + 1] = fmaf(-2.f, acc[4 * i + 1], q.y);
+    f[4 * i + 2] = fmaf(-2.f, acc[4 * i + 2], q.z);
+    f[4 * i + 3] = fmaf(-2.f, acc[4 * i + 3], q.w);
+  }
   float fb = f[0];
   uint32_t best = 0;
 #pragma unroll
@@ -173,19 +168,19 @@ __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const EncBoo
       best = uint32_t(e);
     }
   constexpr float kappa = float(G + 8) * (1.0f / 8388608.0f);
-  const float eps = fmaf(kappa, nx2 + eb.cmax2, 1e-37f);
+  const float eps = fmaf(kappa, nx2 + m.cmax2, 1e-37f);
   const float thr = fmaf(2.f, eps, fb);
   uint32_t cand = 0;
 #pragma unroll
   for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
-  cand &= eb.uniq;
-  const bool clean = finite32(thr) && finite32(fb) && !eb.bad;
+  cand &= m.uniq;
+  const bool clean = finite32(thr) && finite32(fb) && !m.bad;
   if (clean && cand == (1u << best)) {
     *certified = false;
     return best;
   }
   *certified = true;
-  return enc_exact<G>(x, G, clean ? cand : 0xffffu, eb.rows);
+  return enc_exact<G, Book>(x, G, clean ? cand : 0xffffu);
 }
 
 // OR together the nibbles of the 8 lanes that share a word and return the

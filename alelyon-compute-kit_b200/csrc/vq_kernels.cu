@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "vq_device.cuh"
 #include "vq_kernels.hpp"
@@ -103,13 +104,21 @@ __device__ __forceinline__ void load_vector(const float* __restrict__ x, uint64_
   }
 }
 
+// At least 4/2/1 resident blocks for group 8/16/32 (64/128/255 registers);
+// the fused AdamW kernels hold more per thread and take 3 blocks at group 8.
 template <int G>
-__global__ void __launch_bounds__(kThreads) k_encode(const float* __restrict__ x, uint64_t n,
-                                                     const float* __restrict__ book, uint32_t* __restrict__ codes,
-                                                     uint32_t* __restrict__ status, int aligned) {
-  __shared__ EncBook<G> eb;
-  enc_book_setup<G>(eb, book);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && eb.bad) atomicOr(status, kNonfinite);
+constexpr int encode_min_blocks() { return G == 8 ? 4 : (G == 16 ? 2 : 1); }
+template <int G>
+constexpr int adamw_min_blocks() { return G == 8 ? 3 : (G == 16 ? 2 : 1); }
+
+template <int G, int SLOT>
+__global__ void __launch_bounds__(kThreads, encode_min_blocks<G>()) k_encode(const float* __restrict__ x, uint64_t n,
+                                                     uint32_t* __restrict__ codes, uint32_t* __restrict__ status,
+                                                     int aligned) {
+  using Book = CBook<G, SLOT, 0>;
+  __shared__ BookMeta meta;
+  meta_setup<G, Book>(meta);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && meta.bad) atomicOr(status, kNonfinite);
   const uint64_t vectors = (n + G - 1) / G;
   const uint64_t full = n / G;
   const uint64_t words = (vectors + 7) / 8;
@@ -127,10 +136,13 @@ __global__ void __launch_bounds__(kThreads) k_encode(const float* __restrict__ x
 #pragma unroll
         for (int j = 0; j < G; ++j) xr[j] = x[v * G + j];
       }
-#pragma unroll
-      for (int j = 0; j < G; ++j) bits |= finite32(xr[j]) ? 0u : kNonfinite;
       bool certified;
-      idx = enc_vector<G>(xr, eb, &certified);
+      idx = enc_vector<G, Book>(xr, meta, &certified);
+      if (certified) {
+        // the rare path: nonfinite values are flagged here, not on every vector
+#pragma unroll
+        for (int j = 0; j < G; ++j) bits |= finite32(xr[j]) ? 0u : kNonfinite;
+      }
     } else if (v < vectors) {
       // The partial last vector: compare its valid components only (vq.py:171-172).
       const int valid = int(n - v * G);
@@ -138,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) k_encode(const float* __restrict__ x
       for (int j = 0; j < G; ++j) xr[j] = j < valid ? x[v * G + j] : 0.f;
 #pragma unroll
       for (int j = 0; j < G; ++j) bits |= (j < valid && !finite32(xr[j])) ? kNonfinite : 0u;
-      idx = enc_exact<G>(xr, valid, 0xffffu, eb.rows);
+      idx = enc_exact<G, Book>(xr, valid, 0xffffu);
     }
     const uint32_t w = pack_nibbles(idx);
     const uint64_t word = (base >> 3) + (lane >> 3);
@@ -269,81 +281,86 @@ __global__ void __launch_bounds__(kThreads) k_adamw(const uint32_t* __restrict__
 
 // ------------------------------------------------ dense X times coded W^T --
 
-// Shared-memory plan of k_dense_lut: the table P[MC][TC][16] then two code
-// stages of 256 rows x (TC/2 + 16) bytes.
-__host__ __device__ constexpr uint32_t lut_row_pitch(uint32_t tc) { return tc / 2 + 16; }
-
-template <int G, int MC>
-__global__ void __launch_bounds__(kThreads, 1) k_dense_lut(const float* __restrict__ X,
+// Y[b] = X[b] decode(W[b])^T with W stored N x K, vectors along K, K % G == 0.
+//
+// Per (rows of X, t-chunk of TC groups) a block builds the table
+// P[m][t][e] = x[m, tG:tG+G] . c_e in shared memory; then each thread owns
+// one row n of W and adds P[m][t][idx(n, t)] over the chunk: one lookup and
+// one add per (row, group). The rows' codes arrive by cp.async into padded
+// shared rows (conflict-free 16-byte reads), double-buffered. Nibbles are
+// turned into byte offsets four at a time ((w << 2) & 0x3C3C3C3C holds 4*idx
+// of the even nibbles, (w >> 2) & 0x3C3C3C3C of the odd ones) and extracted
+// with one byte permute each; with TC a template constant every table offset
+// is an immediate, so a lookup is one permute, one shared load and one add.
+// A block works on `items_per_expert`-th of one expert's rows.
+template <int G, int MC, int TC>
+__global__ void __launch_bounds__(kThreads, 2) k_dense_lut(const float* __restrict__ X,
                                                            const uint32_t* __restrict__ codes,
                                                            const float* __restrict__ books, float* __restrict__ Y,
-                                                           uint32_t M, uint32_t N, uint32_t K, uint32_t rows_per_block,
-                                                           uint32_t TC, uint64_t words_per_expert,
-                                                           uint32_t* __restrict__ status) {
+                                                           uint32_t M, uint32_t N, uint32_t K,
+                                                           uint32_t items_per_expert, uint32_t batches_per_item,
+                                                           uint64_t words_per_expert, uint32_t* __restrict__ status) {
+  constexpr uint32_t kPitch = TC / 2 + 16;  // bytes of one staged row, padded
+  constexpr uint32_t kStage = kThreads * kPitch;
+  constexpr uint32_t kPieces = TC / 32;     // 16-byte pieces (32 groups) per staged row
   extern __shared__ __align__(16) unsigned char smem[];
-  float* P = reinterpret_cast<float*>(smem);
-  unsigned char* stage0 = smem + size_t(MC) * TC * 16 * 4;
-  const uint32_t pitch = lut_row_pitch(TC);
-  const size_t stage_bytes = size_t(kThreads) * pitch;  // stage b starts at stage0 + b * stage_bytes
-  __shared__ float sbook[16 * 32];
+  float* P = reinterpret_cast<float*>(smem);                       // [MC][TC][16]
+  unsigned char* stage0 = smem + size_t(MC) * TC * 64;             // [2][kThreads][kPitch]
+  __shared__ float sbook[16 * G];
 
-  const uint32_t b = blockIdx.y;
+  const uint32_t e = blockIdx.x / items_per_expert, part = blockIdx.x % items_per_expert;
   const uint32_t T = K / G;
-  const float* Xb = X + uint64_t(b) * M * K;
-  const uint32_t* Cb = codes + uint64_t(b) * words_per_expert;
-  float* Yb = Y + uint64_t(b) * M * N;
-  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) sbook[i] = books[uint64_t(b) * 16 * G + i];
+  const uint32_t nbatches = (N + kThreads - 1) / kThreads;
+  const uint32_t b0 = part * batches_per_item, b1 = min(nbatches, b0 + batches_per_item);
+  if (b0 >= b1) return;  // the whole block leaves together
+  const uint32_t r0 = b0 * kThreads, r1 = min(N, b1 * kThreads);
+  const float* Xb = X + uint64_t(e) * M * K;
+  const unsigned char* Cb = reinterpret_cast<const unsigned char*>(codes + uint64_t(e) * words_per_expert);
+  float* Yb = Y + uint64_t(e) * M * N;
+  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) sbook[i] = books[uint64_t(e) * 16 * G + i];
   __syncthreads();
-  if (blockIdx.x == 0) {
+  if (part == 0) {
     uint32_t bits = 0;
     for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) bits |= finite32(sbook[i]) ? 0u : kNonfinite;
     flag_warp(status, bits);
   }
-  const uint32_t r0 = blockIdx.x * rows_per_block;
-  const uint32_t r1 = min(N, r0 + rows_per_block);
+  const uint32_t nb = (r1 - r0 + kThreads - 1) / kThreads;
 
   for (uint32_t m0 = 0; m0 < M; m0 += MC) {
     const uint32_t mc = min(uint32_t(MC), M - m0);
     for (uint32_t t0 = 0; t0 < T; t0 += TC) {
-      const uint32_t tc = min(TC, T - t0);
-      __syncthreads();  // the previous table is no longer read
-      // P[m][t][e] = sum_j x[m0+m, (t0+t)*G + j] * c[e][j]
-      for (uint32_t i = threadIdx.x; i < mc * tc; i += blockDim.x) {
-        const uint32_t m = i / tc, t = i % tc;
+      __syncthreads();  // the previous table and stages are no longer read
+      for (uint32_t i = threadIdx.x; i < mc * TC; i += blockDim.x) {
+        const uint32_t m = i / TC, t = i % TC;
         const float* xs = Xb + uint64_t(m0 + m) * K + uint64_t(t0 + t) * G;
         float xr[G];
 #pragma unroll
         for (int j = 0; j < G; ++j) xr[j] = __ldg(xs + j);
         float* dst = P + (size_t(m) * TC + t) * 16;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float s = 0.f;
+        for (int c = 0; c < 16; ++c) {
+          float acc = 0.f;
 #pragma unroll
-          for (int j = 0; j < G; ++j) s = fmaf(xr[j], sbook[e * G + j], s);
-          dst[e] = s;
+          for (int j = 0; j < G; ++j) acc = fmaf(xr[j], sbook[c * G + j], acc);
+          dst[c] = acc;
         }
       }
-      __syncthreads();
-      // rows in batches of 256, one row per thread; code tiles double-buffered
-      const uint32_t batches = (r1 - r0 + kThreads - 1) / kThreads;
-      auto issue = [&](uint32_t batch, int buf) {
+      auto issue = [&](uint32_t batch, uint32_t buf) {
         const uint32_t rb = r0 + batch * kThreads;
         const uint32_t nrows = min(uint32_t(kThreads), r1 - rb);
-        const uint32_t pieces = tc / 32;  // 16-byte pieces of this chunk in one row
-        for (uint32_t i = threadIdx.x; i < nrows * pieces; i += blockDim.x) {
-          const uint32_t r = i / pieces, pc = i % pieces;
-          const unsigned char* src = reinterpret_cast<const unsigned char*>(Cb) +
-                                     (uint64_t(rb + r) * T + t0) / 2 + uint64_t(pc) * 16;
-          unsigned char* dst = stage0 + buf * stage_bytes + size_t(r) * pitch + pc * 16;
-          const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+        for (uint32_t i = threadIdx.x; i < nrows * kPieces; i += blockDim.x) {
+          const uint32_t r = i / kPieces, pc = i % kPieces;
+          const unsigned char* src = Cb + (uint64_t(rb + r) * T + t0) / 2 + pc * 16;
+          const uint32_t saddr =
+              static_cast<uint32_t>(__cvta_generic_to_shared(stage0 + buf * kStage + r * kPitch + pc * 16));
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(src));
         }
         asm volatile("cp.async.commit_group;\n" ::);
       };
-      if (batches) issue(0, 0);
-      for (uint32_t batch = 0; batch < batches; ++batch) {
-        const int buf = batch & 1;
-        if (batch + 1 < batches) {
+      issue(0, 0);
+      for (uint32_t batch = 0; batch < nb; ++batch) {
+        const uint32_t buf = batch & 1;
+        if (batch + 1 < nb) {
           issue(batch + 1, buf ^ 1);
           asm volatile("cp.async.wait_group 1;\n" ::);
         } else {
@@ -352,31 +369,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_dense_lut(const float* __restri
         __syncthreads();
         const uint32_t row = r0 + batch * kThreads + threadIdx.x;
         if (row < r1) {
-          float acc[MC];
+          float acc[MC][4];
 #pragma unroll
-          for (int m = 0; m < MC; ++m) acc[m] = 0.f;
-          const uint4* src = reinterpret_cast<const uint4*>(stage0 + buf * stage_bytes + size_t(threadIdx.x) * pitch);
-          for (uint32_t piece = 0; piece < tc / 32; ++piece) {
-            const uint4 q4 = src[piece];
-            const uint32_t wds[4] = {q4.x, q4.y, q4.z, q4.w};
-            const float* Pp = P + size_t(piece) * 32 * 16;
+          for (int m = 0; m < MC; ++m)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+          const unsigned char* rowp = stage0 + buf * kStage + threadIdx.x * kPitch;
+          const unsigned char* Pb = smem;
+#pragma unroll
+          for (int pc = 0; pc < int(kPieces); ++pc) {
+            const uint4 q4 = *reinterpret_cast<const uint4*>(rowp + pc * 16);
+            const uint32_t wd[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
-              const uint32_t w = wds[wi];
+              const uint32_t lo = (wd[wi] << 2) & 0x3C3C3C3Cu;  // 4 * nibbles 0, 2, 4, 6
+              const uint32_t hi = (wd[wi] >> 2) & 0x3C3C3C3Cu;  // 4 * nibbles 1, 3, 5, 7
 #pragma unroll
-              for (int s = 0; s < 8; ++s) {
-                const uint32_t off = (wi * 8 + s) * 16 + ((w >> (4 * s)) & 15u);
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t olo = __byte_perm(lo, 0, 0x4440 + kk);
+                const uint32_t ohi = __byte_perm(hi, 0, 0x4440 + kk);
+                const int t = pc * 32 + wi * 8 + 2 * kk;
 #pragma unroll
-                for (int m = 0; m < MC; ++m)
-                  if (m < int(mc)) acc[m] += Pp[size_t(m) * TC * 16 + off];
+                for (int m = 0; m < MC; ++m) {
+                  const unsigned char* pm = Pb + (size_t(m) * TC + t) * 64;
+                  acc[m][(2 * kk) & 3] += *reinterpret_cast<const float*>(pm + olo);
+                  acc[m][(2 * kk + 1) & 3] += *reinterpret_cast<const float*>(pm + 64 + ohi);
+                }
               }
             }
           }
 #pragma unroll
           for (int m = 0; m < MC; ++m) {
             if (m < int(mc)) {
-              float* y = Yb + uint64_t(m0 + m) * N + row;
-              *y = t0 ? *y + acc[m] : acc[m];
+              const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
+              float* dst = Yb + uint64_t(m0 + m) * N + row;
+              *dst = t0 ? *dst + y : y;
             }
           }
         }
@@ -567,28 +594,26 @@ struct AdamwBatch {
   uint32_t n;             // values per tensor
 };
 
+// AdamW output `state` (0: W', 1: M', 2: V') of the first `valid` values of
+// vector v of expert e, into x (zeros beyond `valid`).
 template <int G>
 __device__ __forceinline__ void adamw_vector(const AdamwBatch& a, const float* __restrict__ sbooks,
-                                             const AdamwCoefs& k, uint32_t e, uint64_t v, int valid,
-                                             float (&w)[G], float (&m)[G], float (&var)[G], uint32_t* bits) {
+                                             const AdamwCoefs& k, uint32_t e, uint64_t v, int valid, int state,
+                                             float (&x)[G], uint32_t* bits) {
   const uint32_t* base = a.codes + uint64_t(e) * 4 * a.words;
   uint32_t code[4];
 #pragma unroll
   for (int s = 0; s < 4; ++s) code[s] = code_at(base + s * a.words, v);
 #pragma unroll
   for (int j = 0; j < G; ++j) {
-    w[j] = m[j] = var[j] = 0.f;
+    x[j] = 0.f;
     if (j < valid) {
       float nw, nm, nv;
       bool skip;
       *bits |= adamw_value(k, sbooks[0 * 16 * G + code[0] * G + j], sbooks[1 * 16 * G + code[1] * G + j],
                            sbooks[2 * 16 * G + code[2] * G + j], sbooks[3 * 16 * G + code[3] * G + j], &nw, &nm,
                            &nv, &skip);
-      if (!skip) {
-        w[j] = nw;
-        m[j] = nm;
-        var[j] = nv;
-      }
+      if (!skip) x[j] = state == 0 ? nw : (state == 1 ? nm : nv);
     }
   }
 }
@@ -627,18 +652,19 @@ __global__ void __launch_bounds__(kThreads) k_adamw_sample(AdamwBatch a, const u
   }
 }
 
-// Entries a trial book selects over the complete vectors of one updated state
-// (the whole-tensor pass of fit_codebook, vq.py:219-222).
-template <int G>
-__global__ void __launch_bounds__(kThreads) k_adamw_usage(AdamwBatch a, uint32_t expert, uint32_t state,
-                                                          const float* __restrict__ trial, uint32_t* __restrict__ out,
-                                                          uint32_t* __restrict__ status) {
+// Entries a trial book (constant slot SLOT, book 0) selects over the
+// complete vectors of one updated state (the whole-tensor pass of
+// fit_codebook, vq.py:219-222).
+template <int G, int SLOT>
+__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage(AdamwBatch a, uint32_t expert, uint32_t state,
+                                                          uint32_t* __restrict__ out, uint32_t* __restrict__ status) {
+  using Book = CBook<G, SLOT, 0>;
   __shared__ float sbooks[4 * 16 * G];
-  __shared__ EncBook<G> eb;
+  __shared__ BookMeta meta;
   __shared__ uint32_t hist[16];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(expert) * 64 * G + i];
   if (threadIdx.x < 16) hist[threadIdx.x] = 0;
-  enc_book_setup<G>(eb, trial);
+  meta_setup<G, Book>(meta);
   const AdamwCoefs k = load_coefs(a.coefs + 7 * expert);
   const uint64_t full = a.n / G;
   const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
@@ -647,13 +673,10 @@ __global__ void __launch_bounds__(kThreads) k_adamw_usage(AdamwBatch a, uint32_t
     const uint64_t v = base + (threadIdx.x & 31);
     uint32_t bits = k.status;
     if (v < full && !bits) {
-      float w[G], m[G], var[G];
-      adamw_vector<G>(a, sbooks, k, expert, v, G, w, m, var, &bits);
+      float x[G];
+      adamw_vector<G>(a, sbooks, k, expert, v, G, int(state), x, &bits);
       bool certified;
-      const uint32_t idx = state == 0 ? enc_vector<G>(w, eb, &certified)
-                          : state == 1 ? enc_vector<G>(m, eb, &certified)
-                                       : enc_vector<G>(var, eb, &certified);
-      atomicAdd(&hist[idx], 1u);
+      atomicAdd(&hist[enc_vector<G, Book>(x, meta, &certified)], 1u);
     }
     flag_warp(status, bits);
   }
@@ -661,20 +684,25 @@ __global__ void __launch_bounds__(kThreads) k_adamw_usage(AdamwBatch a, uint32_t
   if (threadIdx.x < 16 && hist[threadIdx.x]) atomicAdd(out + threadIdx.x, hist[threadIdx.x]);
 }
 
-// decode -> AdamW -> encode of W', M', V' with their new books, one vector
-// per thread, and a count of weight values whose decoded value changed.
-template <int G>
-__global__ void __launch_bounds__(kThreads) k_adamw_encode(AdamwBatch a, const float* __restrict__ new_books,
-                                                           uint32_t* __restrict__ out_codes,
+// decode -> AdamW -> encode of W', M', V' of one expert with their new books
+// (constant slot SLOT, books 0, 1, 2), one vector per thread, and a count of
+// weight values whose decoded value changed.
+template <int G, int SLOT>
+__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_encode(AdamwBatch a, uint32_t e, uint32_t* __restrict__ out_codes,
                                                            uint32_t* __restrict__ changed,
                                                            uint32_t* __restrict__ status) {
+  using BW = CBook<G, SLOT, 0>;
+  using BM = CBook<G, SLOT, 1>;
+  using BV = CBook<G, SLOT, 2>;
   __shared__ float sbooks[4 * 16 * G];
-  __shared__ EncBook<G> eb[3];
-  const uint32_t e = blockIdx.y;
+  __shared__ BookMeta meta[3];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(e) * 64 * G + i];
-  for (int s = 0; s < 3; ++s) enc_book_setup<G>(eb[s], new_books + (uint64_t(e) * 3 + s) * 16 * G);
+  meta_setup<G, BW>(meta[0]);
+  meta_setup<G, BM>(meta[1]);
+  meta_setup<G, BV>(meta[2]);
   const AdamwCoefs k = load_coefs(a.coefs + 7 * e);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && (eb[0].bad || eb[1].bad || eb[2].bad)) atomicOr(status, kNonfinite);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && (meta[0].bad || meta[1].bad || meta[2].bad))
+    atomicOr(status, kNonfinite);
   const uint64_t vectors = (uint64_t(a.n) + G - 1) / G;
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warps = uint64_t(gridDim.x) * (blockDim.x / 32);
@@ -685,22 +713,19 @@ __global__ void __launch_bounds__(kThreads) k_adamw_encode(AdamwBatch a, const f
     uint32_t idx[3] = {0, 0, 0}, bits = k.status;
     if (v < vectors && !bits) {
       const int valid = int(min(uint64_t(G), uint64_t(a.n) - v * G));
-      float w[G], m[G], var[G];
-      adamw_vector<G>(a, sbooks, k, e, v, valid, w, m, var, &bits);
+      float x[G];
       bool certified;
-      if (valid == G) {
-        idx[0] = enc_vector<G>(w, eb[0], &certified);
-        idx[1] = enc_vector<G>(m, eb[1], &certified);
-        idx[2] = enc_vector<G>(var, eb[2], &certified);
-      } else {
-        idx[0] = enc_exact<G>(w, valid, 0xffffu, eb[0].rows);
-        idx[1] = enc_exact<G>(m, valid, 0xffffu, eb[1].rows);
-        idx[2] = enc_exact<G>(var, valid, 0xffffu, eb[2].rows);
-      }
+      // one state at a time: the AdamW arithmetic is recomputed per state
+      // (cheap) so only one vector of values is live
+      adamw_vector<G>(a, sbooks, k, e, v, valid, 0, x, &bits);
+      idx[0] = valid == G ? enc_vector<G, BW>(x, meta[0], &certified) : enc_exact<G, BW>(x, valid, 0xffffu);
+      adamw_vector<G>(a, sbooks, k, e, v, valid, 1, x, &bits);
+      idx[1] = valid == G ? enc_vector<G, BM>(x, meta[1], &certified) : enc_exact<G, BM>(x, valid, 0xffffu);
+      adamw_vector<G>(a, sbooks, k, e, v, valid, 2, x, &bits);
+      idx[2] = valid == G ? enc_vector<G, BV>(x, meta[2], &certified) : enc_exact<G, BV>(x, valid, 0xffffu);
       // vq.py:402: decoded new weight against decoded old weight, value by value
       const uint32_t old = code_at(a.codes + uint64_t(e) * 4 * a.words, v);
-      for (int j = 0; j < valid; ++j)
-        changes += eb[0].rows[idx[0] * G + j] != sbooks[old * G + j];
+      for (int j = 0; j < valid; ++j) changes += BW::at(int(idx[0]), j) != sbooks[old * G + j];
     }
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
@@ -736,6 +761,13 @@ uint32_t grid_for(uint64_t items, int per_sm = 8) {
   return uint32_t(std::max<uint64_t>(1, std::min(want, cap)));
 }
 
+template <typename Kernel>
+int resident_per_sm(Kernel k, size_t smem) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess || n < 1) n = 1;
+  return n;
+}
+
 template <template <int> class F, typename... Args>
 cudaError_t by_group(uint32_t g, Args&&... args) {
   switch (g) {
@@ -746,6 +778,62 @@ cudaError_t by_group(uint32_t g, Args&&... args) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The constant-bank slots of one device. A launch holds the ring's lock from
+// choosing its slot to recording the slot's event: it makes its stream wait
+// for the slot's previous launch (on whatever stream that ran), copies its
+// book(s) into the slot on its own stream, launches, and records the event.
+struct SlotRing {
+  std::mutex mu;
+  uint32_t next = 0;
+  cudaEvent_t done[kBookSlots] = {};
+};
+SlotRing g_rings[64];
+
+class BookSlot {
+ public:
+  BookSlot(cudaStream_t stream, const void* src, size_t bytes) : stream_(stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    ring_ = &g_rings[dev & 63];
+    lock_ = std::unique_lock<std::mutex>(ring_->mu);
+    index_ = int(ring_->next++ % kBookSlots);
+    cudaEvent_t& ev = ring_->done[index_];
+    err_ = ev ? cudaStreamWaitEvent(stream, ev, 0) : cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (err_ == cudaSuccess)
+      err_ = cudaMemcpyToSymbolAsync(c_books, src, bytes, size_t(index_) * kSlotFloats * sizeof(float),
+                                     cudaMemcpyDeviceToDevice, stream);
+  }
+  ~BookSlot() {
+    if (lock_.owns_lock()) release();
+  }
+  int index() const { return index_; }
+  cudaError_t error() const { return err_; }
+  cudaError_t release() {
+    cudaError_t e = cudaEventRecord(ring_->done[index_], stream_);
+    lock_.unlock();
+    return e;
+  }
+
+ private:
+  cudaStream_t stream_;
+  SlotRing* ring_ = nullptr;
+  std::unique_lock<std::mutex> lock_;
+  int index_ = 0;
+  cudaError_t err_ = cudaSuccess;
+};
+
+#define ACK_SLOT_SWITCH(slot, LAUNCH) \
+  switch (slot) {                     \
+    case 0: LAUNCH(0); break;         \
+    case 1: LAUNCH(1); break;         \
+    case 2: LAUNCH(2); break;         \
+    case 3: LAUNCH(3); break;         \
+    case 4: LAUNCH(4); break;         \
+    case 5: LAUNCH(5); break;         \
+    case 6: LAUNCH(6); break;         \
+    default: LAUNCH(7); break;        \
+  }
 
 template <int G>
 struct RunDecode {
@@ -765,8 +853,17 @@ struct RunEncode {
   static cudaError_t run(const float* x, uint64_t n, const float* book, uint32_t* codes, uint32_t* status,
                          cudaStream_t s) {
     const uint64_t vectors = (n + G - 1) / G;
-    k_encode<G><<<grid_for(vectors, 4), kThreads, 0, s>>>(x, n, book, codes, status, aligned16(x) ? 1 : 0);
-    return cudaGetLastError();
+    const int aligned = aligned16(x) ? 1 : 0;
+    const int per_sm = resident_per_sm(k_encode<G, 0>, 0);
+    const uint32_t grid = grid_for(vectors, per_sm);
+    BookSlot slot(s, book, 16 * G * sizeof(float));
+    if (slot.error() != cudaSuccess) return slot.error();
+#define ACK_LAUNCH_ENCODE(S) k_encode<G, S><<<grid, kThreads, 0, s>>>(x, n, codes, status, aligned)
+    ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
+#undef ACK_LAUNCH_ENCODE
+    const cudaError_t e = cudaGetLastError();
+    const cudaError_t r = slot.release();
+    return e != cudaSuccess ? e : r;
   }
 };
 
@@ -782,28 +879,47 @@ struct RunMatmulExact {
   }
 };
 
-template <int G, int MC>
-cudaError_t launch_dense_lut_mc(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t M,
-                                uint32_t N, uint32_t K, uint32_t batch, uint64_t words, uint32_t* status,
-                                cudaStream_t s) {
-  const uint32_t T = K / G;
-  // table budget: MC x TC x 16 floats <= 128 KiB; code stages 2 x 256 rows
-  // x (TC/2 + 16) bytes <= 96 KiB; TC a multiple of 32
-  const uint32_t by_table = (128u * 1024u / (MC * 64u)) / 32u * 32u;
-  const uint32_t by_stage = ((96u * 1024u / (2u * kThreads)) - 16u) * 2u / 32u * 32u;
-  uint32_t tc = std::min<uint32_t>(T, std::min(by_table, by_stage));
-  tc = std::max<uint32_t>(tc, 32u);
-  const size_t smem = size_t(MC) * tc * 64 + 2 * size_t(kThreads) * lut_row_pitch(tc);
-  // rows per block: enough blocks to fill the GPU, many rows to amortise the table
-  const uint64_t want_blocks = uint64_t(sm_count()) * 4;
-  uint64_t rows = (uint64_t(N) * batch + want_blocks - 1) / want_blocks;
-  rows = std::min<uint64_t>(std::max<uint64_t>(rows, kThreads), 8192);
-  rows = (rows + kThreads - 1) / kThreads * kThreads;
-  dim3 grid(uint32_t((N + rows - 1) / rows), batch);
-  cudaError_t err = cudaFuncSetAttribute(k_dense_lut<G, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+// Rows of W per work item, in 256-row batches: the fewest waves of resident
+// blocks, each item's table build counted as 0.3 of a batch.
+uint32_t balance_batches(uint32_t nbatches, uint32_t experts, uint64_t resident) {
+  double best = 1e300;
+  uint32_t pick = nbatches;
+  for (uint32_t b = 1; b <= nbatches; ++b) {
+    const uint64_t items = uint64_t(experts) * ((nbatches + b - 1) / b);
+    const uint64_t waves = (items + resident - 1) / resident;
+    const double cost = double(waves) * (b + 0.3);
+    if (cost < best - 1e-9) {
+      best = cost;
+      pick = b;
+    }
+  }
+  return pick;
+}
+
+template <int G, int MC, int TC>
+cudaError_t launch_dense_lut(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t M,
+                             uint32_t N, uint32_t K, uint32_t batch, uint64_t words, uint32_t* status,
+                             cudaStream_t s) {
+  const size_t smem = size_t(MC) * TC * 64 + 2 * size_t(kThreads) * (TC / 2 + 16);
+  cudaError_t err = cudaFuncSetAttribute(k_dense_lut<G, MC, TC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
   if (err != cudaSuccess) return err;
-  k_dense_lut<G, MC><<<grid, kThreads, smem, s>>>(X, codes, books, Y, M, N, K, uint32_t(rows), tc, words, status);
+  const uint64_t resident = uint64_t(sm_count()) * resident_per_sm(k_dense_lut<G, MC, TC>, smem);
+  const uint32_t nbatches = (N + kThreads - 1) / kThreads;
+  const uint32_t per_item = balance_batches(nbatches, batch, resident);
+  const uint32_t items = (nbatches + per_item - 1) / per_item;
+  k_dense_lut<G, MC, TC><<<uint32_t(uint64_t(items) * batch), kThreads, smem, s>>>(
+      X, codes, books, Y, M, N, K, items, per_item, words, status);
   return cudaGetLastError();
+}
+
+template <int G, int MC>
+cudaError_t launch_dense_mc(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t M,
+                            uint32_t N, uint32_t K, uint32_t batch, uint64_t words, uint32_t* status, cudaStream_t s) {
+  const uint32_t T = K / G;
+  if (MC <= 2 && T % 256 == 0) return launch_dense_lut<G, MC, (MC <= 2 ? 256 : 128)>(X, codes, books, Y, M, N, K, batch, words, status, s);
+  if (MC > 2 && T % 128 == 0) return launch_dense_lut<G, MC, 128>(X, codes, books, Y, M, N, K, batch, words, status, s);
+  return launch_dense_lut<G, MC, 32>(X, codes, books, Y, M, N, K, batch, words, status, s);
 }
 
 template <int G>
@@ -818,10 +934,10 @@ struct RunDense {
     const uint64_t words = packed_words(uint64_t(N) * K, G);
     const bool nt = (p.flags & 2u) != 0;
     if (nt && K % G == 0 && (K / G) % 32 == 0 && aligned16(codes) && (words * 4) % 16 == 0) {
-      if (M == 1) return launch_dense_lut_mc<G, 1>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
-      if (M == 2) return launch_dense_lut_mc<G, 2>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
-      if (M <= 4) return launch_dense_lut_mc<G, 4>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
-      return launch_dense_lut_mc<G, 8>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
+      if (M == 1) return launch_dense_mc<G, 1>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
+      if (M == 2) return launch_dense_mc<G, 2>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
+      if (M <= 4) return launch_dense_mc<G, 4>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
+      return launch_dense_mc<G, 8>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
     }
     Operand A{X, nullptr, nullptr, 0};
     Operand B{nullptr, codes, books, nt ? 1 : 0};
@@ -870,21 +986,40 @@ struct RunAdamwFused {
       dim3 grid(std::max<uint32_t>(1, std::min<uint32_t>(uint32_t((items + kThreads - 1) / kThreads), 64)), p.batch);
       k_adamw_sample<G><<<grid, kThreads, 0, s>>>(a, static_cast<const uint32_t*>(ptr[3]), p.aux0,
                                                    static_cast<float*>(ptr[5]), status);
-    } else if (p.op == Op::AdamwUsage) {
+      return cudaGetLastError();
+    }
+    if (p.op == Op::AdamwUsage) {
       cudaError_t err = cudaMemsetAsync(ptr[5], 0, 16 * sizeof(uint32_t), s);
       if (err != cudaSuccess) return err;
-      k_adamw_usage<G><<<grid_for(p.m / G, 4), kThreads, 0, s>>>(a, p.aux1, p.aux0, static_cast<const float*>(ptr[3]),
-                                                                 static_cast<uint32_t*>(ptr[5]), status);
-    } else {
-      cudaError_t err = cudaMemsetAsync(ptr[6], 0, size_t(p.batch) * sizeof(uint32_t), s);
-      if (err != cudaSuccess) return err;
-      const uint32_t per = std::max<uint32_t>(1, grid_for(vectors * p.batch, 4) / p.batch);
-      dim3 grid(std::min<uint32_t>(per, uint32_t((vectors + kThreads - 1) / kThreads)), p.batch);
-      k_adamw_encode<G><<<grid, kThreads, 0, s>>>(a, static_cast<const float*>(ptr[3]),
-                                                   static_cast<uint32_t*>(ptr[5]), static_cast<uint32_t*>(ptr[6]),
-                                                   status);
+      const uint32_t grid = grid_for(p.m / G, resident_per_sm(k_adamw_usage<G, 0>, 0));
+      BookSlot slot(s, ptr[3], 16 * G * sizeof(float));
+      if (slot.error() != cudaSuccess) return slot.error();
+      uint32_t* out = static_cast<uint32_t*>(ptr[5]);
+#define ACK_LAUNCH_USAGE(S) k_adamw_usage<G, S><<<grid, kThreads, 0, s>>>(a, p.aux1, p.aux0, out, status)
+      ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_USAGE)
+#undef ACK_LAUNCH_USAGE
+      const cudaError_t e = cudaGetLastError();
+      const cudaError_t r = slot.release();
+      return e != cudaSuccess ? e : r;
     }
-    return cudaGetLastError();
+    cudaError_t err = cudaMemsetAsync(ptr[6], 0, size_t(p.batch) * sizeof(uint32_t), s);
+    if (err != cudaSuccess) return err;
+    const uint32_t grid = grid_for(vectors, resident_per_sm(k_adamw_encode<G, 0>, 0));
+    const float* new_books = static_cast<const float*>(ptr[3]);
+    uint32_t* out = static_cast<uint32_t*>(ptr[5]);
+    uint32_t* changed = static_cast<uint32_t*>(ptr[6]);
+    for (uint32_t e = 0; e < p.batch; ++e) {
+      BookSlot slot(s, new_books + uint64_t(e) * 3 * 16 * G, 3 * 16 * G * sizeof(float));
+      if (slot.error() != cudaSuccess) return slot.error();
+#define ACK_LAUNCH_ADAMW(S) k_adamw_encode<G, S><<<grid, kThreads, 0, s>>>(a, e, out, changed, status)
+      ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ADAMW)
+#undef ACK_LAUNCH_ADAMW
+      const cudaError_t le = cudaGetLastError();
+      const cudaError_t r = slot.release();
+      if (le != cudaSuccess) return le;
+      if (r != cudaSuccess) return r;
+    }
+    return cudaSuccess;
   }
 };
 
@@ -930,8 +1065,8 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
 }
 
 const char* kernel_manifest() {
-  return "vq4-b200/1 sm_100a: k_decode k_decode_scalar k_encode k_matmul_exact k_adamw k_dense_lut "
-         "k_coded_lut k_gemm_generic k_adamw_sample k_adamw_usage k_adamw_encode";
+  return "vq4-b200/2 sm_100a: k_decode k_decode_scalar k_encode(constant-bank books) k_matmul_exact k_adamw "
+         "k_dense_lut(byte-permute lookups) k_coded_lut k_gemm_generic k_adamw_sample k_adamw_usage k_adamw_encode";
 }
 
 }  // namespace ack

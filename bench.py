@@ -224,11 +224,13 @@ def run_cfg2(args, world, rank, local):
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("timed")
         start.record()
         for _ in range(args.steps):
             step()
         stop.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = start.elapsed_time(stop)
     if world > 1:
         import torch.distributed as dist
@@ -316,11 +318,13 @@ def _timed(torch, fn, steps, warmup, world, device, local):
         dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("timed")
         start.record()
         for _ in range(steps):
             fn()
         stop.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = start.elapsed_time(stop)
     if world > 1:
         import torch.distributed as dist

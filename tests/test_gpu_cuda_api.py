@@ -71,3 +71,30 @@ def test_grouped_dense_on_a_side_stream():
 def test_launch_refuses_host_tensors_and_mixed_devices():
     with pytest.raises(ack.AckError, match="not a CUDA tensor"):
         cuda.decode(torch.zeros(1, dtype=torch.int32), torch.zeros(16, 8), 8, 8)
+
+
+def test_concurrent_encodes_with_different_books_on_many_streams():
+    """16 encodes with 16 different codebooks, interleaved over 4 streams,
+    wrap the constant-bank book slots twice; every result must still be the
+    oracle's (a slot is reused only after its previous kernel finished)."""
+    from alelyon_compute_kit import vq
+    rng = np.random.default_rng(11)
+    group, n = 16, 1 << 20
+    streams = [torch.cuda.Stream() for _ in range(4)]
+    jobs = []
+    for i in range(16):
+        x = rng.standard_normal(n).astype(np.float32)
+        book = rng.standard_normal((16, group)).astype(np.float32)
+        jobs.append((x, book))
+    outs = []
+    for i, (x, book) in enumerate(jobs):
+        s = streams[i % 4]
+        with torch.cuda.stream(s):
+            tx = torch.from_numpy(x).cuda()
+            tb = torch.from_numpy(book).cuda()
+            codes, status = cuda.encode(tx, tb, group)
+            outs.append((codes, status, tx, tb))
+    torch.cuda.synchronize()
+    for (x, book), (codes, status, _, _) in zip(jobs, outs):
+        cuda.check(status)
+        np.testing.assert_array_equal(u32(codes), oc.encode(x, book, group))

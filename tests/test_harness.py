@@ -77,7 +77,8 @@ def test_bank_round_trip_and_refusals(tmp_path):
     stats = bank.stats()
     assert stats["materialized_experts"] == 1 and stats["updated_experts"] == 1
     # a corrupted shard is refused
-    shard = next(p for p in (tmp_path / "b").iterdir() if p.suffix == ".vq")
+    generation = json.loads((tmp_path / "b" / "expert-1-2.json").read_bytes())["generation"]
+    shard = tmp_path / "b" / f"expert-1-2-g{generation}-t0.vq"
     data = bytearray(shard.read_bytes())
     data[-1] ^= 1
     shard.write_bytes(bytes(data))
