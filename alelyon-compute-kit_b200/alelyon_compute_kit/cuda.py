@@ -21,12 +21,17 @@ from . import ack
 
 ENTRIES = 16
 OP_ENCODE1, OP_DECODE1, OP_MATMUL1, OP_ADAMW1 = 0, 1, 2, 3
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE = range(16, 23)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK = range(16, 24)
 
 
 def words_for(count: int, group: int) -> int:
     """u32 words of the packed image of `count` values."""
     return ((count + group - 1) // group + 7) // 8
+
+
+def tile32_words(rows: int, cols: int, group: int) -> int:
+    """u32 words of the tile32 layout of a coded rows x cols matrix."""
+    return (rows + 31) // 32 * 32 * (cols // group) // 8
 
 
 def plan1(op, m, n, k, group, flags=0) -> bytes:
@@ -101,14 +106,34 @@ def encode(x, book, group: int, *, out=None, status=None):
     return out, status
 
 
-def dense(x, codes, books, n: int, group: int, *, transpose_b: bool = True, out=None, status=None):
+def repack_tile32(codes, n: int, k: int, group: int, *, out=None, status=None):
+    """The tile32 layout of E canonical n x k images (vectors along k,
+    (k / group) % 32 == 0): `codes` (E, words) int32 -> (E, tile32 words).
+    Static weights are repacked once; `dense(..., layout="tile32")` then reads
+    each warp's 32 rows as coalesced 512-byte lines."""
+    e = codes.shape[0]
+    out = torch.empty((e, tile32_words(n, k, group)), dtype=torch.int32, device=codes.device) if out is None else out
+    status = status_word(codes.device) if status is None else status
+    launch(plan2(OP_REPACK, n, 1, k, group, batch=e), [codes, None, None, None, None, out, None, status])
+    return out, status
+
+
+def dense(x, codes, books, n: int, group: int, *, transpose_b: bool = True, layout: str = "canonical", out=None,
+          status=None):
     """Y[e] = X[e] @ decode(W[e]).T (W[e] stored n x k) for e < E, one launch.
-    `x` (E, M, K) float32; `codes` (E, words) int32; `books` (E, 16, group)."""
+    `x` (E, M, K) float32; `codes` (E, words) int32, canonical or (layout
+    "tile32", from `repack_tile32`); `books` (E, 16, group)."""
     e, m, k = x.shape
     out = torch.empty((e, m, n), dtype=torch.float32, device=x.device) if out is None else out
     status = status_word(x.device) if status is None else status
-    launch(plan2(OP_DENSE, m, n, k, group, flags=2 if transpose_b else 0, batch=e),
-           [x, codes, books, None, None, out, None, status])
+    flags = 2 if transpose_b else 0
+    if layout == "tile32":
+        if not transpose_b:
+            raise ack.AckError("the tile32 layout holds W stored n x k (transpose_b=True)")
+        flags |= 4
+    elif layout != "canonical":
+        raise ack.AckError(f"unknown code layout {layout!r}")
+    launch(plan2(OP_DENSE, m, n, k, group, flags=flags, batch=e), [x, codes, books, None, None, out, None, status])
     return out, status
 
 

@@ -39,12 +39,20 @@ __device__ __forceinline__ void flag_warp(uint32_t* status, uint32_t bits) {
 // and V with three books).
 constexpr int kBookSlots = 8;
 constexpr int kSlotFloats = 3 * 16 * 32;
-__constant__ float c_books[kBookSlots][kSlotFloats];
+__constant__ float4 c_books[kBookSlots][kSlotFloats / 4];
 
-// Book B (0..2) of slot SLOT, row-major 16 x G.
+// Book B (0..2) of slot SLOT, row-major 16 x G, read in 16-byte quads: one
+// constant-bank load feeds four FMAs (scalar constant loads with computed
+// offsets would saturate the address-divergence unit instead).
 template <int G, int SLOT, int B>
 struct CBook {
-  static __device__ __forceinline__ float at(int e, int j) { return c_books[SLOT][B * 16 * G + e * G + j]; }
+  // components 4q..4q+3 of entry e
+  static __device__ __forceinline__ float4 quad(int e, int q) { return c_books[SLOT][(B * 16 * G + e * G) / 4 + q]; }
+  static __device__ __forceinline__ float at(int e, int j) {
+    const float4 t = quad(e, j >> 2);
+    const int r = j & 3;
+    return r == 0 ? t.x : (r == 1 ? t.y : (r == 2 ? t.z : t.w));
+  }
 };
 
 // Facts about a codebook the search needs, computed once per block:
@@ -60,9 +68,15 @@ struct alignas(16) BookMeta {
   uint32_t bad;
 };
 
-// Fill `m`; every thread of the block calls it, it ends with a barrier.
+// The BookMeta of each slot's books, written once per launch by
+// k_book_meta right after the slot is filled (stream-ordered before the
+// kernels that read it).
+__device__ BookMeta g_meta[kBookSlots][3];
+
+// Compute `m` with the first warp of the block (the other threads return
+// at once); no barrier.
 template <int G, class Book>
-__device__ void meta_setup(BookMeta& m) {
+__device__ void meta_compute(BookMeta& m) {
   if (threadIdx.x < 32) {
     const int e = threadIdx.x & 15;
     double s = 0.0;
@@ -89,6 +103,15 @@ __device__ void meta_setup(BookMeta& m) {
       m.bad = b != 0;
     }
   }
+}
+
+// Copy slot SLOT's meta of book B into shared memory; all threads call it,
+// it ends with a barrier.
+template <int SLOT, int B>
+__device__ __forceinline__ void meta_load(BookMeta& m) {
+  constexpr int kWords = sizeof(BookMeta) / 4;
+  if (threadIdx.x < kWords)
+    reinterpret_cast<uint32_t*>(&m)[threadIdx.x] = reinterpret_cast<const uint32_t*>(&g_meta[SLOT][B])[threadIdx.x];
   __syncthreads();
 }
 
@@ -98,19 +121,26 @@ __device__ void meta_setup(BookMeta& m) {
 // rounded on its own, over the first `valid` components; the lowest index
 // wins a tie; a NaN distance wins at its first occurrence (np.argmin).
 template <int G, class Book>
+__device__ __noinline__ uint32_t enc_exact_mem(const float* x, int valid, uint32_t cand);
+
+// Inline wrapper: the exact pass is rare, so it lives out of line and the
+// hot path's register budget stays the filter's.
+template <int G, class Book>
 __device__ __forceinline__ uint32_t enc_exact(const float (&x)[G], int valid, uint32_t cand) {
+  return enc_exact_mem<G, Book>(x, valid, cand);
+}
+
+template <int G, class Book>
+__device__ __noinline__ uint32_t enc_exact_mem(const float* x, int valid, uint32_t cand) {
   double best = 0.0;
   int chosen = -1;
   bool nan_seen = false;
   for (int e = 0; e < 16; ++e) {
     if (!((cand >> e) & 1u)) continue;
     double d = 0.0;
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      if (j < valid) {
-        const double t = __dsub_rn(double(x[j]), double(Book::at(e, j)));
-        d = __dadd_rn(d, __dmul_rn(t, t));
-      }
+    for (int j = 0; j < valid; ++j) {
+      const double t = __dsub_rn(double(x[j]), double(Book::at(e, j)));
+      d = __dadd_rn(d, __dmul_rn(t, t));
     }
     if (nan_seen) continue;
     if (d != d) {
@@ -143,11 +173,14 @@ __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const BookMe
   for (int e = 0; e < 16; ++e) acc[e] = 0.f;
   float nx2 = 0.f;
 #pragma unroll
-  for (int j = 0; j < G; ++j) {
-    const float xj = x[j];
+  for (int q = 0; q < G / 4; ++q) {
+    const float x0 = x[4 * q], x1 = x[4 * q + 1], x2 = x[4 * q + 2], x3 = x[4 * q + 3];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = fmaf(xj, Book::at(e, j), acc[e]);
-    nx2 = fmaf(xj, xj, nx2);
+    for (int e = 0; e < 16; ++e) {
+      const float4 c = Book::quad(e, q);  // components in order: the same sums as one by one
+      acc[e] = fmaf(x3, c.w, fmaf(x2, c.z, fmaf(x1, c.y, fmaf(x0, c.x, acc[e]))));
+    }
+    nx2 = fmaf(x3, x3, fmaf(x2, x2, fmaf(x1, x1, fmaf(x0, x0, nx2))));
   }
   float f[16];
   const float4* q4 = reinterpret_cast<const float4*>(m.q);

@@ -104,20 +104,40 @@ __device__ __forceinline__ void load_vector(const float* __restrict__ x, uint64_
   }
 }
 
-// At least 4/2/1 resident blocks for group 8/16/32 (64/128/255 registers);
-// the fused AdamW kernels hold more per thread and take 3 blocks at group 8.
+// At least 4/3/2 resident blocks for group 8/16/32; the fused AdamW kernels
+// hold more per thread.
 template <int G>
-constexpr int encode_min_blocks() { return G == 8 ? 4 : (G == 16 ? 2 : 1); }
+constexpr int encode_min_blocks() { return G == 8 ? 4 : (G == 16 ? 3 : 2); }
 template <int G>
 constexpr int adamw_min_blocks() { return G == 8 ? 3 : (G == 16 ? 2 : 1); }
 
+// BookMeta of the NB books in slot SLOT, into g_meta (one warp).
+template <int G, int SLOT, int NB>
+__global__ void k_book_meta() {
+  __shared__ BookMeta m;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b == 0) meta_compute<G, CBook<G, SLOT, 0>>(m);
+    if (b == 1) meta_compute<G, CBook<G, SLOT, 1>>(m);
+    if (b == 2) meta_compute<G, CBook<G, SLOT, 2>>(m);
+    __syncwarp();
+    constexpr int kWords = sizeof(BookMeta) / 4;
+    if (threadIdx.x < kWords)
+      reinterpret_cast<uint32_t*>(&g_meta[SLOT][b])[threadIdx.x] = reinterpret_cast<const uint32_t*>(&m)[threadIdx.x];
+    __syncwarp();
+  }
+}
+
+// A persistent grid; each warp takes 32 consecutive vectors per step (one
+// per lane) and packs their nibbles into 4 words with shuffles.
 template <int G, int SLOT>
 __global__ void __launch_bounds__(kThreads, encode_min_blocks<G>()) k_encode(const float* __restrict__ x, uint64_t n,
-                                                     uint32_t* __restrict__ codes, uint32_t* __restrict__ status,
-                                                     int aligned) {
+                                                                             uint32_t* __restrict__ codes,
+                                                                             uint32_t* __restrict__ status,
+                                                                             int aligned) {
   using Book = CBook<G, SLOT, 0>;
   __shared__ BookMeta meta;
-  meta_setup<G, Book>(meta);
+  meta_load<SLOT, 0>(meta);
   if (blockIdx.x == 0 && threadIdx.x == 0 && meta.bad) atomicOr(status, kNonfinite);
   const uint64_t vectors = (n + G - 1) / G;
   const uint64_t full = n / G;
@@ -413,6 +433,126 @@ __global__ void __launch_bounds__(kThreads, 2) k_dense_lut(const float* __restri
   }
 }
 
+// Repack E canonical N x K images (vectors along K) into the tile32 layout:
+// 16-byte unit c of row r goes to ((r / 32) * T/32 + c) * 32 + r % 32; rows
+// past N in the last tile become zero codes.
+__global__ void __launch_bounds__(kThreads) k_repack_tile32(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                            uint32_t N, uint32_t T, uint64_t src_units,
+                                                            uint64_t dst_units, uint32_t batch) {
+  const uint32_t ct = T / 32;  // 16-byte units per row
+  const uint64_t total = dst_units * batch;
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t e = i / dst_units, u = i % dst_units;
+    const uint32_t lane = uint32_t(u % 32);
+    const uint64_t tc = u / 32;
+    const uint32_t c = uint32_t(tc % ct);
+    const uint64_t row = (tc / ct) * 32 + lane;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < N) v = __ldg(src + e * src_units + row * ct + c);
+    dst[i] = v;
+  }
+}
+
+// Y[b] = X[b] decode(W[b])^T with W[b] in the tile32 layout. The same table
+// and the same per-row lookup order as k_dense_lut (results are bitwise the
+// same), but each warp reads its 32 rows' codes as coalesced 512-byte lines
+// straight into registers: no shared-memory staging and no barrier inside a
+// t-chunk. A block shares one table; its warps take row tiles in turn.
+template <int G, int MC, int TC>
+__global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restrict__ X,
+                                                           const uint4* __restrict__ codes,
+                                                           const float* __restrict__ books, float* __restrict__ Y,
+                                                           uint32_t M, uint32_t N, uint32_t K,
+                                                           uint32_t items_per_expert, uint32_t tiles_per_item,
+                                                           uint64_t units_per_expert, uint32_t* __restrict__ status) {
+  constexpr int kPieces = TC / 32;
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* P = reinterpret_cast<float*>(smem);  // [MC][TC][16]
+  __shared__ float sbook[16 * G];
+  const uint32_t e = blockIdx.x / items_per_expert, part = blockIdx.x % items_per_expert;
+  const uint32_t T = K / G, ct = T / 32;
+  const uint32_t ntiles = (N + 31) / 32;
+  const uint32_t tl0 = part * tiles_per_item, tl1 = min(ntiles, tl0 + tiles_per_item);
+  if (tl0 >= tl1) return;  // the whole block leaves together
+  const float* Xb = X + uint64_t(e) * M * K;
+  const uint4* Cb = codes + uint64_t(e) * units_per_expert;
+  float* Yb = Y + uint64_t(e) * M * N;
+  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) sbook[i] = books[uint64_t(e) * 16 * G + i];
+  __syncthreads();
+  if (part == 0) {
+    uint32_t bits = 0;
+    for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) bits |= finite32(sbook[i]) ? 0u : kNonfinite;
+    flag_warp(status, bits);
+  }
+  const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (uint32_t m0 = 0; m0 < M; m0 += MC) {
+    const uint32_t mc = min(uint32_t(MC), M - m0);
+    for (uint32_t t0 = 0; t0 < T; t0 += TC) {
+      __syncthreads();  // the previous table is no longer read
+      for (uint32_t i = threadIdx.x; i < mc * TC; i += blockDim.x) {
+        const uint32_t m = i / TC, t = i % TC;
+        const float* xs = Xb + uint64_t(m0 + m) * K + uint64_t(t0 + t) * G;
+        float xr[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) xr[j] = __ldg(xs + j);
+        float* dst = P + (size_t(m) * TC + t) * 16;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < G; ++j) acc = fmaf(xr[j], sbook[c * G + j], acc);
+          dst[c] = acc;
+        }
+      }
+      __syncthreads();
+      for (uint32_t tile = tl0 + warp; tile < tl1; tile += kThreads / 32) {
+        const uint4* src = Cb + (uint64_t(tile) * ct + t0 / 32) * 32 + lane;
+        uint4 q[kPieces];
+#pragma unroll
+        for (int pc = 0; pc < kPieces; ++pc) q[pc] = __ldg(src + pc * 32);
+        float acc[MC][4];
+#pragma unroll
+        for (int m = 0; m < MC; ++m)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[m][r] = 0.f;
+        const unsigned char* Pb = smem;
+#pragma unroll
+        for (int pc = 0; pc < kPieces; ++pc) {
+          const uint32_t wd[4] = {q[pc].x, q[pc].y, q[pc].z, q[pc].w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t lo = (wd[wi] << 2) & 0x3C3C3C3Cu;  // 4 * nibbles 0, 2, 4, 6
+            const uint32_t hi = (wd[wi] >> 2) & 0x3C3C3C3Cu;  // 4 * nibbles 1, 3, 5, 7
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t olo = __byte_perm(lo, 0, 0x4440 + kk);
+              const uint32_t ohi = __byte_perm(hi, 0, 0x4440 + kk);
+              const int t = pc * 32 + wi * 8 + 2 * kk;
+#pragma unroll
+              for (int m = 0; m < MC; ++m) {
+                const unsigned char* pm = Pb + (size_t(m) * TC + t) * 64;
+                acc[m][(2 * kk) & 3] += *reinterpret_cast<const float*>(pm + olo);
+                acc[m][(2 * kk + 1) & 3] += *reinterpret_cast<const float*>(pm + 64 + ohi);
+              }
+            }
+          }
+        }
+        const uint32_t row = tile * 32 + lane;
+        if (row < N) {
+#pragma unroll
+          for (int m = 0; m < MC; ++m) {
+            if (m < int(mc)) {
+              const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
+              float* dst = Yb + uint64_t(m0 + m) * N + row;
+              *dst = t0 ? *dst + y : y;
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------ coded A times coded B^T (LUT) --
 
 // C[m, n] = sum_t L[a(m,t)][b(n,t)] with L = C_A C_B^T (16 x 16, each entry
@@ -594,8 +734,36 @@ struct AdamwBatch {
   uint32_t n;             // values per tensor
 };
 
-// AdamW output `state` (0: W', 1: M', 2: V') of the first `valid` values of
-// vector v of expert e, into x (zeros beyond `valid`).
+// AdamW outputs W', M', V' of the first `valid` values of vector v of
+// expert e (zeros beyond `valid`).
+template <int G>
+__device__ __forceinline__ void adamw_vector3(const AdamwBatch& a, const float* __restrict__ sbooks,
+                                              const AdamwCoefs& k, uint32_t e, uint64_t v, int valid, float (&w)[G],
+                                              float (&m)[G], float (&var)[G], uint32_t* bits) {
+  const uint32_t* base = a.codes + uint64_t(e) * 4 * a.words;
+  uint32_t code[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) code[s] = code_at(base + s * a.words, v);
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    w[j] = m[j] = var[j] = 0.f;
+    if (j < valid) {
+      float nw, nm, nv;
+      bool skip;
+      *bits |= adamw_value(k, sbooks[0 * 16 * G + code[0] * G + j], sbooks[1 * 16 * G + code[1] * G + j],
+                           sbooks[2 * 16 * G + code[2] * G + j], sbooks[3 * 16 * G + code[3] * G + j], &nw, &nm,
+                           &nv, &skip);
+      if (!skip) {
+        w[j] = nw;
+        m[j] = nm;
+        var[j] = nv;
+      }
+    }
+  }
+}
+
+// One of the three outputs (0: W', 1: M', 2: V'), for the whole-tensor
+// usage pass, which needs one state only.
 template <int G>
 __device__ __forceinline__ void adamw_vector(const AdamwBatch& a, const float* __restrict__ sbooks,
                                              const AdamwCoefs& k, uint32_t e, uint64_t v, int valid, int state,
@@ -654,32 +822,30 @@ __global__ void __launch_bounds__(kThreads) k_adamw_sample(AdamwBatch a, const u
 
 // Entries a trial book (constant slot SLOT, book 0) selects over the
 // complete vectors of one updated state (the whole-tensor pass of
-// fit_codebook, vq.py:219-222).
+// fit_codebook, vq.py:219-222). One vector per thread.
 template <int G, int SLOT>
-__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage(AdamwBatch a, uint32_t expert, uint32_t state,
-                                                          uint32_t* __restrict__ out, uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage(AdamwBatch a, uint32_t expert,
+                                                                                 uint32_t state,
+                                                                                 uint32_t* __restrict__ out,
+                                                                                 uint32_t* __restrict__ status) {
   using Book = CBook<G, SLOT, 0>;
   __shared__ float sbooks[4 * 16 * G];
   __shared__ BookMeta meta;
   __shared__ uint32_t hist[16];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(expert) * 64 * G + i];
   if (threadIdx.x < 16) hist[threadIdx.x] = 0;
-  meta_setup<G, Book>(meta);
+  meta_load<SLOT, 0>(meta);
   const AdamwCoefs k = load_coefs(a.coefs + 7 * expert);
   const uint64_t full = a.n / G;
-  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-  // a whole warp iterates together so flag_warp stays convergent
-  for (uint64_t base = uint64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u); base < full; base += stride) {
-    const uint64_t v = base + (threadIdx.x & 31);
-    uint32_t bits = k.status;
-    if (v < full && !bits) {
-      float x[G];
-      adamw_vector<G>(a, sbooks, k, expert, v, G, int(state), x, &bits);
-      bool certified;
-      atomicAdd(&hist[enc_vector<G, Book>(x, meta, &certified)], 1u);
-    }
-    flag_warp(status, bits);
+  const uint64_t v = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  uint32_t bits = k.status;
+  if (v < full && !bits) {
+    float x[G];
+    adamw_vector<G>(a, sbooks, k, expert, v, G, int(state), x, &bits);
+    bool certified;
+    atomicAdd(&hist[enc_vector<G, Book>(x, meta, &certified)], 1u);
   }
+  flag_warp(status, bits);
   __syncthreads();
   if (threadIdx.x < 16 && hist[threadIdx.x]) atomicAdd(out + threadIdx.x, hist[threadIdx.x]);
 }
@@ -688,53 +854,62 @@ __global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage
 // (constant slot SLOT, books 0, 1, 2), one vector per thread, and a count of
 // weight values whose decoded value changed.
 template <int G, int SLOT>
-__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_encode(AdamwBatch a, uint32_t e, uint32_t* __restrict__ out_codes,
-                                                           uint32_t* __restrict__ changed,
-                                                           uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_encode(AdamwBatch a, uint32_t e,
+                                                                                  uint32_t* __restrict__ out_codes,
+                                                                                  uint32_t* __restrict__ changed,
+                                                                                  uint32_t* __restrict__ status) {
   using BW = CBook<G, SLOT, 0>;
   using BM = CBook<G, SLOT, 1>;
   using BV = CBook<G, SLOT, 2>;
   __shared__ float sbooks[4 * 16 * G];
   __shared__ BookMeta meta[3];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(e) * 64 * G + i];
-  meta_setup<G, BW>(meta[0]);
-  meta_setup<G, BM>(meta[1]);
-  meta_setup<G, BV>(meta[2]);
+  {
+    constexpr int kWords = sizeof(BookMeta) / 4;
+    if (threadIdx.x < 3 * kWords)
+      reinterpret_cast<uint32_t*>(meta)[threadIdx.x] = reinterpret_cast<const uint32_t*>(g_meta[SLOT])[threadIdx.x];
+  }
+  __syncthreads();
   const AdamwCoefs k = load_coefs(a.coefs + 7 * e);
   if (blockIdx.x == 0 && threadIdx.x == 0 && (meta[0].bad || meta[1].bad || meta[2].bad))
     atomicOr(status, kNonfinite);
   const uint64_t vectors = (uint64_t(a.n) + G - 1) / G;
   const uint32_t lane = threadIdx.x & 31;
-  const uint64_t warps = uint64_t(gridDim.x) * (blockDim.x / 32);
+  const uint64_t base = uint64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u);
+  const uint64_t v = base + lane;
   uint32_t changes = 0;
-  for (uint64_t base = (uint64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32) * 32; base < vectors;
-       base += warps * 32) {
-    const uint64_t v = base + lane;
-    uint32_t idx[3] = {0, 0, 0}, bits = k.status;
-    if (v < vectors && !bits) {
-      const int valid = int(min(uint64_t(G), uint64_t(a.n) - v * G));
+  uint32_t idx[3] = {0, 0, 0}, bits = k.status;
+  if (v < vectors && !bits) {
+    const int valid = int(min(uint64_t(G), uint64_t(a.n) - v * G));
+    bool certified;
+    if (G <= 16) {
+      // the AdamW arithmetic (two divisions and a square root per value) once
+      float w[G], m[G], var[G];
+      adamw_vector3<G>(a, sbooks, k, e, v, valid, w, m, var, &bits);
+      idx[0] = valid == G ? enc_vector<G, BW>(w, meta[0], &certified) : enc_exact<G, BW>(w, valid, 0xffffu);
+      idx[1] = valid == G ? enc_vector<G, BM>(m, meta[1], &certified) : enc_exact<G, BM>(m, valid, 0xffffu);
+      idx[2] = valid == G ? enc_vector<G, BV>(var, meta[2], &certified) : enc_exact<G, BV>(var, valid, 0xffffu);
+    } else {
+      // group 32: one state at a time keeps one vector of values live
       float x[G];
-      bool certified;
-      // one state at a time: the AdamW arithmetic is recomputed per state
-      // (cheap) so only one vector of values is live
       adamw_vector<G>(a, sbooks, k, e, v, valid, 0, x, &bits);
       idx[0] = valid == G ? enc_vector<G, BW>(x, meta[0], &certified) : enc_exact<G, BW>(x, valid, 0xffffu);
       adamw_vector<G>(a, sbooks, k, e, v, valid, 1, x, &bits);
       idx[1] = valid == G ? enc_vector<G, BM>(x, meta[1], &certified) : enc_exact<G, BM>(x, valid, 0xffffu);
       adamw_vector<G>(a, sbooks, k, e, v, valid, 2, x, &bits);
       idx[2] = valid == G ? enc_vector<G, BV>(x, meta[2], &certified) : enc_exact<G, BV>(x, valid, 0xffffu);
-      // vq.py:402: decoded new weight against decoded old weight, value by value
-      const uint32_t old = code_at(a.codes + uint64_t(e) * 4 * a.words, v);
-      for (int j = 0; j < valid; ++j) changes += BW::at(int(idx[0]), j) != sbooks[old * G + j];
     }
-#pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      const uint32_t word_bits = pack_nibbles(idx[s]);
-      const uint64_t word = (base >> 3) + (lane >> 3);
-      if ((lane & 7) == 0 && word < a.words) out_codes[(uint64_t(e) * 3 + s) * a.words + word] = word_bits;
-    }
-    flag_warp(status, bits);
+    // vq.py:402: decoded new weight against decoded old weight, value by value
+    const uint32_t old = code_at(a.codes + uint64_t(e) * 4 * a.words, v);
+    for (int j = 0; j < valid; ++j) changes += BW::at(int(idx[0]), j) != sbooks[old * G + j];
   }
+#pragma unroll
+  for (int s = 0; s < 3; ++s) {
+    const uint32_t word_bits = pack_nibbles(idx[s]);
+    const uint64_t word = (base >> 3) + (lane >> 3);
+    if ((lane & 7) == 0 && word < a.words) out_codes[(uint64_t(e) * 3 + s) * a.words + word] = word_bits;
+  }
+  flag_warp(status, bits);
   for (int o = 16; o; o >>= 1) changes += __shfl_xor_sync(0xffffffffu, changes, o);
   if (lane == 0 && changes) atomicAdd(changed + e, changes);
 }
@@ -854,11 +1029,12 @@ struct RunEncode {
                          cudaStream_t s) {
     const uint64_t vectors = (n + G - 1) / G;
     const int aligned = aligned16(x) ? 1 : 0;
-    const int per_sm = resident_per_sm(k_encode<G, 0>, 0);
-    const uint32_t grid = grid_for(vectors, per_sm);
+    const uint64_t grid = grid_for(vectors, resident_per_sm(k_encode<G, 0>, 0));
     BookSlot slot(s, book, 16 * G * sizeof(float));
     if (slot.error() != cudaSuccess) return slot.error();
-#define ACK_LAUNCH_ENCODE(S) k_encode<G, S><<<grid, kThreads, 0, s>>>(x, n, codes, status, aligned)
+#define ACK_LAUNCH_ENCODE(S)                                   \
+  k_book_meta<G, S, 1><<<1, 32, 0, s>>>();                     \
+  k_encode<G, S><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status, aligned)
     ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
 #undef ACK_LAUNCH_ENCODE
     const cudaError_t e = cudaGetLastError();
@@ -922,6 +1098,34 @@ cudaError_t launch_dense_mc(const float* X, const uint32_t* codes, const float* 
   return launch_dense_lut<G, MC, 32>(X, codes, books, Y, M, N, K, batch, words, status, s);
 }
 
+template <int G, int MC, int TC>
+cudaError_t launch_dense_t32(const float* X, const uint4* codes, const float* books, float* Y, uint32_t M,
+                             uint32_t N, uint32_t K, uint32_t batch, uint32_t* status, cudaStream_t s) {
+  const size_t smem = size_t(MC) * TC * 64;
+  cudaError_t err = cudaFuncSetAttribute(k_dense_t32<G, MC, TC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+  if (err != cudaSuccess) return err;
+  const uint64_t resident = uint64_t(sm_count()) * resident_per_sm(k_dense_t32<G, MC, TC>, smem);
+  const uint32_t ntiles = (N + 31) / 32;
+  const uint32_t warps = kThreads / 32;
+  const uint32_t nbatches = (ntiles + warps - 1) / warps;  // a batch: one tile per warp
+  const uint32_t per_item = balance_batches(nbatches, batch, resident);
+  const uint32_t items = (nbatches + per_item - 1) / per_item;
+  const uint64_t units = tile32_bytes(N, K, G) / 16;
+  k_dense_t32<G, MC, TC><<<uint32_t(uint64_t(items) * batch), kThreads, smem, s>>>(
+      X, codes, books, Y, M, N, K, items, per_item * warps, units, status);
+  return cudaGetLastError();
+}
+
+template <int G, int MC>
+cudaError_t launch_t32_mc(const float* X, const uint4* codes, const float* books, float* Y, uint32_t M, uint32_t N,
+                          uint32_t K, uint32_t batch, uint32_t* status, cudaStream_t s) {
+  const uint32_t T = K / G;
+  if (T % 256 == 0 && MC <= 2) return launch_dense_t32<G, MC, (MC <= 2 ? 256 : 128)>(X, codes, books, Y, M, N, K, batch, status, s);
+  if (T % 128 == 0) return launch_dense_t32<G, MC, 128>(X, codes, books, Y, M, N, K, batch, status, s);
+  return launch_dense_t32<G, MC, 32>(X, codes, books, Y, M, N, K, batch, status, s);
+}
+
 template <int G>
 struct RunDense {
   static cudaError_t run(const Plan& p, void* const* ptr, cudaStream_t s) {
@@ -933,6 +1137,14 @@ struct RunDense {
     const uint32_t M = uint32_t(p.m), N = uint32_t(p.n), K = uint32_t(p.k);
     const uint64_t words = packed_words(uint64_t(N) * K, G);
     const bool nt = (p.flags & 2u) != 0;
+    if (p.flags & 4u) {
+      if (!aligned16(codes)) return cudaErrorMisalignedAddress;
+      const uint4* c4 = reinterpret_cast<const uint4*>(codes);
+      if (M == 1) return launch_t32_mc<G, 1>(X, c4, books, Y, M, N, K, p.batch, status, s);
+      if (M == 2) return launch_t32_mc<G, 2>(X, c4, books, Y, M, N, K, p.batch, status, s);
+      if (M <= 4) return launch_t32_mc<G, 4>(X, c4, books, Y, M, N, K, p.batch, status, s);
+      return launch_t32_mc<G, 8>(X, c4, books, Y, M, N, K, p.batch, status, s);
+    }
     if (nt && K % G == 0 && (K / G) % 32 == 0 && aligned16(codes) && (words * 4) % 16 == 0) {
       if (M == 1) return launch_dense_mc<G, 1>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
       if (M == 2) return launch_dense_mc<G, 2>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
@@ -991,11 +1203,13 @@ struct RunAdamwFused {
     if (p.op == Op::AdamwUsage) {
       cudaError_t err = cudaMemsetAsync(ptr[5], 0, 16 * sizeof(uint32_t), s);
       if (err != cudaSuccess) return err;
-      const uint32_t grid = grid_for(p.m / G, resident_per_sm(k_adamw_usage<G, 0>, 0));
+      const uint32_t grid = uint32_t((p.m / G + kThreads - 1) / kThreads);
       BookSlot slot(s, ptr[3], 16 * G * sizeof(float));
       if (slot.error() != cudaSuccess) return slot.error();
       uint32_t* out = static_cast<uint32_t*>(ptr[5]);
-#define ACK_LAUNCH_USAGE(S) k_adamw_usage<G, S><<<grid, kThreads, 0, s>>>(a, p.aux1, p.aux0, out, status)
+#define ACK_LAUNCH_USAGE(S)                  \
+  k_book_meta<G, S, 1><<<1, 32, 0, s>>>();   \
+  k_adamw_usage<G, S><<<grid, kThreads, 0, s>>>(a, p.aux1, p.aux0, out, status)
       ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_USAGE)
 #undef ACK_LAUNCH_USAGE
       const cudaError_t e = cudaGetLastError();
@@ -1004,14 +1218,16 @@ struct RunAdamwFused {
     }
     cudaError_t err = cudaMemsetAsync(ptr[6], 0, size_t(p.batch) * sizeof(uint32_t), s);
     if (err != cudaSuccess) return err;
-    const uint32_t grid = grid_for(vectors, resident_per_sm(k_adamw_encode<G, 0>, 0));
+    const uint32_t grid = uint32_t((vectors + kThreads - 1) / kThreads);
     const float* new_books = static_cast<const float*>(ptr[3]);
     uint32_t* out = static_cast<uint32_t*>(ptr[5]);
     uint32_t* changed = static_cast<uint32_t*>(ptr[6]);
     for (uint32_t e = 0; e < p.batch; ++e) {
       BookSlot slot(s, new_books + uint64_t(e) * 3 * 16 * G, 3 * 16 * G * sizeof(float));
       if (slot.error() != cudaSuccess) return slot.error();
-#define ACK_LAUNCH_ADAMW(S) k_adamw_encode<G, S><<<grid, kThreads, 0, s>>>(a, e, out, changed, status)
+#define ACK_LAUNCH_ADAMW(S)                  \
+  k_book_meta<G, S, 3><<<1, 32, 0, s>>>();   \
+  k_adamw_encode<G, S><<<grid, kThreads, 0, s>>>(a, e, out, changed, status)
       ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ADAMW)
 #undef ACK_LAUNCH_ADAMW
       const cudaError_t le = cudaGetLastError();
@@ -1059,6 +1275,15 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
     case Op::DecodeLarge:
       return by_group<RunDecode>(g, static_cast<const uint32_t*>(ptr[0]), static_cast<const float*>(ptr[1]),
                                  static_cast<float*>(ptr[5]), p.m, static_cast<uint32_t*>(ptr[7]), s);
+    case Op::RepackTile32: {
+      if (!aligned16(ptr[0]) || !aligned16(ptr[5])) return cudaErrorMisalignedAddress;
+      const uint32_t T = uint32_t(p.k / g);
+      const uint64_t src_units = packed_bytes(p.m * p.k, g) / 16, dst_units = tile32_bytes(p.m, p.k, g) / 16;
+      k_repack_tile32<<<grid_for(dst_units * p.batch), kThreads, 0, s>>>(
+          static_cast<const uint4*>(ptr[0]), static_cast<uint4*>(ptr[5]), uint32_t(p.m), T, src_units, dst_units,
+          p.batch);
+      return cudaGetLastError();
+    }
     default:
       return cudaErrorInvalidValue;
   }
@@ -1066,7 +1291,7 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
 
 const char* kernel_manifest() {
   return "vq4-b200/2 sm_100a: k_decode k_decode_scalar k_encode(constant-bank books) k_matmul_exact k_adamw "
-         "k_dense_lut(byte-permute lookups) k_coded_lut k_gemm_generic k_adamw_sample k_adamw_usage k_adamw_encode";
+         "k_dense_lut(byte-permute lookups) k_dense_t32 k_repack_tile32 k_coded_lut k_gemm_generic k_adamw_sample k_adamw_usage k_adamw_encode";
 }
 
 }  // namespace ack

@@ -92,7 +92,7 @@ constexpr uint32_t kMaxSamples = 65536;         // fit_codebook's sample bound (
 PlanError parse_schema2(Plan* p) {
   const auto& w = p->words;
   uint32_t op = w[0], group = w[4], entries = w[5], flags = w[6], reserved = w[7];
-  if (op < 16 || op > 22) return PlanError::Operation;
+  if (op < 16 || op > 23) return PlanError::Operation;
   if (!valid_group(group)) return PlanError::Group;
   if (entries != kEntries) return PlanError::Entries;
   if (reserved != 0 || w[12] || w[13] || w[14] || w[15]) return PlanError::Reserved;
@@ -111,15 +111,29 @@ PlanError parse_schema2(Plan* p) {
   switch (p->op) {
     case Op::Dense: {
       // flag bit 1: W stored N x K (groups along K); clear: W stored K x N.
-      if (flags & ~2u) return PlanError::Flags;
+      // flag bit 2: W is in the tile32 layout (needs bit 1, K % G == 0 and
+      // (K / G) % 32 == 0).
+      if (flags & ~6u) return PlanError::Flags;
+      if ((flags & 4u) && (!(flags & 2u) || p->k % group || (p->k / group) % 32)) return PlanError::Flags;
       if (p->aux0 || p->aux1 || p->aux2) return PlanError::Aux;
       if (!p->m || !p->n || !p->k) return PlanError::Geometry;
       if (!E) return PlanError::Batch;
       if (p->m > kMaxDim2 || p->n > kMaxDim2 || p->k > kMaxDim2) return PlanError::Geometry;
       if (p->m * p->k > kMaxOperand2 || p->n * p->k > kMaxOperand2 || p->m * p->n > kMaxOperand2)
         return PlanError::AddressLimit;
-      uint64_t wb = packed_bytes(p->n * p->k, group);
+      uint64_t wb = (flags & 4u) ? tile32_bytes(p->n, p->k, group) : packed_bytes(p->n * p->k, group);
       p->required = {E * p->m * p->k * 4, E * wb, E * book, 0, 0, E * p->m * p->n * 4, 0, 4};
+      break;
+    }
+    case Op::RepackTile32: {
+      // canonical N x K image (m = N, k = K) -> tile32 layout, batch of E
+      if (flags) return PlanError::Flags;
+      if (p->aux0 || p->aux1 || p->aux2) return PlanError::Aux;
+      if (!p->m || p->n != 1 || !p->k) return PlanError::Geometry;
+      if (p->k % group || (p->k / group) % 32) return PlanError::Geometry;
+      if (!E) return PlanError::Batch;
+      if (p->m > kMaxDim2 || p->k > kMaxDim2) return PlanError::Geometry;
+      p->required = {E * packed_bytes(p->m * p->k, group), 0, 0, 0, 0, E * tile32_bytes(p->m, p->k, group), 0, 4};
       break;
     }
     case Op::Coded: {

@@ -21,7 +21,7 @@ constexpr int kSlots = 8;                        // schema 2; schema 1 uses the 
 enum class Op : uint32_t {
   Encode = 0, Decode = 1, Matmul = 2, AdamW = 3,
   Dense = 16, Coded = 17, AdamwSample = 18, AdamwUsage = 19, AdamwEncode = 20,
-  EncodeLarge = 21, DecodeLarge = 22,
+  EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23,
 };
 
 // Refusals. The schema-1 names are vq4_ops.rs:66-84; the schema-2 ones are
@@ -57,6 +57,15 @@ inline uint64_t packed_bytes(uint64_t values, uint32_t group) {
   return ((values + group - 1) / group + 7) / 8 * 4;
 }
 inline uint64_t packed_words(uint64_t values, uint32_t group) { return packed_bytes(values, group) / 4; }
+
+// The tile32 layout of a coded N x K matrix (vectors along K, T = K/G a
+// multiple of 32): rows grouped in tiles of 32 (the last tile padded with
+// zero codes); within a tile, 16-byte chunk c (32 groups) of row r sits at
+// ((tile * T/32 + c) * 32 + r % 32) * 16 bytes, so a warp reads chunk c of its
+// 32 rows as one contiguous 512-byte line.
+inline uint64_t tile32_bytes(uint64_t rows, uint64_t cols, uint32_t group) {
+  return (rows + 31) / 32 * 32 * (cols / group) / 2;
+}
 
 // Parse a plan block (32 bytes: schema 1, 64 bytes: schema 2). `slot` receives
 // the offending slot for Capacity.

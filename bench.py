@@ -210,9 +210,15 @@ def run_cfg2(args, world, rank, local):
     codes, books, x, book = make_cfg2(torch, cuda, vq, experts, m, device)
     y = torch.empty((experts, m, N_ROWS), dtype=torch.float32, device=device)
     status = cuda.status_word(device)
+    layout = args.layout
+    if layout == "tile32":
+        # resident weights are repacked once into the tile32 layout (outside the timed region)
+        codes_canonical = codes
+        codes, status = cuda.repack_tile32(codes_canonical, N_ROWS, K_COLS, GROUP, status=status)
+        cuda.check(status)
 
     def step():
-        cuda.dense(x, codes, books, N_ROWS, GROUP, out=y, status=status)
+        cuda.dense(x, codes, books, N_ROWS, GROUP, layout=layout, out=y, status=status)
 
     for _ in range(args.warmup):
         step()
@@ -246,7 +252,8 @@ def run_cfg2(args, world, rank, local):
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
     achieved = algorithmic / (ms_step / 1e3) / 1e9
-    traffic_name = f"dense_lut_cfg2_m{m}"
+    kernel = "k_dense_t32" if layout == "tile32" else "k_dense_lut"
+    traffic_name = f"{kernel}_cfg2_m{m}"
     traffic = profile_traffic(traffic_name)
     result = {
         "metric": f"vq4 packed GEMV coded-weight GB/s (cfg2 W 11008x4096 g16, M={m}, grouped)",
@@ -256,21 +263,23 @@ def run_cfg2(args, world, rank, local):
         "config": {"workload": f"cfg2-grouped-gemv-m{m}", "experts_per_gpu": experts, "M": m, "N": N_ROWS,
                    "K": K_COLS, "group": GROUP, "coded_bytes_per_gpu_step": coded,
                    "l2": "inputs larger than L2 (codes of all experts exceed 126 MB per launch)",
+                   "weight_layout": layout,
                    "parallelism": f"expert-sharded x{world}, no collective"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak if peak else 6650.0, "unit": "GB/s",
                      "frac": round(achieved / (peak if peak else 6650.0), 4),
                      "traffic": traffic, "peak_source": "measured" if peak else "fallback",
-                     "kernel": "k_dense_lut", "algorithmic_bytes_per_launch": algorithmic},
+                     "kernel": kernel, "algorithmic_bytes_per_launch": algorithmic},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
+    canonical = codes_canonical if layout == "tile32" else codes
     if rank == 0 and not args.no_e2e:
-        result["e2e"] = run_cfg2_e2e(args, torch, vq, codes, books, x, book, local)
+        result["e2e"] = run_cfg2_e2e(args, torch, vq, canonical, books, x, book, local)
     if rank == 0 and not args.no_cpu:
         sample = min(experts, 8)
         gbs, done, threads, elapsed = cpu_dense_sample(
-            codes[:sample].cpu().numpy().view(np.uint32), books[:sample].cpu().numpy(), x[:sample].cpu().numpy(),
+            canonical[:sample].cpu().numpy().view(np.uint32), books[:sample].cpu().numpy(), x[:sample].cpu().numpy(),
             args.cpu_budget)
         result["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                   "sample": f"{done} experts of the workload (decode + dot, float64 sums), "
@@ -554,6 +563,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--group", type=int, default=16)
+    ap.add_argument("--layout", choices=("tile32", "canonical"), default="tile32")
     ap.add_argument("--values", type=int, default=1 << 30)
     ap.add_argument("--dist", choices=("gauss", "heavy"), default="gauss")
     ap.add_argument("--experts-cfg4", type=int, default=8)

@@ -98,3 +98,25 @@ def test_concurrent_encodes_with_different_books_on_many_streams():
     for (x, book), (codes, status, _, _) in zip(jobs, outs):
         cuda.check(status)
         np.testing.assert_array_equal(u32(codes), oc.encode(x, book, group))
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_tile32_layout_is_bitwise_the_canonical_product(group):
+    rng = np.random.default_rng(group + 3)
+    for (e, m, n, k) in ((3, 1, 1000, 32 * group), (2, 3, 517, 256 * group), (2, 8, 64, 128 * group),
+                         (1, 16, 333, 32 * group)):
+        codes = np.stack([o.pack(rng.integers(0, 16, n * k // group)) for _ in range(e)])
+        books = rng.standard_normal((e, 16, group)).astype(np.float32)
+        x = rng.standard_normal((e, m, k)).astype(np.float32)
+        tc = torch.from_numpy(codes.view(np.int32)).cuda()
+        tb = torch.from_numpy(books).cuda()
+        tx = torch.from_numpy(x).cuda()
+        packed, status = cuda.repack_tile32(tc, n, k, group)
+        y_t32, _ = cuda.dense(tx, packed, tb, n, group, layout="tile32", status=status)
+        y_can, _ = cuda.dense(tx, tc, tb, n, group, status=status)
+        cuda.check(status)
+        np.testing.assert_array_equal(y_t32.cpu().numpy().view(np.uint32), y_can.cpu().numpy().view(np.uint32))
+        wd = o.decode(codes[0], books[0], n * k, group).reshape(n, k).astype(np.float64)
+        y64 = x[0].astype(np.float64) @ wd.T
+        err = np.max(np.abs(y_t32[0].cpu().numpy() - y64) / (np.abs(x[0]).astype(np.float64) @ np.abs(wd).T))
+        assert err <= 1e-5

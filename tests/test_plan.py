@@ -216,3 +216,15 @@ def test_schema2_outputs_must_not_alias_and_unused_slots_may_be_null():
     bad = list(ids)
     bad[3] = 0
     assert validate_buffers(words, caps, bad) == SHAPE and last_error().endswith("vq2-null-allocation-identity")
+
+
+def test_schema2_tile32_repack_and_prepacked_dense():
+    n, k, g, e = 1000, 4096, 16, 3
+    tile32 = (n + 31) // 32 * 32 * (k // g) // 2
+    assert required(plan2(23, n, 1, k, g, batch=e)) == [e * n * k // g // 2, 0, 0, 0, 0, e * tile32, 0, 4]
+    assert required(plan2(16, 1, n, k, g, flags=6, batch=e))[1] == e * tile32
+    for words, name in ((plan2(16, 1, n, k, g, flags=4), "vq2-unsupported-flags"),
+                        (plan2(16, 1, n, 40 * g, g, flags=6), "vq2-unsupported-flags"),
+                        (plan2(23, n, 1, 40 * g, g), "vq2-invalid-geometry"),
+                        (plan2(23, n, 2, k, g), "vq2-invalid-geometry")):
+        assert refusal(words)[1].endswith(name), words
