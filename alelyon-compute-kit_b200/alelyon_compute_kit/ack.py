@@ -235,6 +235,8 @@ class _Lib:
         c.ack_vq_plan_validate_dispatch.argtypes = [vp, sz, ctypes.POINTER(ctypes.c_uint32)]
         c.ack_inject_fault.restype = ctypes.c_int32
         c.ack_inject_fault.argtypes = [vp, ctypes.c_int32, ctypes.c_int32]
+        c.ack_kernel_manifest.restype = ctypes.c_int32
+        c.ack_kernel_manifest.argtypes = [ctypes.c_char_p, sz, ctypes.POINTER(sz)]
 
     def last_error(self) -> str:
         buf = ctypes.create_string_buffer(1024)
@@ -289,6 +291,20 @@ def abi_info() -> AckAbiInfo:
     """The loaded library's ABI description."""
     lib = _lib()
     return lib.info if lib.info is not None else lib.handshake()
+
+
+def kernel_manifest() -> dict:
+    """The library's kernel manifest: sha256 of each source it was built
+    from, the kernels each defines, nvcc release and flags, arch."""
+    import json
+    lib = _lib()
+    need = ctypes.c_size_t()
+    lib.cdll.ack_kernel_manifest(None, 0, ctypes.byref(need))
+    buf = ctypes.create_string_buffer(need.value)
+    rc = lib.cdll.ack_kernel_manifest(buf, need.value, None)
+    if rc != ACK_OK:
+        raise AckError(f"ack_kernel_manifest refused ({rc}): {lib.last_error()}")
+    return json.loads(buf.value.decode())
 
 
 def dispatch_stats_available() -> bool:

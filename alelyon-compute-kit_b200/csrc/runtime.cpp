@@ -203,10 +203,10 @@ uint64_t fnv1a(const void* data, size_t len, uint64_t h = 0xcbf29ce484222325ull)
   return h;
 }
 
-uint64_t shader_identity() {
-  const char* m = ack::kernel_manifest();
-  return fnv1a(m, strlen(m));
-}
+#include "manifest.inc"
+
+// FNV-1a over the embedded kernel manifest (sources' sha256, compiler, flags).
+uint64_t shader_identity() { return fnv1a(kManifestJson, sizeof(kManifestJson) - 1); }
 
 constexpr const char* kVersion = "alelyon-compute-kit-b200 0.1.0";
 
@@ -580,6 +580,18 @@ ACK_EXPORT int32_t ack_inject_fault(const AckDevice* handle, int32_t kind, int32
 // ------------------------------------------------------------ vq4 entries --
 
 ACK_EXPORT uint32_t ack_vq_schema(void) { return ACK_VQ_SCHEMA; }
+
+ACK_EXPORT int32_t ack_kernel_manifest(char* out, size_t len, size_t* needed) {
+  const size_t n = sizeof(kManifestJson);
+  if (needed) *needed = n;
+  if (!out) return needed ? ACK_OK : ACK_ERR_NULL;
+  if (len < n) {
+    set_error(format("kernel manifest needs %zu bytes, %zu given", n, len));
+    return ACK_ERR_SIZE;
+  }
+  memcpy(out, kManifestJson, n);
+  return ACK_OK;
+}
 ACK_EXPORT uint32_t ack_vq2_schema(void) { return ACK_VQ2_SCHEMA; }
 
 namespace {

@@ -1289,9 +1289,4 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
   }
 }
 
-const char* kernel_manifest() {
-  return "vq4-b200/2 sm_100a: k_decode k_decode_scalar k_encode(constant-bank books) k_matmul_exact k_adamw "
-         "k_dense_lut(byte-permute lookups) k_dense_t32 k_repack_tile32 k_coded_lut k_gemm_generic k_adamw_sample k_adamw_usage k_adamw_encode";
-}
-
 }  // namespace ack

@@ -12,7 +12,4 @@ namespace ack {
 // have passed admission; pointers are device addresses in slot order.
 cudaError_t launch(const Plan& plan, void* const* ptr, cudaStream_t stream);
 
-// Identity string of the compiled kernel set (hashed into AckAbiInfo.shaders).
-const char* kernel_manifest();
-
 }  // namespace ack

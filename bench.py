@@ -53,9 +53,9 @@ def measured_peaks() -> dict:
 
 
 def profile_traffic(name: str):
-    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<name>.md,
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<name>.txt,
     a line `traffic_bytes_per_launch: <int>`), or None."""
-    path = ROOT / "profiles" / f"{name}.md"
+    path = ROOT / "profiles" / f"{name}.txt"
     try:
         for line in path.read_text().splitlines():
             if line.strip().startswith("traffic_bytes_per_launch:"):

@@ -188,13 +188,39 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
 #define ACK_VQ2_ADAMW_ENCODE 20u /* decode -> AdamW -> encode W', M', V' in one pass */
 #define ACK_VQ2_ENCODE 21u       /* encode with a 64-bit value count */
 #define ACK_VQ2_DECODE 22u       /* decode with a 64-bit value count */
+#define ACK_VQ2_REPACK_TILE32 23u /* canonical N x K images -> the tile32 layout op 16 reads */
+
+/* Flags of ACK_VQ2_DENSE: bit 1 = W stored N x K (vectors along K); bit 2 =
+ * W given in the tile32 layout (requires bit 1 and (K / group) % 32 == 0):
+ * rows in tiles of 32, the last padded with zero codes; 16-byte chunk c of
+ * row r at byte ((r / 32) * (K / group / 32) + c) * 512 + (r % 32) * 16. */
+#define ACK_VQ2_DENSE_NT 2u
+#define ACK_VQ2_DENSE_TILE32 4u
 
 uint32_t ack_vq2_schema(void);
+
+/* The kernel manifest, the CUDA counterpart of the reference's vq4 entry in
+ * K/kernels/MANIFEST.json:2137-2144: a NUL-terminated JSON object with the
+ * sha256 of every library source, the kernels each defines, the nvcc
+ * release and flags and the arch (sm_100a). `*needed` receives the size
+ * including the NUL; `out` may be null to ask for it. ACK_ERR_SIZE if `len`
+ * is short. AckAbiInfo.shaders is the FNV-1a hash of the same text. */
+int32_t ack_kernel_manifest(char *out, size_t len, size_t *needed);
 /* `plan` is 16 little-endian u32 [op, m, n, k, group, 16, flags, 0, batch,
  * aux0, aux1, aux2, 0, 0, 0, 0]; `slots` is ACK_VQ2_SLOTS buffer handles
  * [in0, in1, in2, in3, in4, out0, out1, status]; a slot the operation does
- * not use may be null. Slot meanings per operation are listed in
- * INTEGRATION.md; refusals are named "vq2-..." and carry the schema-1 codes. */
+ * not use may be null; refusals are named "vq2-..." and carry the schema-1
+ * codes. Slots per operation (in0, in1, in2, in3 -> out0, out1):
+ *   16 dense      X (batch x M x K f32), W codes (batch x words), W books
+ *                 (batch x 16 x g) -> Y (batch x M x N)
+ *   17 coded      A codes, A book, B codes, B book -> C (M x N)
+ *   18 sample     W/M/V/G images per expert, their 4 books, 7 coefficients,
+ *                 aux0 = S sample vector positions -> (batch x 3 x S x g) f32
+ *   19 usage      as 18, trial book; aux0 = state, aux1 = expert -> 16 u32
+ *   20 encode     as 18, new books (batch x 3 x 16 x g) -> codes
+ *                 (batch x 3 x words), changed (batch u32)
+ *   21/22         values or codes, book -> codes or values
+ *   23 repack     canonical codes (batch x words) -> tile32 codes */
 int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslots,
                 const uint8_t *plan, size_t plan_len);
 
@@ -204,7 +230,8 @@ int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslo
  * their byte capacities, work enqueued on the caller's CUDA stream `stream`
  * (a cudaStream_t; null = the legacy default stream) on the current device.
  * A 32-byte plan uses slots [b0, b1, b2, b3, out, status]; a 64-byte plan the
- * ack_vq2 slots. Every non-null pointer must be 16-byte aligned. */
+ * ack_vq2 slots. Every non-null pointer must be 4-byte aligned; the
+ * 128-bit kernels (tile32 codes) also want 16-byte alignment. */
 typedef struct AckVqOperands {
     uint32_t size;      /* sizeof(AckVqOperands) */
     uint32_t nslots;    /* 6 for a schema-1 plan, 8 for a schema-2 plan */

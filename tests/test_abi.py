@@ -45,6 +45,34 @@ def test_struct_layouts_are_the_references():
     assert info.operators == 0  # no dense operator family is claimed
 
 
+def test_kernel_manifest_names_the_sources_the_library_was_built_from():
+    """The CUDA counterpart of the reference's MANIFEST.json vq4 entry: every
+    source's sha256 must be that of the file in this tree (a stale build
+    fails here), and AckAbiInfo.shaders hashes the same text."""
+    import hashlib
+    m = ack.kernel_manifest()
+    assert m["arch"] == "sm_100a" and m["format"] == "vq4/v1"
+    assert "compute_100a" in m["flags"] and "release 12" in m["compiler"]
+    pkg = ROOT / "alelyon-compute-kit_b200"
+    for name, entry in m["sources"].items():
+        path = next(p for p in [pkg / "csrc" / name, ROOT / "include" / name] if p.exists())
+        assert entry["source_sha256"] == hashlib.sha256(path.read_bytes()).hexdigest(), name
+    kernels = set(m["sources"]["vq_kernels.cu"]["kernels"])
+    assert {"k_decode", "k_encode", "k_dense_t32", "k_coded_lut", "k_adamw_encode"} <= kernels
+    c = lib().cdll
+    need = ctypes.c_size_t()
+    assert c.ack_kernel_manifest(None, 0, ctypes.byref(need)) == ack.ACK_OK
+    short = ctypes.create_string_buffer(8)
+    assert c.ack_kernel_manifest(short, 8, None) == ack.ACK_ERR_SIZE
+    assert c.ack_kernel_manifest(None, 0, None) == ack.ACK_ERR_NULL
+    buf = ctypes.create_string_buffer(need.value)
+    assert c.ack_kernel_manifest(buf, need.value, None) == ack.ACK_OK
+    h = 0xcbf29ce484222325
+    for byte in buf.value:
+        h = ((h ^ byte) * 0x100000001b3) & (2 ** 64 - 1)
+    assert ack.abi_info().shaders == h
+
+
 def test_optional_extension_does_not_relabel_existing_abi_layout():  # vq4_abi.rs:30
     c = lib().cdll
     assert c.ack_vq_schema() == 1
