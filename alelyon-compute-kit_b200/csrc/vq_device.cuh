@@ -30,32 +30,52 @@ __device__ __forceinline__ void flag_warp(uint32_t* status, uint32_t bits) {
 }
 
 // Codebooks of in-flight encode launches live in the constant bank. The
-// launcher copies the caller's book into one of kBookSlots slots on the
-// launch stream (stream-ordered, device to device) and picks the kernel
-// instance compiled for that slot, so every book value the 16 x G filter
-// multiplies by is a compile-time constant-bank operand: a warp-wide
-// broadcast from the constant cache, with no shared-memory traffic. A slot
-// holds up to three books of group 32 (the fused AdamW pass re-encodes W, M
-// and V with three books).
+// launcher stages the caller's book into one of kBookSlots slots on the
+// launch stream and picks the kernel instance compiled for that slot, so
+// every book value the 16 x G filter multiplies by is a compile-time
+// constant-bank operand: a warp-wide broadcast from the constant cache, with
+// no shared-memory traffic. A slot holds up to three books of group 32 (the
+// fused AdamW pass re-encodes W, M and V with three books) and, after them,
+// each book's BookMeta.
+//
+// Within a slot a book is stored pair-interleaved: value j of entry e at
+// float ((e / 2) * G + j) * 2 + e % 2, so the 16-byte quad (p, h) holds
+// (c_2p[2h], c_2p+1[2h], c_2p[2h+1], c_2p+1[2h+1]): two entry pairs that one
+// packed two-lane FMA each consumes.
 constexpr int kBookSlots = 8;
-constexpr int kSlotFloats = 3 * 16 * 32;
+constexpr int kSlotBookFloats = 3 * 16 * 32;
+constexpr int kMetaFloats = 32;  // one BookMeta (19 words used), per book
+constexpr int kSlotFloats = kSlotBookFloats + 3 * kMetaFloats;
 __constant__ float4 c_books[kBookSlots][kSlotFloats / 4];
 
-// Book B (0..2) of slot SLOT, row-major 16 x G, read in 16-byte quads: one
-// constant-bank load feeds four FMAs (scalar constant loads with computed
-// offsets would saturate the address-divergence unit instead).
+template <int G>
+__host__ __device__ constexpr int book_pos(int e, int j) { return ((e >> 1) * G + j) * 2 + (e & 1); }
+
+// Book B (0..2) of slot SLOT and its BookMeta, which the staging kernel
+// stores after the books (float kSlotBookFloats + B * kMetaFloats).
 template <int G, int SLOT, int B>
 struct CBook {
-  // components 4q..4q+3 of entry e
-  static __device__ __forceinline__ float4 quad(int e, int q) { return c_books[SLOT][(B * 16 * G + e * G) / 4 + q]; }
+  // entries 2p, 2p+1 at components 2h, 2h+1
+  static __device__ __forceinline__ float4 quad(int p, int h) { return c_books[SLOT][(B * 16 * G + p * 2 * G) / 4 + h]; }
   static __device__ __forceinline__ float at(int e, int j) {
-    const float4 t = quad(e, j >> 2);
-    const int r = j & 3;
-    return r == 0 ? t.x : (r == 1 ? t.y : (r == 2 ? t.z : t.w));
+    return reinterpret_cast<const float*>(c_books[SLOT])[B * 16 * G + book_pos<G>(e, j)];
   }
+  // quad i of the BookMeta (compile-time i: an immediate constant operand)
+  static __device__ __forceinline__ float4 metaq(int i) {
+    return c_books[SLOT][(kSlotBookFloats + B * kMetaFloats) / 4 + i];
+  }
+  // (q_2p, q_2p+1)
+  static __device__ __forceinline__ float2 qpair(int p) {
+    const float4 t = metaq(p >> 1);
+    return (p & 1) ? make_float2(t.z, t.w) : make_float2(t.x, t.y);
+  }
+  static __device__ __forceinline__ float cmax2() { return metaq(4).x; }
+  static __device__ __forceinline__ uint32_t uniq() { return __float_as_uint(metaq(4).y); }
+  static __device__ __forceinline__ bool bad() { return __float_as_uint(metaq(4).z) != 0; }
 };
 
-// Facts about a codebook the search needs, computed once per block:
+// Facts about a codebook the search needs, computed once per launch by the
+// staging kernel and stored in the slot beside the book:
 //   q      fl32(||c_e||^2), the square norm summed in float64 then rounded
 //   cmax2  max_e ||c_e||^2 rounded up
 //   uniq   bit e set when row e differs from every lower row; a duplicate
@@ -67,52 +87,37 @@ struct alignas(16) BookMeta {
   uint32_t uniq;
   uint32_t bad;
 };
+static_assert(sizeof(BookMeta) <= kMetaFloats * 4, "BookMeta fits its slot region");
 
-// The BookMeta of each slot's books, written once per launch by
-// k_book_meta right after the slot is filled (stream-ordered before the
-// kernels that read it).
-__device__ BookMeta g_meta[kBookSlots][3];
-
-// Compute `m` with the first warp of the block (the other threads return
-// at once); no barrier.
-template <int G, class Book>
-__device__ void meta_compute(BookMeta& m) {
-  if (threadIdx.x < 32) {
-    const int e = threadIdx.x & 15;
-    double s = 0.0;
-    bool bad = false;
-    for (int j = 0; j < G; ++j) {
-      const float c = Book::at(e, j);
-      bad |= !finite32(c);
-      s = __dadd_rn(s, __dmul_rn(double(c), double(c)));
-    }
-    bool uniq = true;
-    for (int f = 0; f < e; ++f) {
-      bool same = true;
-      for (int j = 0; j < G; ++j) same &= Book::at(f, j) == Book::at(e, j);
-      if (same) uniq = false;
-    }
-    float up = __double2float_ru(s);
-    for (int o = 8; o; o >>= 1) up = fmaxf(up, __shfl_xor_sync(0xffffffffu, up, o));
-    const uint32_t u = __ballot_sync(0xffffffffu, uniq) & 0xffffu;
-    const uint32_t b = __ballot_sync(0xffffffffu, bad) & 0xffffu;
-    if (threadIdx.x < 16) m.q[e] = __double2float_rn(s);
-    if (threadIdx.x == 0) {
-      m.cmax2 = up;
-      m.uniq = u;
-      m.bad = b != 0;
-    }
+// Compute `m` for the row-major 16 x G book `book` with one warp (lanes
+// 0..31 must all call it); no barrier.
+template <int G>
+__device__ void meta_compute(const float* __restrict__ book, BookMeta& m) {
+  const int lane = threadIdx.x & 31;
+  const int e = lane & 15;
+  double s = 0.0;
+  bool bad = false;
+  for (int j = 0; j < G; ++j) {
+    const float c = book[e * G + j];
+    bad |= !finite32(c);
+    s = __dadd_rn(s, __dmul_rn(double(c), double(c)));
   }
-}
-
-// Copy slot SLOT's meta of book B into shared memory; all threads call it,
-// it ends with a barrier.
-template <int SLOT, int B>
-__device__ __forceinline__ void meta_load(BookMeta& m) {
-  constexpr int kWords = sizeof(BookMeta) / 4;
-  if (threadIdx.x < kWords)
-    reinterpret_cast<uint32_t*>(&m)[threadIdx.x] = reinterpret_cast<const uint32_t*>(&g_meta[SLOT][B])[threadIdx.x];
-  __syncthreads();
+  bool uniq = true;
+  for (int f = 0; f < e; ++f) {
+    bool same = true;
+    for (int j = 0; j < G; ++j) same &= book[f * G + j] == book[e * G + j];
+    if (same) uniq = false;
+  }
+  float up = __double2float_ru(s);
+  for (int o = 8; o; o >>= 1) up = fmaxf(up, __shfl_xor_sync(0xffffffffu, up, o));
+  const uint32_t u = __ballot_sync(0xffffffffu, uniq) & 0xffffu;
+  const uint32_t b = __ballot_sync(0xffffffffu, bad) & 0xffffu;
+  if (lane < 16) m.q[e] = __double2float_rn(s);
+  if (lane == 0) {
+    m.cmax2 = up;
+    m.uniq = u;
+    m.bad = b != 0;
+  }
 }
 
 // Exact nearest entry among the set bits of `cand`, computed the way the
@@ -157,62 +162,71 @@ __device__ __noinline__ uint32_t enc_exact_mem(const float* x, int valid, uint32
 // Certified nearest entry of one complete vector.
 //
 // Filter: f_e = ||c_e||^2 - 2 x.c_e in FP32 (16 fused multiply-adds per
-// component, the book values constant-bank operands). |f_e - G_e| <= eps
+// component as 8 two-lane packed FMAs, the book values constant-bank
+// operands; ||x||^2 as two interleaved partial sums). |f_e - G_e| <= eps
 // with G_e the exact value of the same expression and
 // eps = (G + 8) 2^-23 (||x||^2 + max ||c||^2): twice the forward-error bound
 // of the FMA chain, the rounded norms and the final FMA, plus an absolute
-// floor for subnormal products. Any entry whose f_e lies within 2 eps of the
-// minimum could be the float64 winner (the float64 distances differ from the
-// exact ones by far less than eps); when that candidate set holds more than
-// one distinct row, or anything is not finite, the exact float64 pass decides
-// among the candidates. The result is always the reference encoder's choice.
+// floor for subnormal products. The float64 winner w (the reference
+// encoder's choice) has f_w <= min_e f_e + 2 eps, so it lies in the
+// candidate set {e : f_e <= min f + 2 eps} (duplicate rows removed: a
+// duplicate of a lower row never wins a tie). A set of one entry is that
+// winner; otherwise, or when anything is not finite, the exact float64 pass
+// decides among the candidates.
+//
+// `src`, when not null, is where x lives in memory: the rare exact pass then
+// reads the vector from there, so the values need not stay in registers
+// after the filter.
 template <int G, class Book>
-__device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], const BookMeta& m, bool* certified) {
-  float acc[16];
+__device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], bool* certified, const float* src = nullptr) {
+  // acc[p] = (x.c_2p, x.c_2p+1): one packed FMA per component and entry pair,
+  // each lane rounded like fmaf, components in order
+  float2 acc[8];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
-  float nx2 = 0.f;
+  for (int p = 0; p < 8; ++p) acc[p] = make_float2(0.f, 0.f);
+  float2 n2 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int q = 0; q < G / 4; ++q) {
-    const float x0 = x[4 * q], x1 = x[4 * q + 1], x2 = x[4 * q + 2], x3 = x[4 * q + 3];
+  for (int h = 0; h < G / 2; ++h) {
+    const float x0 = x[2 * h], x1 = x[2 * h + 1];
+    const float2 xx0 = make_float2(x0, x0), xx1 = make_float2(x1, x1);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float4 c = Book::quad(e, q);  // components in order: the same sums as one by one
-      acc[e] = fmaf(x3, c.w, fmaf(x2, c.z, fmaf(x1, c.y, fmaf(x0, c.x, acc[e]))));
+    for (int p = 0; p < 8; ++p) {
+      const float4 c = Book::quad(p, h);
+      acc[p] = __ffma2_rn(xx1, make_float2(c.z, c.w), __ffma2_rn(xx0, make_float2(c.x, c.y), acc[p]));
     }
-    nx2 = fmaf(x3, x3, fmaf(x2, x2, fmaf(x1, x1, fmaf(x0, x0, nx2))));
+    n2 = __ffma2_rn(make_float2(x0, x1), make_float2(x0, x1), n2);
   }
+  const float nx2 = n2.x + n2.y;
   float f[16];
-  const float4* q4 = reinterpret_cast<const float4*>(m.q);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 q = q4[i];
-    f[4 * i + 0] = fmaf(-2.f, acc[4 * i + 0], q.x);
-    f[4 * i + 1] = fmaf(-2.f, acc[4 * i + 1], q.y);
-    f[4 * i + 2] = fmaf(-2.f, acc[4 * i + 2], q.z);
-    f[4 * i + 3] = fmaf(-2.f, acc[4 * i + 3], q.w);
+  for (int p = 0; p < 8; ++p) {
+    const float2 t = __ffma2_rn(make_float2(-2.f, -2.f), acc[p], Book::qpair(p));
+    f[2 * p] = t.x;
+    f[2 * p + 1] = t.y;
   }
-  float fb = f[0];
-  uint32_t best = 0;
+  // the minimum as a tree (a NaN f_e is skipped here and caught below)
+  float lo[8];
 #pragma unroll
-  for (int e = 1; e < 16; ++e)
-    if (f[e] < fb) {
-      fb = f[e];
-      best = uint32_t(e);
-    }
+  for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
+#pragma unroll
+  for (int w = 4; w; w >>= 1)
+#pragma unroll
+    for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
+  const float fb = lo[0];
   constexpr float kappa = float(G + 8) * (1.0f / 8388608.0f);
-  const float eps = fmaf(kappa, nx2 + m.cmax2, 1e-37f);
+  const float eps = fmaf(kappa, nx2 + Book::cmax2(), 1e-37f);
   const float thr = fmaf(2.f, eps, fb);
   uint32_t cand = 0;
 #pragma unroll
   for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
-  cand &= m.uniq;
-  const bool clean = finite32(thr) && finite32(fb) && !m.bad;
-  if (clean && cand == (1u << best)) {
+  cand &= Book::uniq();
+  const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
+  if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
     *certified = false;
-    return best;
+    return uint32_t(__ffs(cand) - 1);
   }
   *certified = true;
+  if (src) return enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
   return enc_exact<G, Book>(x, G, clean ? cand : 0xffffu);
 }
 

@@ -104,79 +104,161 @@ __device__ __forceinline__ void load_vector(const float* __restrict__ x, uint64_
   }
 }
 
-// At least 4/3/2 resident blocks for group 8/16/32; the fused AdamW kernels
+// At least 3/3/2 resident blocks for group 8/16/32 (measured best: more
+// would spill the double buffer); the fused AdamW kernels
 // hold more per thread.
 template <int G>
-constexpr int encode_min_blocks() { return G == 8 ? 4 : (G == 16 ? 3 : 2); }
+constexpr int encode_min_blocks() { return G == 32 ? 2 : 3; }
 template <int G>
 constexpr int adamw_min_blocks() { return G == 8 ? 3 : (G == 16 ? 2 : 1); }
 
-// BookMeta of the NB books in slot SLOT, into g_meta (one warp).
-template <int G, int SLOT, int NB>
-__global__ void k_book_meta() {
-  __shared__ BookMeta m;
+// Book staging area: the launcher's staging kernel writes the
+// pair-interleaved image of a slot's books and their BookMeta here, then
+// the stream copies it into the slot's constant bank.
+__device__ __align__(16) float g_stage[kBookSlots][kSlotFloats];
+
+// Stage `nb` row-major 16 x G books from `src` for slot `slot`: warp b writes
+// book b pair-interleaved into g_stage[slot] and its BookMeta after the
+// books (the slot layout CBook reads).
+template <int G>
+__global__ void k_stage_books(const float* __restrict__ src, int nb, int slot) {
+  __shared__ BookMeta m[3];
+  const int b = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (b >= nb) return;
+  const float* book = src + b * 16 * G;
+  float* dst = g_stage[slot] + b * 16 * G;
+  for (int i = lane; i < 16 * G; i += 32) dst[book_pos<G>(i / G, i % G)] = book[i];
+  meta_compute<G>(book, m[b]);
+  __syncwarp();
+  constexpr int kWords = sizeof(BookMeta) / 4;
+  uint32_t* meta = reinterpret_cast<uint32_t*>(g_stage[slot] + kSlotBookFloats + b * kMetaFloats);
+  if (lane < kWords) meta[lane] = reinterpret_cast<const uint32_t*>(&m[b])[lane];
+}
+
+// One encode step of a warp: 32 consecutive vectors from `base` (one per
+// lane; `xr` holds the lane's complete vector), nibbles packed into 4 words
+// with shuffles.
+template <int G, int SLOT>
+__device__ __forceinline__ void enc_step(const float* __restrict__ x, uint64_t n, uint64_t base,
+                                         const float (&xr)[G], uint32_t* __restrict__ codes,
+                                         uint32_t* __restrict__ status) {
+  using Book = CBook<G, SLOT, 0>;
+  const uint64_t vectors = (n + G - 1) / G, full = n / G, words = (vectors + 7) / 8;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t v = base + lane;
+  uint32_t idx = 0, bits = 0;
+  if (v < full) {
+    bool certified;
+    const float* src = x + v * G;
+    idx = enc_vector<G, Book>(xr, &certified, src);
+    if (certified) {
+      // the rare path: nonfinite values are flagged here, not on every
+      // vector (read again from memory: the registers are free by now)
+      for (int j = 0; j < G; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+    }
+  } else if (v < vectors) {
+    // The partial last vector: compare its valid components only (vq.py:171-172).
+    const int valid = int(n - v * G);
+    const float* src = x + v * G;
+    for (int j = 0; j < valid; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+    idx = enc_exact_mem<G, Book>(src, valid, 0xffffu);
+  }
+  const uint32_t w = pack_nibbles(idx);
+  const uint64_t word = (base >> 3) + (lane >> 3);
+  if ((lane & 7) == 0 && word < words) codes[word] = w;
+  flag_warp(status, bits);
+}
+
+template <int G, bool VEC>
+__device__ __forceinline__ void enc_load(const float* __restrict__ x, uint64_t v, uint64_t full, float (&xr)[G]) {
+  if (v < full) {
+    if (VEC) {
+      load_vector<G>(x, v, xr);
+    } else {
 #pragma unroll
-  for (int b = 0; b < NB; ++b) {
-    if (b == 0) meta_compute<G, CBook<G, SLOT, 0>>(m);
-    if (b == 1) meta_compute<G, CBook<G, SLOT, 1>>(m);
-    if (b == 2) meta_compute<G, CBook<G, SLOT, 2>>(m);
-    __syncwarp();
-    constexpr int kWords = sizeof(BookMeta) / 4;
-    if (threadIdx.x < kWords)
-      reinterpret_cast<uint32_t*>(&g_meta[SLOT][b])[threadIdx.x] = reinterpret_cast<const uint32_t*>(&m)[threadIdx.x];
-    __syncwarp();
+      for (int j = 0; j < G; ++j) xr[j] = x[v * G + j];
+    }
   }
 }
 
-// A persistent grid; each warp takes 32 consecutive vectors per step (one
-// per lane) and packs their nibbles into 4 words with shuffles.
-template <int G, int SLOT>
+// A persistent grid; each warp takes 32 consecutive vectors per step. The
+// next step's vectors are loaded into registers while the current ones are
+// filtered (two buffers, used in turn). VEC: x is 16-byte aligned.
+template <int G, int SLOT, bool VEC>
 __global__ void __launch_bounds__(kThreads, encode_min_blocks<G>()) k_encode(const float* __restrict__ x, uint64_t n,
                                                                              uint32_t* __restrict__ codes,
-                                                                             uint32_t* __restrict__ status,
-                                                                             int aligned) {
+                                                                             uint32_t* __restrict__ status) {
   using Book = CBook<G, SLOT, 0>;
-  __shared__ BookMeta meta;
-  meta_load<SLOT, 0>(meta);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && meta.bad) atomicOr(status, kNonfinite);
-  const uint64_t vectors = (n + G - 1) / G;
-  const uint64_t full = n / G;
-  const uint64_t words = (vectors + 7) / 8;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && Book::bad()) atomicOr(status, kNonfinite);
+  const uint64_t vectors = (n + G - 1) / G, full = n / G;
   const uint32_t lane = threadIdx.x & 31;
-  const uint64_t warps = uint64_t(gridDim.x) * (blockDim.x / 32);
-  for (uint64_t base = (uint64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32) * 32; base < vectors;
-       base += warps * 32) {
-    const uint64_t v = base + lane;
-    uint32_t idx = 0, bits = 0;
-    float xr[G];
-    if (v < full) {
-      if (aligned) {
-        load_vector<G>(x, v, xr);
-      } else {
-#pragma unroll
-        for (int j = 0; j < G; ++j) xr[j] = x[v * G + j];
-      }
-      bool certified;
-      idx = enc_vector<G, Book>(xr, meta, &certified);
-      if (certified) {
-        // the rare path: nonfinite values are flagged here, not on every vector
-#pragma unroll
-        for (int j = 0; j < G; ++j) bits |= finite32(xr[j]) ? 0u : kNonfinite;
-      }
-    } else if (v < vectors) {
-      // The partial last vector: compare its valid components only (vq.py:171-172).
-      const int valid = int(n - v * G);
-#pragma unroll
-      for (int j = 0; j < G; ++j) xr[j] = j < valid ? x[v * G + j] : 0.f;
-#pragma unroll
-      for (int j = 0; j < G; ++j) bits |= (j < valid && !finite32(xr[j])) ? kNonfinite : 0u;
-      idx = enc_exact<G, Book>(xr, valid, 0xffffu);
-    }
-    const uint32_t w = pack_nibbles(idx);
-    const uint64_t word = (base >> 3) + (lane >> 3);
-    if ((lane & 7) == 0 && word < words) codes[word] = w;
-    flag_warp(status, bits);
+  const uint64_t stride = uint64_t(gridDim.x) * (blockDim.x / 32) * 32;
+  uint64_t base = (uint64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32) * 32;
+  float xa[G], xb[G];
+  enc_load<G, VEC>(x, base + lane, full, xa);
+  for (; base < vectors; base += 2 * stride) {
+    enc_load<G, VEC>(x, base + stride + lane, full, xb);
+    enc_step<G, SLOT>(x, n, base, xa, codes, status);
+    if (base + stride >= vectors) break;
+    enc_load<G, VEC>(x, base + 2 * stride + lane, full, xa);
+    enc_step<G, SLOT>(x, n, base + stride, xb, codes, status);
   }
+}
+
+// Group 32 with 16-byte aligned x: each warp step copies its 32 vectors
+// (4 KB, contiguous) into a per-warp shared buffer with cp.async, 16 bytes
+// per lane per instruction, double-buffered; quad L of a step sits at
+// L ^ ((L >> 3) & 7), so both the copy and each lane's read of its own
+// vector are free of bank conflicts. Fully coalesced global reads and no
+// registers held for the prefetch.
+__device__ __forceinline__ uint32_t enc_swizzle(uint32_t L) { return L ^ ((L >> 3) & 7u); }
+
+template <int G, int SLOT>
+__global__ void __launch_bounds__(kThreads, 3) k_encode_async(const float* __restrict__ x, uint64_t n,
+                                                              uint32_t* __restrict__ codes,
+                                                              uint32_t* __restrict__ status) {
+  using Book = CBook<G, SLOT, 0>;
+  constexpr int kQuads = 8 * G;  // 16-byte quads per warp step
+  extern __shared__ __align__(16) float4 sx[];  // [warps][2][kQuads]
+  if (blockIdx.x == 0 && threadIdx.x == 0 && Book::bad()) atomicOr(status, kNonfinite);
+  const uint64_t vectors = (n + G - 1) / G, full = n / G;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  float4* buf0 = sx + size_t(warp) * 2 * kQuads;
+  const uint64_t stride = uint64_t(gridDim.x) * (blockDim.x / 32) * 32;
+  const uint64_t quads_full = full * (G / 4);
+  uint64_t base = (uint64_t(blockIdx.x) * (blockDim.x / 32) + warp) * 32;
+  auto issue = [&](uint64_t b, float4* buf) {
+    const uint64_t q0 = b * (G / 4);
+#pragma unroll
+    for (int k = 0; k < G / 4; ++k) {
+      const uint32_t L = lane + 32 * k;
+      if (q0 + L < quads_full) {  // complete vectors only; the tail is read directly
+        const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(buf + enc_swizzle(L)));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(x + (q0 + L) * 4) : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (base < vectors) issue(base, buf0);
+  for (int s = 0; base < vectors; base += stride, s ^= 1) {
+    const float4* cur = buf0 + s * kQuads;
+    if (base + stride < vectors) issue(base + stride, buf0 + (s ^ 1) * kQuads);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncwarp();
+    float xr[G];
+#pragma unroll
+    for (int q = 0; q < G / 4; ++q) {
+      const float4 t = cur[enc_swizzle(lane * (G / 4) + q)];
+      xr[4 * q] = t.x;
+      xr[4 * q + 1] = t.y;
+      xr[4 * q + 2] = t.z;
+      xr[4 * q + 3] = t.w;
+    }
+    __syncwarp();  // every lane holds its vector before the buffer is refilled
+    enc_step<G, SLOT>(x, n, base, xr, codes, status);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // ------------------------------------------- shader-exact packed-pair matmul --
@@ -457,99 +539,128 @@ __global__ void __launch_bounds__(kThreads) k_repack_tile32(const uint4* __restr
 // and the same per-row lookup order as k_dense_lut (results are bitwise the
 // same), but each warp reads its 32 rows' codes as coalesced 512-byte lines
 // straight into registers: no shared-memory staging and no barrier inside a
-// t-chunk. A block shares one table; its warps take row tiles in turn.
+// t-chunk.
+//
+// Persistent grid: the work units are (expert, 32-row tile), expert-major,
+// and block b takes the contiguous range [U b / grid, U (b + 1) / grid), so
+// every block gets the same number of tiles to within one whatever the
+// expert count. Per expert segment of its range and per (m, t)-chunk a block
+// builds the table once: the chunk of X arrives in shared memory in one
+// round trip, lane e % 16 holds book row e in registers and a half-warp
+// computes the 16 entries of one group, stored as one contiguous 64-byte row
+// (conflict-free).
 template <int G, int MC, int TC>
 __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restrict__ X,
                                                            const uint4* __restrict__ codes,
                                                            const float* __restrict__ books, float* __restrict__ Y,
-                                                           uint32_t M, uint32_t N, uint32_t K,
-                                                           uint32_t items_per_expert, uint32_t tiles_per_item,
+                                                           uint32_t M, uint32_t N, uint32_t K, uint32_t experts,
                                                            uint64_t units_per_expert, uint32_t* __restrict__ status) {
   constexpr int kPieces = TC / 32;
   extern __shared__ __align__(16) unsigned char smem[];
   float* P = reinterpret_cast<float*>(smem);  // [MC][TC][16]
-  __shared__ float sbook[16 * G];
-  const uint32_t e = blockIdx.x / items_per_expert, part = blockIdx.x % items_per_expert;
+  float* Xs = P + MC * TC * 16;                // [TC * G]: one row's X chunk
   const uint32_t T = K / G, ct = T / 32;
   const uint32_t ntiles = (N + 31) / 32;
-  const uint32_t tl0 = part * tiles_per_item, tl1 = min(ntiles, tl0 + tiles_per_item);
-  if (tl0 >= tl1) return;  // the whole block leaves together
-  const float* Xb = X + uint64_t(e) * M * K;
-  const uint4* Cb = codes + uint64_t(e) * units_per_expert;
-  float* Yb = Y + uint64_t(e) * M * N;
-  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) sbook[i] = books[uint64_t(e) * 16 * G + i];
-  __syncthreads();
-  if (part == 0) {
-    uint32_t bits = 0;
-    for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) bits |= finite32(sbook[i]) ? 0u : kNonfinite;
-    flag_warp(status, bits);
-  }
+  const uint64_t total = uint64_t(experts) * ntiles;
+  const bool x_vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0;
+  const uint64_t u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (uint32_t m0 = 0; m0 < M; m0 += MC) {
-    const uint32_t mc = min(uint32_t(MC), M - m0);
-    for (uint32_t t0 = 0; t0 < T; t0 += TC) {
-      __syncthreads();  // the previous table is no longer read
-      for (uint32_t i = threadIdx.x; i < mc * TC; i += blockDim.x) {
-        const uint32_t m = i / TC, t = i % TC;
-        const float* xs = Xb + uint64_t(m0 + m) * K + uint64_t(t0 + t) * G;
-        float xr[G];
+  for (uint64_t s0 = u0; s0 < u1;) {
+    const uint32_t e = uint32_t(s0 / ntiles);
+    const uint64_t s1 = min(u1, uint64_t(e + 1) * ntiles);
+    const uint32_t tl0 = uint32_t(s0 - uint64_t(e) * ntiles), tl1 = uint32_t(s1 - uint64_t(e) * ntiles);
+    const float* Xb = X + uint64_t(e) * M * K;
+    const uint4* Cb = codes + uint64_t(e) * units_per_expert;
+    float* Yb = Y + uint64_t(e) * M * N;
+    float brow[G];  // book row lane % 16
+    {
+      const float* b = books + uint64_t(e) * 16 * G + (lane & 15) * G;
 #pragma unroll
-        for (int j = 0; j < G; ++j) xr[j] = __ldg(xs + j);
-        float* dst = P + (size_t(m) * TC + t) * 16;
+      for (int j = 0; j < G; ++j) brow[j] = __ldg(b + j);
+    }
+    if (tl0 == 0 && warp == 0) {  // the one block whose range starts the expert checks its book
+      uint32_t bits = 0;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float acc = 0.f;
+      for (int j = 0; j < G; ++j) bits |= finite32(brow[j]) ? 0u : kNonfinite;
+      flag_warp(status, bits);
+    }
+    for (uint32_t m0 = 0; m0 < M; m0 += MC) {
+      const uint32_t mc = min(uint32_t(MC), M - m0);
+      for (uint32_t t0 = 0; t0 < T; t0 += TC) {
+        for (uint32_t m = 0; m < mc; ++m) {
+          // this row's X chunk into shared memory in one round trip, then
+          // the 16 dots of each group: half-warp per group, lane = entry
+          __syncthreads();  // the previous table / chunk is no longer read
+          const float* xrow = Xb + uint64_t(m0 + m) * K + uint64_t(t0) * G;
+          if (x_vec) {
+            for (uint32_t i = threadIdx.x; i < TC * G / 4; i += kThreads)
+              reinterpret_cast<float4*>(Xs)[i] = __ldg(reinterpret_cast<const float4*>(xrow) + i);
+          } else {
+            for (uint32_t i = threadIdx.x; i < TC * G; i += kThreads) Xs[i] = __ldg(xrow + i);
+          }
+          __syncthreads();
+          for (uint32_t t = warp * 2 + (lane >> 4); t < TC; t += 2 * (kThreads / 32)) {
+            const float4* xs = reinterpret_cast<const float4*>(Xs + t * G);
+            float acc = 0.f;
 #pragma unroll
-          for (int j = 0; j < G; ++j) acc = fmaf(xr[j], sbook[c * G + j], acc);
-          dst[c] = acc;
+            for (int q = 0; q < G / 4; ++q) {
+              const float4 v = xs[q];
+              acc = fmaf(v.x, brow[4 * q], acc);
+              acc = fmaf(v.y, brow[4 * q + 1], acc);
+              acc = fmaf(v.z, brow[4 * q + 2], acc);
+              acc = fmaf(v.w, brow[4 * q + 3], acc);
+            }
+            P[(size_t(m) * TC + t) * 16 + (lane & 15)] = acc;
+          }
         }
-      }
-      __syncthreads();
-      for (uint32_t tile = tl0 + warp; tile < tl1; tile += kThreads / 32) {
-        const uint4* src = Cb + (uint64_t(tile) * ct + t0 / 32) * 32 + lane;
-        uint4 q[kPieces];
+        __syncthreads();
+        for (uint32_t tile = tl0 + warp; tile < tl1; tile += kThreads / 32) {
+          const uint4* src = Cb + (uint64_t(tile) * ct + t0 / 32) * 32 + lane;
+          uint4 q[kPieces];
 #pragma unroll
-        for (int pc = 0; pc < kPieces; ++pc) q[pc] = __ldg(src + pc * 32);
-        float acc[MC][4];
+          for (int pc = 0; pc < kPieces; ++pc) q[pc] = __ldg(src + pc * 32);
+          float acc[MC][4];
 #pragma unroll
-        for (int m = 0; m < MC; ++m)
+          for (int m = 0; m < MC; ++m)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) acc[m][r] = 0.f;
-        const unsigned char* Pb = smem;
+            for (int r = 0; r < 4; ++r) acc[m][r] = 0.f;
+          const unsigned char* Pb = smem;
 #pragma unroll
-        for (int pc = 0; pc < kPieces; ++pc) {
-          const uint32_t wd[4] = {q[pc].x, q[pc].y, q[pc].z, q[pc].w};
+          for (int pc = 0; pc < kPieces; ++pc) {
+            const uint32_t wd[4] = {q[pc].x, q[pc].y, q[pc].z, q[pc].w};
 #pragma unroll
-          for (int wi = 0; wi < 4; ++wi) {
-            const uint32_t lo = (wd[wi] << 2) & 0x3C3C3C3Cu;  // 4 * nibbles 0, 2, 4, 6
-            const uint32_t hi = (wd[wi] >> 2) & 0x3C3C3C3Cu;  // 4 * nibbles 1, 3, 5, 7
+            for (int wi = 0; wi < 4; ++wi) {
+              const uint32_t lo = (wd[wi] << 2) & 0x3C3C3C3Cu;  // 4 * nibbles 0, 2, 4, 6
+              const uint32_t hi = (wd[wi] >> 2) & 0x3C3C3C3Cu;  // 4 * nibbles 1, 3, 5, 7
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t olo = __byte_perm(lo, 0, 0x4440 + kk);
-              const uint32_t ohi = __byte_perm(hi, 0, 0x4440 + kk);
-              const int t = pc * 32 + wi * 8 + 2 * kk;
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t olo = __byte_perm(lo, 0, 0x4440 + kk);
+                const uint32_t ohi = __byte_perm(hi, 0, 0x4440 + kk);
+                const int t = pc * 32 + wi * 8 + 2 * kk;
 #pragma unroll
-              for (int m = 0; m < MC; ++m) {
-                const unsigned char* pm = Pb + (size_t(m) * TC + t) * 64;
-                acc[m][(2 * kk) & 3] += *reinterpret_cast<const float*>(pm + olo);
-                acc[m][(2 * kk + 1) & 3] += *reinterpret_cast<const float*>(pm + 64 + ohi);
+                for (int m = 0; m < MC; ++m) {
+                  const unsigned char* pm = Pb + (size_t(m) * TC + t) * 64;
+                  acc[m][(2 * kk) & 3] += *reinterpret_cast<const float*>(pm + olo);
+                  acc[m][(2 * kk + 1) & 3] += *reinterpret_cast<const float*>(pm + 64 + ohi);
+                }
               }
             }
           }
-        }
-        const uint32_t row = tile * 32 + lane;
-        if (row < N) {
+          const uint32_t row = tile * 32 + lane;
+          if (row < N) {
 #pragma unroll
-          for (int m = 0; m < MC; ++m) {
-            if (m < int(mc)) {
-              const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
-              float* dst = Yb + uint64_t(m0 + m) * N + row;
-              *dst = t0 ? *dst + y : y;
+            for (int m = 0; m < MC; ++m) {
+              if (m < int(mc)) {
+                const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
+                float* dst = Yb + uint64_t(m0 + m) * N + row;
+                *dst = t0 ? *dst + y : y;
+              }
             }
           }
         }
       }
     }
+    s0 = s1;
   }
 }
 
@@ -830,11 +941,10 @@ __global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage
                                                                                  uint32_t* __restrict__ status) {
   using Book = CBook<G, SLOT, 0>;
   __shared__ float sbooks[4 * 16 * G];
-  __shared__ BookMeta meta;
   __shared__ uint32_t hist[16];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(expert) * 64 * G + i];
   if (threadIdx.x < 16) hist[threadIdx.x] = 0;
-  meta_load<SLOT, 0>(meta);
+  __syncthreads();
   const AdamwCoefs k = load_coefs(a.coefs + 7 * expert);
   const uint64_t full = a.n / G;
   const uint64_t v = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -843,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_usage
     float x[G];
     adamw_vector<G>(a, sbooks, k, expert, v, G, int(state), x, &bits);
     bool certified;
-    atomicAdd(&hist[enc_vector<G, Book>(x, meta, &certified)], 1u);
+    atomicAdd(&hist[enc_vector<G, Book>(x, &certified)], 1u);
   }
   flag_warp(status, bits);
   __syncthreads();
@@ -862,17 +972,10 @@ __global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_encod
   using BM = CBook<G, SLOT, 1>;
   using BV = CBook<G, SLOT, 2>;
   __shared__ float sbooks[4 * 16 * G];
-  __shared__ BookMeta meta[3];
   for (int i = threadIdx.x; i < 64 * G; i += blockDim.x) sbooks[i] = a.books[uint64_t(e) * 64 * G + i];
-  {
-    constexpr int kWords = sizeof(BookMeta) / 4;
-    if (threadIdx.x < 3 * kWords)
-      reinterpret_cast<uint32_t*>(meta)[threadIdx.x] = reinterpret_cast<const uint32_t*>(g_meta[SLOT])[threadIdx.x];
-  }
   __syncthreads();
   const AdamwCoefs k = load_coefs(a.coefs + 7 * e);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && (meta[0].bad || meta[1].bad || meta[2].bad))
-    atomicOr(status, kNonfinite);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && (BW::bad() || BM::bad() || BV::bad())) atomicOr(status, kNonfinite);
   const uint64_t vectors = (uint64_t(a.n) + G - 1) / G;
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t base = uint64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u);
@@ -886,18 +989,18 @@ __global__ void __launch_bounds__(kThreads, adamw_min_blocks<G>()) k_adamw_encod
       // the AdamW arithmetic (two divisions and a square root per value) once
       float w[G], m[G], var[G];
       adamw_vector3<G>(a, sbooks, k, e, v, valid, w, m, var, &bits);
-      idx[0] = valid == G ? enc_vector<G, BW>(w, meta[0], &certified) : enc_exact<G, BW>(w, valid, 0xffffu);
-      idx[1] = valid == G ? enc_vector<G, BM>(m, meta[1], &certified) : enc_exact<G, BM>(m, valid, 0xffffu);
-      idx[2] = valid == G ? enc_vector<G, BV>(var, meta[2], &certified) : enc_exact<G, BV>(var, valid, 0xffffu);
+      idx[0] = valid == G ? enc_vector<G, BW>(w, &certified) : enc_exact<G, BW>(w, valid, 0xffffu);
+      idx[1] = valid == G ? enc_vector<G, BM>(m, &certified) : enc_exact<G, BM>(m, valid, 0xffffu);
+      idx[2] = valid == G ? enc_vector<G, BV>(var, &certified) : enc_exact<G, BV>(var, valid, 0xffffu);
     } else {
       // group 32: one state at a time keeps one vector of values live
       float x[G];
       adamw_vector<G>(a, sbooks, k, e, v, valid, 0, x, &bits);
-      idx[0] = valid == G ? enc_vector<G, BW>(x, meta[0], &certified) : enc_exact<G, BW>(x, valid, 0xffffu);
+      idx[0] = valid == G ? enc_vector<G, BW>(x, &certified) : enc_exact<G, BW>(x, valid, 0xffffu);
       adamw_vector<G>(a, sbooks, k, e, v, valid, 1, x, &bits);
-      idx[1] = valid == G ? enc_vector<G, BM>(x, meta[1], &certified) : enc_exact<G, BM>(x, valid, 0xffffu);
+      idx[1] = valid == G ? enc_vector<G, BM>(x, &certified) : enc_exact<G, BM>(x, valid, 0xffffu);
       adamw_vector<G>(a, sbooks, k, e, v, valid, 2, x, &bits);
-      idx[2] = valid == G ? enc_vector<G, BV>(x, meta[2], &certified) : enc_exact<G, BV>(x, valid, 0xffffu);
+      idx[2] = valid == G ? enc_vector<G, BV>(x, &certified) : enc_exact<G, BV>(x, valid, 0xffffu);
     }
     // vq.py:402: decoded new weight against decoded old weight, value by value
     const uint32_t old = code_at(a.codes + uint64_t(e) * 4 * a.words, v);
@@ -965,9 +1068,24 @@ struct SlotRing {
 };
 SlotRing g_rings[64];
 
+// Device address of g_stage, looked up once per device.
+float* stage_address(cudaError_t* err) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev & 63]) *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&addr[dev & 63]), g_stage);
+  return addr[dev & 63];
+}
+
+// One launch's hold on a slot: waits for the slot's previous user, stages
+// `nb` books of group `group` from `src` (device memory) into it, and on
+// release records the slot's event.
 class BookSlot {
  public:
-  BookSlot(cudaStream_t stream, const void* src, size_t bytes) : stream_(stream) {
+  BookSlot(cudaStream_t stream, const void* src, int nb, uint32_t group) : stream_(stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     ring_ = &g_rings[dev & 63];
@@ -975,9 +1093,17 @@ class BookSlot {
     index_ = int(ring_->next++ % kBookSlots);
     cudaEvent_t& ev = ring_->done[index_];
     err_ = ev ? cudaStreamWaitEvent(stream, ev, 0) : cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-    if (err_ == cudaSuccess)
-      err_ = cudaMemcpyToSymbolAsync(c_books, src, bytes, size_t(index_) * kSlotFloats * sizeof(float),
-                                     cudaMemcpyDeviceToDevice, stream);
+    float* stage = nullptr;
+    if (err_ == cudaSuccess) stage = stage_address(&err_);
+    if (err_ != cudaSuccess) return;
+    const float* books = static_cast<const float*>(src);
+    if (group == 8) k_stage_books<8><<<1, 32 * nb, 0, stream>>>(books, nb, index_);
+    else if (group == 16) k_stage_books<16><<<1, 32 * nb, 0, stream>>>(books, nb, index_);
+    else k_stage_books<32><<<1, 32 * nb, 0, stream>>>(books, nb, index_);
+    err_ = cudaGetLastError();
+    if (err_ == cudaSuccess)  // books and their meta: the whole slot
+      err_ = cudaMemcpyToSymbolAsync(c_books, stage + size_t(index_) * kSlotFloats, kSlotFloats * sizeof(float),
+                                     size_t(index_) * kSlotFloats * sizeof(float), cudaMemcpyDeviceToDevice, stream);
   }
   ~BookSlot() {
     if (lock_.owns_lock()) release();
@@ -1028,13 +1154,40 @@ struct RunEncode {
   static cudaError_t run(const float* x, uint64_t n, const float* book, uint32_t* codes, uint32_t* status,
                          cudaStream_t s) {
     const uint64_t vectors = (n + G - 1) / G;
-    const int aligned = aligned16(x) ? 1 : 0;
-    const uint64_t grid = grid_for(vectors, resident_per_sm(k_encode<G, 0>, 0));
-    BookSlot slot(s, book, 16 * G * sizeof(float));
+    const bool vec = aligned16(x);
+    if constexpr (G == 32) {
+      if (vec) return run_async(x, n, book, codes, status, s);
+    }
+    const uint64_t grid = grid_for(vectors, resident_per_sm(k_encode<G, 0, true>, 0));
+    BookSlot slot(s, book, 1, G);
     if (slot.error() != cudaSuccess) return slot.error();
-#define ACK_LAUNCH_ENCODE(S)                                   \
-  k_book_meta<G, S, 1><<<1, 32, 0, s>>>();                     \
-  k_encode<G, S><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status, aligned)
+#define ACK_LAUNCH_ENCODE(S)                                                                 \
+  if (vec) k_encode<G, S, true><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status);  \
+  else k_encode<G, S, false><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status)
+    ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
+#undef ACK_LAUNCH_ENCODE
+    const cudaError_t e = cudaGetLastError();
+    const cudaError_t r = slot.release();
+    return e != cudaSuccess ? e : r;
+  }
+
+  // group 32, aligned x: coalesced cp.async staging (k_encode_async)
+  static cudaError_t run_async(const float* x, uint64_t n, const float* book, uint32_t* codes, uint32_t* status,
+                               cudaStream_t s) {
+    const uint64_t vectors = (n + G - 1) / G;
+    constexpr size_t smem = size_t(kThreads / 32) * 2 * 8 * G * 16;
+    cudaError_t err = cudaSuccess;
+#define ACK_ASYNC_ATTR(S)                                                                                       \
+  if (err == cudaSuccess)                                                                                       \
+    err = cudaFuncSetAttribute(k_encode_async<G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    ACK_ASYNC_ATTR(0) ACK_ASYNC_ATTR(1) ACK_ASYNC_ATTR(2) ACK_ASYNC_ATTR(3)
+    ACK_ASYNC_ATTR(4) ACK_ASYNC_ATTR(5) ACK_ASYNC_ATTR(6) ACK_ASYNC_ATTR(7)
+#undef ACK_ASYNC_ATTR
+    if (err != cudaSuccess) return err;
+    const uint64_t grid = grid_for(vectors, resident_per_sm(k_encode_async<G, 0>, smem));
+    BookSlot slot(s, book, 1, G);
+    if (slot.error() != cudaSuccess) return slot.error();
+#define ACK_LAUNCH_ENCODE(S) k_encode_async<G, S><<<uint32_t(grid), kThreads, smem, s>>>(x, n, codes, status)
     ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
 #undef ACK_LAUNCH_ENCODE
     const cudaError_t e = cudaGetLastError();
@@ -1101,19 +1254,16 @@ cudaError_t launch_dense_mc(const float* X, const uint32_t* codes, const float* 
 template <int G, int MC, int TC>
 cudaError_t launch_dense_t32(const float* X, const uint4* codes, const float* books, float* Y, uint32_t M,
                              uint32_t N, uint32_t K, uint32_t batch, uint32_t* status, cudaStream_t s) {
-  const size_t smem = size_t(MC) * TC * 64;
+  const size_t smem = size_t(MC) * TC * 64 + size_t(TC) * G * 4;
   cudaError_t err = cudaFuncSetAttribute(k_dense_t32<G, MC, TC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(smem));
   if (err != cudaSuccess) return err;
   const uint64_t resident = uint64_t(sm_count()) * resident_per_sm(k_dense_t32<G, MC, TC>, smem);
-  const uint32_t ntiles = (N + 31) / 32;
-  const uint32_t warps = kThreads / 32;
-  const uint32_t nbatches = (ntiles + warps - 1) / warps;  // a batch: one tile per warp
-  const uint32_t per_item = balance_batches(nbatches, batch, resident);
-  const uint32_t items = (nbatches + per_item - 1) / per_item;
+  const uint64_t tiles = uint64_t(batch) * ((N + 31) / 32);
+  // one persistent wave, at least one tile per warp per block
+  const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(resident, (tiles + 7) / 8));
   const uint64_t units = tile32_bytes(N, K, G) / 16;
-  k_dense_t32<G, MC, TC><<<uint32_t(uint64_t(items) * batch), kThreads, smem, s>>>(
-      X, codes, books, Y, M, N, K, items, per_item * warps, units, status);
+  k_dense_t32<G, MC, TC><<<uint32_t(grid), kThreads, smem, s>>>(X, codes, books, Y, M, N, K, batch, units, status);
   return cudaGetLastError();
 }
 
@@ -1204,12 +1354,10 @@ struct RunAdamwFused {
       cudaError_t err = cudaMemsetAsync(ptr[5], 0, 16 * sizeof(uint32_t), s);
       if (err != cudaSuccess) return err;
       const uint32_t grid = uint32_t((p.m / G + kThreads - 1) / kThreads);
-      BookSlot slot(s, ptr[3], 16 * G * sizeof(float));
+      BookSlot slot(s, ptr[3], 1, G);
       if (slot.error() != cudaSuccess) return slot.error();
       uint32_t* out = static_cast<uint32_t*>(ptr[5]);
-#define ACK_LAUNCH_USAGE(S)                  \
-  k_book_meta<G, S, 1><<<1, 32, 0, s>>>();   \
-  k_adamw_usage<G, S><<<grid, kThreads, 0, s>>>(a, p.aux1, p.aux0, out, status)
+#define ACK_LAUNCH_USAGE(S) k_adamw_usage<G, S><<<grid, kThreads, 0, s>>>(a, p.aux1, p.aux0, out, status)
       ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_USAGE)
 #undef ACK_LAUNCH_USAGE
       const cudaError_t e = cudaGetLastError();
@@ -1223,11 +1371,9 @@ struct RunAdamwFused {
     uint32_t* out = static_cast<uint32_t*>(ptr[5]);
     uint32_t* changed = static_cast<uint32_t*>(ptr[6]);
     for (uint32_t e = 0; e < p.batch; ++e) {
-      BookSlot slot(s, new_books + uint64_t(e) * 3 * 16 * G, 3 * 16 * G * sizeof(float));
+      BookSlot slot(s, new_books + uint64_t(e) * 3 * 16 * G, 3, G);
       if (slot.error() != cudaSuccess) return slot.error();
-#define ACK_LAUNCH_ADAMW(S)                  \
-  k_book_meta<G, S, 3><<<1, 32, 0, s>>>();   \
-  k_adamw_encode<G, S><<<grid, kThreads, 0, s>>>(a, e, out, changed, status)
+#define ACK_LAUNCH_ADAMW(S) k_adamw_encode<G, S><<<grid, kThreads, 0, s>>>(a, e, out, changed, status)
       ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ADAMW)
 #undef ACK_LAUNCH_ADAMW
       const cudaError_t le = cudaGetLastError();
