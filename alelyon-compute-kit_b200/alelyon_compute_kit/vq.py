@@ -42,7 +42,7 @@ _HEADER = struct.Struct("<8sIIIIQQ")
 _MAGIC = b"ACKVQ4\0\0"
 
 # schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE = range(16, 23)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK = range(16, 24)
 
 
 def _integer(value, name: str, minimum: int, maximum: int) -> int:
@@ -278,6 +278,110 @@ def fit_codebook(values, *, group: int = 16, iterations: int = 4,
     return _fit(sample, len(complete), group, iterations, init, whole_usage)
 
 
+class ResidentStack:
+    """A `VQStack` held in device memory (see `VQDevice.resident`): codes
+    (canonical or tile32) and books uploaded once, plus per-M activation,
+    output and status buffers reused across calls. `free()` (or leaving a
+    `with` block) releases the device memory."""
+
+    def __init__(self, backend: "VQDevice", stack: "VQStack", layout: str) -> None:
+        if layout not in ("tile32", "canonical"):
+            raise ValueError(f"unknown code layout {layout!r}")
+        if len(stack.shape) != 2:
+            raise ValueError("vq matmul requires matrices")
+        n, k = stack.shape
+        if layout == "tile32" and (k % stack.group or (k // stack.group) % 32):
+            raise ValueError("the tile32 layout needs (K / group) % 32 == 0 for a stored N x K matrix")
+        self.backend, self.shape, self.group, self.layout = backend, stack.shape, stack.group, layout
+        self.count = len(stack)
+        self._io: dict = {}
+        device = backend.device
+        self._buffers = []
+        with device._lock:
+            device._require_open()
+            canon = device.buffer(stack.codes.nbytes)
+            self._buffers.append(canon)
+            canon.upload(stack.codes)
+            books = device.buffer(stack.books.nbytes)
+            self._buffers.append(books)
+            books.upload(stack.books)
+            self.books = books
+            if layout == "tile32":
+                words = (n + 31) // 32 * 32 * (k // stack.group) // 8
+                tiled = device.buffer(self.count * words * 4)
+                self._buffers.append(tiled)
+                status = self._status()
+                plan = backend._plan2(OP_REPACK, n, 1, k, stack.group, batch=self.count)
+                backend._launch2(plan, [canon, None, None, None, None, tiled, None, status])
+                self._check(status)
+                canon.free()
+                self._buffers.remove(canon)
+                self.codes = tiled
+            else:
+                self.codes = canon
+
+    def __len__(self) -> int:
+        return self.count
+
+    def _status(self):
+        status = self.backend.device.buffer(4)
+        self._buffers.append(status)
+        status.upload(np.zeros(1, dtype=np.uint32))
+        return status
+
+    @staticmethod
+    def _check(status) -> None:
+        flags = int(status.download(np.uint32)[0])
+        if flags:
+            raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+
+    def matmul(self, xs, *, transpose_b: bool = True, out: np.ndarray | None = None) -> np.ndarray:
+        if self.layout == "tile32" and not transpose_b:
+            raise ValueError("the tile32 layout holds W stored N x K (transpose_b=True)")
+        backend, device = self.backend, self.backend.device
+        x = _float_array(np.asarray(xs), "activations")
+        if x.ndim != 3 or x.shape[0] != self.count:
+            raise ValueError("activations must be (count, M, K) with one matrix per coded weight")
+        e, m, k = x.shape
+        n, k2 = self.shape if transpose_b else self.shape[::-1]
+        if k != k2:
+            raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
+        flags = (2 if transpose_b else 0) | (4 if self.layout == "tile32" else 0)
+        plan = backend._plan2(OP_DENSE, m, n, k, self.group, flags=flags, batch=e)
+        with device._lock:
+            device._require_open()
+            if not self.codes._handle:
+                raise ack.AckError("resident stack has been freed")
+            io = self._io.get((m, k, n))
+            if io is None:
+                xb, yb = device.buffer(x.nbytes), device.buffer(e * m * n * 4)
+                status = device.buffer(4)
+                self._buffers += [xb, yb, status]
+                io = self._io[(m, k, n)] = (xb, yb, status)
+            xb, yb, status = io
+            xb.upload(x)
+            status.upload(np.zeros(1, dtype=np.uint32))
+            backend._launch2(plan, [xb, self.codes, self.books, None, None, yb, None, status])
+            self._check(status)
+            if out is not None:
+                yb.download(np.float32, out.reshape(-1))
+                return out
+            y = yb.download(np.float32)
+        return y.reshape(e, m, n)
+
+    def free(self) -> None:
+        for b in self._buffers:
+            b.free()
+        self._buffers = []
+        self._io = {}
+
+    def __enter__(self) -> "ResidentStack":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.free()
+
+
 @dataclass(frozen=True, init=False)
 class VQStack:
     """E coded matrices of one shape and group, stored contiguously: codes
@@ -498,12 +602,25 @@ class VQDevice:
         return self.matmul_dense_grouped(np.asarray(x)[None], VQStack.from_arrays([w]),
                                          transpose_b=transpose_b)[0]
 
-    def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True) -> np.ndarray:
+    def resident(self, stack: "VQStack", *, layout: str = "tile32") -> "ResidentStack":
+        """Upload a `VQStack` once and keep it on the device: the weights of
+        a grouped product that runs many times (serving, a training step).
+        `layout="tile32"` (matrices stored N x K with (K / group) % 32 == 0)
+        repacks the codes on the device into the layout whose rows a warp
+        reads as coalesced lines; "canonical" keeps the wire layout."""
+        return ResidentStack(self, stack, layout)
+
+    def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True, out: np.ndarray | None = None) -> np.ndarray:
         """E independent products in one launch: `xs` is (E, M, K) float32
         (or a sequence of (M, K)), `ws` a `VQStack` (or a sequence of
-        VQArray) of E matrices of one shape and group. Returns (E, M, N)."""
+        VQArray) of E matrices of one shape and group, or a `ResidentStack`
+        (then only X and Y cross the bus, into `out` when given: a
+        contiguous (E, M, N) float32 array, ideally in pinned memory).
+        Returns (E, M, N)."""
         if type(transpose_b) is not bool:
             raise ValueError("transpose flags must be boolean")
+        if isinstance(ws, ResidentStack):
+            return ws.matmul(xs, transpose_b=transpose_b, out=out)
         stack = ws if isinstance(ws, VQStack) else VQStack.from_arrays(ws)
         if len(stack.shape) != 2:
             raise ValueError("vq matmul requires matrices")

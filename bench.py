@@ -10,8 +10,8 @@ headline metric is coded-weight GB/s = (code bytes + codebook bytes) / time.
 
   value    device time of the grouped launch, inputs resident in HBM
   e2e      the same metric through VQDevice.matmul_dense_grouped with host
-           (pinned) buffers: the inputs are copied to the device and Y back
-           every step
+           (pinned) buffers and device-resident weights: X is copied to the
+           device and Y back every step
   roofline the k_dense_lut launch against the measured HBM copy bandwidth
   cpu_baseline / --impl reference
            the CPU restatement (decode + dot product, all host threads) on a
@@ -288,33 +288,38 @@ def run_cfg2(args, world, rank, local):
 
 
 def run_cfg2_e2e(args, torch, vq, codes, books, x, book, local):
-    """Through the public API with host buffers: VQDevice.matmul_dense_grouped
-    uploads X, codes and books and downloads Y every step."""
+    """Through the public API with host buffers. The weights are made
+    resident once (VQDevice.resident: uploaded and repacked on the device,
+    outside the timed region); every step copies X from pinned host memory,
+    runs the grouped product and copies Y back into pinned host memory
+    (VQDevice.matmul_dense_grouped on the ResidentStack)."""
     from alelyon_compute_kit import ack
     experts, m = codes.shape[0], x.shape[1]
-    pin_codes = torch.empty(codes.shape, dtype=torch.int32, pin_memory=True)
-    pin_codes.copy_(codes)
-    pin_books = torch.empty(books.shape, dtype=torch.float32, pin_memory=True)
-    pin_books.copy_(books)
+    host_codes = codes.cpu().numpy().view(np.uint32)
+    host_books = books.cpu().numpy()
     pin_x = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
     pin_x.copy_(x)
-    stack = vq.VQStack((N_ROWS, K_COLS), GROUP, pin_codes.numpy().view(np.uint32), pin_books.numpy())
-    xs = pin_x.numpy()
+    pin_y = torch.empty((experts, m, N_ROWS), dtype=torch.float32, pin_memory=True)
+    stack = vq.VQStack((N_ROWS, K_COLS), GROUP, host_codes, host_books)
+    xs, ys = pin_x.numpy(), pin_y.numpy()
     os.environ.setdefault("ACK_DEVICE", f"gpu:{local}")
     with ack.Device() as dev:
         backend = vq.VQDevice(dev)
-        for _ in range(2):
-            backend.matmul_dense_grouped(xs, stack)
-        steps = max(3, min(args.steps, 10))
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            yv = backend.matmul_dense_grouped(xs, stack)
-        elapsed = (time.perf_counter() - t0) / steps
-    h2d = pin_codes.numel() * 4 + pin_books.numel() * 4 + pin_x.numel() * 4 + 4
-    d2h = yv.nbytes + 4
+        with backend.resident(stack, layout=args.layout) as weights:
+            del stack, host_codes
+            for _ in range(3):
+                backend.matmul_dense_grouped(xs, weights, out=ys)
+            steps = max(5, args.steps)
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                backend.matmul_dense_grouped(xs, weights, out=ys)
+            elapsed = (time.perf_counter() - t0) / steps
+    h2d = xs.nbytes + 4          # X and the cleared status word
+    d2h = ys.nbytes + 4          # Y and the status word
     return {"value": round(experts * (CODE_BYTES + BOOK_BYTES) / elapsed / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(elapsed * 1e3, 3),
-            "api": "VQDevice.matmul_dense_grouped (C ABI ack_vq2, host buffers)"}
+            "api": "VQDevice.matmul_dense_grouped on a ResidentStack (C ABI ack_vq2; weights resident, "
+                   "X in and Y out through pinned host memory every step)"}
 
 
 def _timed(torch, fn, steps, warmup, world, device, local):
@@ -387,7 +392,8 @@ def run_codec(args, world, rank, local, which):
     algorithmic = 4 * n + code_bytes + 64 * group
     peak = measured_peaks().get("hbm_gbs") or 6650.0
     achieved = algorithmic / (ms / 1e3) / 1e9
-    kernel = "k_encode" if which == "encode" else "k_decode"
+    # x from torch is 16-byte aligned: group 32 runs the cp.async variant
+    kernel = ("k_encode_async" if group == 32 else "k_encode") if which == "encode" else "k_decode"
     result = {
         "metric": f"vq4 {which} Gvalues/s (cfg5, 2^30 values, g{group}, {args.dist})",
         "value": round(world * n / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
@@ -398,7 +404,8 @@ def run_codec(args, world, rank, local, which):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"{kernel}_cfg5_g{group}"),
                      "kernel": kernel, "algorithmic_bytes_per_launch": algorithmic},
-        "gpu_launches": args.steps, "clocks": clocks,
+        # encode: the book-staging kernel and the encode kernel per step
+        "gpu_launches": args.steps * (2 if which == "encode" else 1), "clocks": clocks,
     }
     if rank == 0 and not args.no_cpu:
         sys.path.insert(0, str(ROOT / "oracle"))

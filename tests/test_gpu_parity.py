@@ -221,6 +221,33 @@ def test_dense_matches_cfg2_shapes(backend):
 
 
 @pytest.mark.parametrize("group", [8, 16, 32])
+def test_resident_stack_is_the_uploaded_product_bit_for_bit(backend, group):
+    """Weights made resident once (tile32 repack on the device, or the wire
+    layout) give the same bits as the per-call product, call after call,
+    into a caller's output array too; ragged N exercises the padded tile."""
+    rng = np.random.default_rng(300 + group)
+    e, n, k = 3, 517, 64 * group
+    ws = [VQArray((n, k), group, o.pack(rng.integers(0, 16, n * k // group)), rand_book(rng, group, 0.05))
+          for _ in range(e)]
+    stack = vq.VQStack.from_arrays(ws)
+    for m in (1, 3):
+        x = rng.standard_normal((e, m, k)).astype(np.float32)
+        want = backend.matmul_dense_grouped(x, stack)
+        for layout in ("tile32", "canonical"):
+            with backend.resident(stack, layout=layout) as weights:
+                assert len(weights) == e
+                out = np.empty((e, m, n), dtype=np.float32)
+                for _ in range(2):
+                    got = backend.matmul_dense_grouped(x, weights, out=out)
+                    assert got is out
+                    np.testing.assert_array_equal(bits(got), bits(want))
+                np.testing.assert_array_equal(bits(backend.matmul_dense_grouped(x, weights)), bits(want))
+    with pytest.raises(ValueError, match="tile32"):
+        backend.resident(vq.VQStack.from_arrays(
+            [VQArray((n, 40 * group), group, o.pack(rng.integers(0, 16, n * 40)), rand_book(rng, group))]))
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
 def test_coded_product_within_tolerance(backend, group):
     rng = np.random.default_rng(200 + group)
     for (m, n, k, flags) in ((70, 300, 16 * group, 2), (64, 256, 8 * group, 2), (5, 9, 3 * group, 2),
