@@ -736,6 +736,54 @@ ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const Ack
   return ACK_OK;
 }
 
+// ---------------------------------------------- encode without allocation --
+// For callers that may not allocate device memory themselves or through this
+// library: the caller passes device pointers to x, the books, the codes and
+// a cleared status word; the only scratch is the library's static array.
+
+ACK_EXPORT int32_t ack_vq_encode_noalloc(const float* x, uint64_t count, uint32_t batch, const float* books,
+                                         uint32_t group, uint32_t* codes, uint32_t* status, void* stream) {
+  const char* entry = "vq-encode-noalloc";
+  if (!x || !books || !codes || !status) {
+    set_error(format("%s: null pointer", entry));
+    return ACK_ERR_NULL;
+  }
+  if (group != 8 && group != 16 && group != 32) {
+    set_error(format("%s: group %u is not 8, 16 or 32", entry, group));
+    return ACK_ERR_SHAPE;
+  }
+  if (count == 0 || count > (uint64_t(1) << 40)) {
+    set_error(format("%s: %llu values per tensor (1 to 2^40 accepted)", entry, (unsigned long long)count));
+    return ACK_ERR_SHAPE;
+  }
+  if (batch == 0 || batch > ack::kStaticEncodeBooks) {
+    set_error(format("%s: batch of %u tensors exceeds the %u books its static scratch holds", entry, batch,
+                     ack::kStaticEncodeBooks));
+    return ACK_ERR_SIZE;
+  }
+  const uintptr_t px = reinterpret_cast<uintptr_t>(x), pb = reinterpret_cast<uintptr_t>(books),
+                  pc = reinterpret_cast<uintptr_t>(codes), ps = reinterpret_cast<uintptr_t>(status);
+  if ((px | pb | pc | ps) & 3u) {
+    set_error(format("%s: pointers must be 4-byte aligned", entry));
+    return ACK_ERR_SHAPE;
+  }
+  // written ranges (codes, status) disjoint from every other range
+  const uint64_t words = ack::packed_words(count, group);
+  const uint64_t rx[2] = {px, px + uint64_t(batch) * count * 4}, rb[2] = {pb, pb + uint64_t(batch) * 16 * group * 4};
+  const uint64_t rc[2] = {pc, pc + uint64_t(batch) * words * 4}, rs[2] = {ps, ps + 4};
+  auto overlap = [](const uint64_t* a, const uint64_t* b) { return a[0] < b[1] && b[0] < a[1]; };
+  if (overlap(rc, rx) || overlap(rc, rb) || overlap(rc, rs) || overlap(rs, rx) || overlap(rs, rb)) {
+    set_error(format("%s: the codes or the status word overlap another operand", entry));
+    return ACK_ERR_SHAPE;
+  }
+  cudaError_t ce = ack::encode_noalloc(x, count, batch, books, group, codes, status, static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) {
+    set_error(format("%s: launch: %s (%s)", entry, cudaGetErrorName(ce), cudaGetErrorString(ce)));
+    return ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
 // ------------------------------------------------------- planner probes --
 
 ACK_EXPORT int32_t ack_vq_plan_probe(const uint8_t* plan, size_t plan_len, uint64_t required_bytes[8],

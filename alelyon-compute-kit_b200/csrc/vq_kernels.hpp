@@ -12,4 +12,13 @@ namespace ack {
 // have passed admission; pointers are device addresses in slot order.
 cudaError_t launch(const Plan& plan, void* const* ptr, cudaStream_t stream);
 
+// Books one ack_vq_encode_noalloc call may encode with (its static scratch).
+constexpr uint32_t kStaticEncodeBooks = 64;
+
+// Encode `batch` tensors of `n` values (x: batch x n floats, books: batch x
+// 16 x group, codes: batch x words(n) u32) using only the library's static
+// scratch; the caller has validated the arguments.
+cudaError_t encode_noalloc(const float* x, uint64_t n, uint32_t batch, const float* books, uint32_t group,
+                           uint32_t* codes, uint32_t* status, cudaStream_t stream);
+
 }  // namespace ack

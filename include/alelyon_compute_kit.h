@@ -240,6 +240,26 @@ typedef struct AckVqOperands {
 } AckVqOperands;
 int32_t ack_vq_launch(const uint8_t *plan, size_t plan_len, const AckVqOperands *ops, void *stream);
 
+/* Encode without any allocation. No counterpart in the reference: an entry
+ * for callers that cannot allocate device memory, because their host owns
+ * every device allocation (an engine or server with its own allocator) or
+ * because an allocation at that point would stall or be refused. It encodes
+ * `batch` tensors of `count` values each (x: batch x count floats, books:
+ * batch x 16 x group, codes: batch x ceil(ceil(count/group)/8) u32 words,
+ * status: one u32 the caller has cleared), all device pointers, 4-byte
+ * aligned, on `stream` (a cudaStream_t) of the current device; the codes are
+ * the bytes ack_vq_launch's encode (op 21) produces. The only device memory
+ * it uses besides these is a fixed 139,264-byte array in the library, held
+ * by every GPU that loads it until exit, which limits a call to batch <= 64
+ * (ACK_ERR_SIZE beyond). The first call on a device looks that array's
+ * address up (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call shares the array: calls that may overlap on the GPU
+ * (other streams, other threads) race and must be serialised by the caller.
+ * ACK_ERR_NULL / ACK_ERR_SHAPE for null, misaligned or overlapping operands
+ * and a group other than 8, 16, 32. */
+int32_t ack_vq_encode_noalloc(const float *x, uint64_t count, uint32_t batch, const float *books, uint32_t group,
+                              uint32_t *codes, uint32_t *status, void *stream);
+
 /* ---- host-only planner introspection (the public methods of the
  * reference's VqPlan, vq4_ops.rs:111-243, which its Rust tests call
  * directly). No device is touched. Each returns ACK_OK or the code ack_vq
