@@ -547,8 +547,13 @@ __global__ void __launch_bounds__(kThreads) k_repack_tile32(const uint4* __restr
 // expert count. Per expert segment of its range and per (m, t)-chunk a block
 // builds the table once: the chunk of X arrives in shared memory in one
 // round trip, lane e % 16 holds book row e in registers and a half-warp
-// computes the 16 entries of one group, stored as one contiguous 64-byte row
-// (conflict-free).
+// computes the 16 entries of one group.
+//
+// The table is P[t][m / 2][e][m % 2]: rows of X in pairs side by side per
+// entry, so one 8-byte shared load fetches an entry for two rows (a
+// half-warp phase of 16 distinct 8-byte entries is conflict-free; 16-byte
+// loads measured slower, their quarter-warp phases conflict). The nibble
+// masks yield 4 idx (MC = 1) or 8 idx (MC > 1) directly in each byte.
 template <int G, int MC, int TC>
 __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restrict__ X,
                                                            const uint4* __restrict__ codes,
@@ -557,7 +562,8 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
                                                            uint64_t units_per_expert, uint32_t* __restrict__ status) {
   constexpr int kPieces = TC / 32;
   extern __shared__ __align__(16) unsigned char smem[];
-  float* P = reinterpret_cast<float*>(smem);  // [MC][TC][16]
+  static_assert(MC == 1 || MC == 2 || MC == 4, "one table load covers MC rows");
+  float* P = reinterpret_cast<float*>(smem);  // [TC][MC/2][16][2], or [TC][16] for MC = 1
   float* Xs = P + MC * TC * 16;                // [TC * G]: one row's X chunk
   const uint32_t T = K / G, ct = T / 32;
   const uint32_t ntiles = (N + 31) / 32;
@@ -610,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
               acc = fmaf(v.z, brow[4 * q + 2], acc);
               acc = fmaf(v.w, brow[4 * q + 3], acc);
             }
-            P[(size_t(m) * TC + t) * 16 + (lane & 15)] = acc;
+            P[size_t(t) * 16 * MC + (MC == 1 ? (lane & 15) : (m >> 1) * 32 + (lane & 15) * 2 + (m & 1))] = acc;
           }
         }
         __syncthreads();
@@ -630,18 +636,32 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
             const uint32_t wd[4] = {q[pc].x, q[pc].y, q[pc].z, q[pc].w};
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
-              const uint32_t lo = (wd[wi] << 2) & 0x3C3C3C3Cu;  // 4 * nibbles 0, 2, 4, 6
-              const uint32_t hi = (wd[wi] >> 2) & 0x3C3C3C3Cu;  // 4 * nibbles 1, 3, 5, 7
+              // 4 MC * nibble of the even (lo) and odd (hi) nibbles, one per byte
+              const uint32_t w = wd[wi];
+              const uint32_t lo = MC == 1 ? (w << 2) & 0x3C3C3C3Cu : (w << 3) & 0x78787878u;
+              const uint32_t hi = MC == 1 ? (w >> 2) & 0x3C3C3C3Cu : (w >> 1) & 0x78787878u;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t olo = __byte_perm(lo, 0, 0x4440 + kk);
                 const uint32_t ohi = __byte_perm(hi, 0, 0x4440 + kk);
                 const int t = pc * 32 + wi * 8 + 2 * kk;
+                const unsigned char* pt = Pb + size_t(t) * 64 * MC;  // row t of the table
+                float vl[MC], vh[MC];
+                if constexpr (MC == 1) {
+                  vl[0] = *reinterpret_cast<const float*>(pt + olo);
+                  vh[0] = *reinterpret_cast<const float*>(pt + 64 + ohi);
+                } else {
+#pragma unroll
+                  for (int mp = 0; mp < MC / 2; ++mp) {
+                    const float2 a = *reinterpret_cast<const float2*>(pt + mp * 128 + olo);
+                    const float2 b = *reinterpret_cast<const float2*>(pt + 64 * MC + mp * 128 + ohi);
+                    vl[2 * mp] = a.x; vl[2 * mp + 1] = a.y; vh[2 * mp] = b.x; vh[2 * mp + 1] = b.y;
+                  }
+                }
 #pragma unroll
                 for (int m = 0; m < MC; ++m) {
-                  const unsigned char* pm = Pb + (size_t(m) * TC + t) * 64;
-                  acc[m][(2 * kk) & 3] += *reinterpret_cast<const float*>(pm + olo);
-                  acc[m][(2 * kk + 1) & 3] += *reinterpret_cast<const float*>(pm + 64 + ohi);
+                  acc[m][(2 * kk) & 3] += vl[m];
+                  acc[m][(2 * kk + 1) & 3] += vh[m];
                 }
               }
             }
@@ -1246,8 +1266,9 @@ template <int G, int MC>
 cudaError_t launch_dense_mc(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t M,
                             uint32_t N, uint32_t K, uint32_t batch, uint64_t words, uint32_t* status, cudaStream_t s) {
   const uint32_t T = K / G;
+  // t-chunk sizes (the tile32 launcher uses the same, so both layouts sum alike)
   if (MC <= 2 && T % 256 == 0) return launch_dense_lut<G, MC, (MC <= 2 ? 256 : 128)>(X, codes, books, Y, M, N, K, batch, words, status, s);
-  if (MC > 2 && T % 128 == 0) return launch_dense_lut<G, MC, 128>(X, codes, books, Y, M, N, K, batch, words, status, s);
+  if (T % 128 == 0) return launch_dense_lut<G, MC, 128>(X, codes, books, Y, M, N, K, batch, words, status, s);
   return launch_dense_lut<G, MC, 32>(X, codes, books, Y, M, N, K, batch, words, status, s);
 }
 
@@ -1270,6 +1291,8 @@ cudaError_t launch_dense_t32(const float* X, const uint4* codes, const float* bo
 template <int G, int MC>
 cudaError_t launch_t32_mc(const float* X, const uint4* codes, const float* books, float* Y, uint32_t M, uint32_t N,
                           uint32_t K, uint32_t batch, uint32_t* status, cudaStream_t s) {
+  // the t-chunk sizes of the canonical path for the same M (the per-row sums
+  // then match it bit for bit): 256 groups for M <= 2, 128 beyond
   const uint32_t T = K / G;
   if (T % 256 == 0 && MC <= 2) return launch_dense_t32<G, MC, (MC <= 2 ? 256 : 128)>(X, codes, books, Y, M, N, K, batch, status, s);
   if (T % 128 == 0) return launch_dense_t32<G, MC, 128>(X, codes, books, Y, M, N, K, batch, status, s);
@@ -1292,8 +1315,7 @@ struct RunDense {
       const uint4* c4 = reinterpret_cast<const uint4*>(codes);
       if (M == 1) return launch_t32_mc<G, 1>(X, c4, books, Y, M, N, K, p.batch, status, s);
       if (M == 2) return launch_t32_mc<G, 2>(X, c4, books, Y, M, N, K, p.batch, status, s);
-      if (M <= 4) return launch_t32_mc<G, 4>(X, c4, books, Y, M, N, K, p.batch, status, s);
-      return launch_t32_mc<G, 8>(X, c4, books, Y, M, N, K, p.batch, status, s);
+      return launch_t32_mc<G, 4>(X, c4, books, Y, M, N, K, p.batch, status, s);  // M > 4: chunks of 4 rows
     }
     if (nt && K % G == 0 && (K / G) % 32 == 0 && aligned16(codes) && (words * 4) % 16 == 0) {
       if (M == 1) return launch_dense_mc<G, 1>(X, codes, books, Y, M, N, K, p.batch, words, status, s);

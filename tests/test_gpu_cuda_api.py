@@ -104,7 +104,8 @@ def test_concurrent_encodes_with_different_books_on_many_streams():
 def test_tile32_layout_is_bitwise_the_canonical_product(group):
     rng = np.random.default_rng(group + 3)
     for (e, m, n, k) in ((3, 1, 1000, 32 * group), (2, 3, 517, 256 * group), (2, 8, 64, 128 * group),
-                         (1, 16, 333, 32 * group)):
+                         (1, 16, 333, 32 * group), (2, 1, 300, 128 * group), (2, 2, 77, 384 * group),
+                         (1, 5, 129, 64 * group)):
         codes = np.stack([o.pack(rng.integers(0, 16, n * k // group)) for _ in range(e)])
         books = rng.standard_normal((e, 16, group)).astype(np.float32)
         x = rng.standard_normal((e, m, k)).astype(np.float32)
