@@ -21,7 +21,7 @@ from . import ack
 
 ENTRIES = 16
 OP_ENCODE1, OP_DECODE1, OP_MATMUL1, OP_ADAMW1 = 0, 1, 2, 3
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK = range(16, 24)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT = range(16, 25)
 
 
 def words_for(count: int, group: int) -> int:
@@ -186,3 +186,25 @@ def adamw_encode(codes, books, coefs, new_books, count: int, group: int, *, batc
     launch(plan2(OP_ADAMW_ENCODE, count, 1, 1, group, batch=batch),
            [codes, books, coefs, new_books, None, out, changed, status])
     return out, changed, status
+
+
+def fit_workspace_bytes(samples: int) -> int:
+    """Workspace bytes of `adamw_fit` per fitted book."""
+    return (samples + 15) // 16 * 16 + 160
+
+
+def adamw_fit(codes, books, coefs, samples, count: int, group: int, *, iterations: int = 4, batch: int = 1, out=None,
+              workspace=None, status=None):
+    """fit_codebook of W', M', V' for each expert on the device, warm-started
+    from the current books: `samples` is `adamw_sample`'s output (E, 3, S,
+    group); returns the fitted books (E, 3, 16, group), bit for bit the CPU
+    fit of the same sample."""
+    s = samples.shape[2]
+    dev = codes.device
+    out = torch.empty((batch, 3, ENTRIES, group), dtype=torch.float32, device=dev) if out is None else out
+    if workspace is None:
+        workspace = torch.empty(batch * 3 * fit_workspace_bytes(s), dtype=torch.uint8, device=dev)
+    status = status_word(dev) if status is None else status
+    launch(plan2(OP_FIT, count, 1, 1, group, flags=1, batch=batch, aux0=s, aux1=iterations),
+           [codes, books, coefs, samples, workspace, out, None, status])
+    return out, status

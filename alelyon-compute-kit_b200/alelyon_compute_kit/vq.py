@@ -42,7 +42,8 @@ _HEADER = struct.Struct("<8sIIIIQQ")
 _MAGIC = b"ACKVQ4\0\0"
 
 # schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK = range(16, 24)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT = \
+    range(16, 25)
 
 
 def _integer(value, name: str, minimum: int, maximum: int) -> int:
@@ -657,15 +658,18 @@ class VQDevice:
 
     def adamw_fused(self, weight: VQArray, momentum: VQArray, variance: VQArray, gradient: VQArray, *,
                     lr: float, beta1: float, beta2: float, eps: float, weight_decay: float, step: int,
-                    sample_vectors: int = 4096, iterations: int = 4):
+                    sample_vectors: int = 4096, iterations: int = 4, fit: str = "host"):
         """One VQAdamW step without FP32 scratch: the device computes the
         AdamW values of the calibration sample (the same values op 3 would
         produce), `fit_codebook`'s Lloyd iterations run on the CPU with the
-        whole-tensor entry check answered by the device, then one device pass
-        decodes, updates and re-encodes W, M and V with the fitted books.
+        whole-tensor entry check answered by the device (fit="host"), or on
+        the device, bit for bit the same books (fit="device"), then one device
+        pass decodes, updates and re-encodes W, M and V with the fitted books.
 
         Returns ((W', M', V') as VQArrays, changed weight values, bytes the
         device produced)."""
+        if fit not in ("host", "device"):
+            raise ValueError(f"fit must be 'host' or 'device', not {fit!r}")
         states = (weight, momentum, variance, gradient)
         coefficients = _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step)
         group = weight.group
@@ -701,6 +705,19 @@ class VQDevice:
             cleanup.callback(sample_out.free)
             self._launch2(self._plan2(OP_ADAMW_SAMPLE, count, 1, 1, group, batch=1, aux0=s),
                           [b_codes, b_books, b_coefs, b_pos, None, sample_out, None, status])
+            if fit == "device":
+                stride = ((s + 15) // 16 * 16 + 160)
+                workspace = device.buffer(3 * stride)
+                cleanup.callback(workspace.free)
+                b_new = device.buffer(3 * ENTRIES * group * 4)
+                cleanup.callback(b_new.free)
+                self._launch2(self._plan2(OP_FIT, count, 1, 1, group, flags=1, batch=1, aux0=s, aux1=iterations),
+                              [b_codes, b_books, b_coefs, sample_out, workspace, b_new, None, status])
+                check()
+                new_books = b_new.download(np.float32).reshape(3, ENTRIES, group)
+                produced = new_books.nbytes
+                return self._adamw_encode(weight, count, group, words, b_codes, b_books, b_coefs, b_new, new_books,
+                                          status, check, cleanup, produced)
             check()
             samples = sample_out.download(np.float32).reshape(3, s, group)
 
@@ -720,17 +737,25 @@ class VQDevice:
                 fitted.append(_fit(samples[which], complete, group, iterations, state.codebook, whole_usage))
             new_books = np.ascontiguousarray(np.stack(fitted), dtype=np.float32)
             b_new = buffer_of(new_books)
-            out_codes = device.buffer(3 * words * 4)
-            cleanup.callback(out_codes.free)
-            changed = device.buffer(4)
-            cleanup.callback(changed.free)
-            self._launch2(self._plan2(OP_ADAMW_ENCODE, count, 1, 1, group, batch=1),
-                          [b_codes, b_books, b_coefs, b_new, None, out_codes, changed, status])
-            check()
-            image = out_codes.download(np.uint32).reshape(3, words)
-            n_changed = int(changed.download(np.uint32)[0])
+            return self._adamw_encode(weight, count, group, words, b_codes, b_books, b_coefs, b_new, new_books,
+                                      status, check, cleanup, samples.nbytes)
+
+    def _adamw_encode(self, weight, count, group, words, b_codes, b_books, b_coefs, b_new, new_books, status, check,
+                      cleanup, produced):
+        """The fused step's last pass: decode, update and re-encode W, M, V
+        with the fitted books `b_new` (device) / `new_books` (host copy)."""
+        device = self.device
+        out_codes = device.buffer(3 * words * 4)
+        cleanup.callback(out_codes.free)
+        changed = device.buffer(4)
+        cleanup.callback(changed.free)
+        self._launch2(self._plan2(OP_ADAMW_ENCODE, count, 1, 1, group, batch=1),
+                      [b_codes, b_books, b_coefs, b_new, None, out_codes, changed, status])
+        check()
+        image = out_codes.download(np.uint32).reshape(3, words)
+        n_changed = int(changed.download(np.uint32)[0])
         encoded = tuple(VQArray(weight.shape, group, image[i], new_books[i]) for i in range(3))
-        return encoded, n_changed, samples.nbytes + image.nbytes
+        return encoded, n_changed, produced + image.nbytes
 
 
 def _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step) -> np.ndarray:
@@ -758,7 +783,14 @@ class VQAdamW:
     are refitted on the CPU; re-encoding is lossy. A failed step leaves the
     three state images and the step counter unchanged."""
 
-    def __init__(self, backend, weight: VQArray, *, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0):
+    def __init__(self, backend, weight: VQArray, *, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0,
+                 fit: str = "host"):
+        """`fit` chooses where a backend with the fused step (`adamw_fused`)
+        refits the codebooks: "host" (the CPU, as the reference) or "device"
+        (the same books bit for bit, computed on the GPU)."""
+        if fit not in ("host", "device"):
+            raise ValueError(f"fit must be 'host' or 'device', not {fit!r}")
+        self.fit = fit
         self.backend = backend
         self.weight = weight
         zeros = np.zeros_like(weight.codes)
@@ -774,7 +806,8 @@ class VQAdamW:
         if fused is not None:
             encoded, changed, produced = fused(
                 self.weight, self.momentum, self.variance, gradient, lr=self.lr, beta1=self.betas[0],
-                beta2=self.betas[1], eps=self.eps, weight_decay=self.weight_decay, step=next_step)
+                beta2=self.betas[1], eps=self.eps, weight_decay=self.weight_decay, step=next_step,
+                **({"fit": self.fit} if self.fit != "host" else {}))
             encoded = list(encoded)
         else:
             scratch = self.backend.adamw(self.weight, self.momentum, self.variance, gradient,
@@ -795,5 +828,6 @@ class VQAdamW:
                 "persistent_state_bytes": sum(s.layout["serialized_bytes"] for s in encoded),
                 "gradient_bytes": gradient.layout["serialized_bytes"],
                 "native_update_output_bytes": produced,
-                "calibration": "CPU float32/float64 temporary arrays",
+                "calibration": ("device float32/float64, bit for bit the CPU fit" if fused is not None and self.fit == "device"
+                                else "CPU float32/float64 temporary arrays"),
                 "model_quality_validated": False}

@@ -717,7 +717,9 @@ ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const Ack
   for (int i = 0; i < n; ++i)
     if (p.required[i] && (ids[i] & 3u)) return plan_refused(entry, ack::PlanError::Misaligned, 2, i);
   const int first_out = p.first_output();
-  for (int o = first_out; o < n; ++o) {
+  // the fit's workspace (in4) is written too
+  const int first_written = (p.schema == 2 && p.op == ack::Op::AdamwFit) ? 4 : first_out;
+  for (int o = first_written; o < n; ++o) {
     if (!p.required[o]) continue;
     for (int i = 0; i < n; ++i) {
       if (i == o || !p.required[i]) continue;

@@ -92,7 +92,7 @@ constexpr uint32_t kMaxSamples = 65536;         // fit_codebook's sample bound (
 PlanError parse_schema2(Plan* p) {
   const auto& w = p->words;
   uint32_t op = w[0], group = w[4], entries = w[5], flags = w[6], reserved = w[7];
-  if (op < 16 || op > 23) return PlanError::Operation;
+  if (op < 16 || op > 24) return PlanError::Operation;
   if (!valid_group(group)) return PlanError::Group;
   if (entries != kEntries) return PlanError::Entries;
   if (reserved != 0 || w[12] || w[13] || w[14] || w[15]) return PlanError::Reserved;
@@ -172,6 +172,21 @@ PlanError parse_schema2(Plan* p) {
       }
       break;
     }
+    case Op::AdamwFit: {
+      // fit_codebook (vq.py:182-257) of W', M', V' on the device, warm-started
+      // from the current books (flag bit 0, the VQAdamW case): aux0 sample
+      // vectors (op 18's output), aux1 Lloyd iterations.
+      if (flags != 1u) return PlanError::Flags;
+      if (!p->m || p->n != 1 || p->k != 1) return PlanError::Geometry;
+      if (p->m > kMaxValues) return PlanError::AddressLimit;
+      if (!E) return PlanError::Batch;
+      if (!p->aux0 || p->aux0 > kMaxSamples || p->aux0 > p->m / group || p->aux1 > 32 || p->aux2)
+        return PlanError::Aux;
+      const uint64_t words = packed_bytes(p->m, group);
+      p->required = {E * 4 * words, E * 4 * book, E * 7 * 4, E * 3 * uint64_t(p->aux0) * group * 4,
+                     E * 3 * fit_workspace_stride(p->aux0), E * 3 * book, 0, 4};
+      break;
+    }
     case Op::EncodeLarge:
     case Op::DecodeLarge: {
       if (flags) return PlanError::Flags;
@@ -241,8 +256,9 @@ PlanError validate_buffers(const Plan& p, const uint64_t* capacities, const uint
       *slot = i;
       return PlanError::Capacity;
     }
-  for (int o = 5; o < 7; ++o) {
-    if (!p.required[o]) continue;
+  // written: out0, out1, and in4 for the fit (its workspace)
+  for (int o = 4; o < 7; ++o) {
+    if (!p.required[o] || (o == 4 && p.op != Op::AdamwFit)) continue;
     for (int i = 0; i < n; ++i)
       if (i != o && p.required[i] && ids[i] == ids[o] && i != 7) return PlanError::OutputAlias;
   }

@@ -21,7 +21,7 @@ constexpr int kSlots = 8;                        // schema 2; schema 1 uses the 
 enum class Op : uint32_t {
   Encode = 0, Decode = 1, Matmul = 2, AdamW = 3,
   Dense = 16, Coded = 17, AdamwSample = 18, AdamwUsage = 19, AdamwEncode = 20,
-  EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23,
+  EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23, AdamwFit = 24,
 };
 
 // Refusals. The schema-1 names are vq4_ops.rs:66-84; the schema-2 ones are
@@ -66,6 +66,11 @@ inline uint64_t packed_words(uint64_t values, uint32_t group) { return packed_by
 inline uint64_t tile32_bytes(uint64_t rows, uint64_t cols, uint32_t group) {
   return (rows + 31) / 32 * 32 * (cols / group) / 2;
 }
+
+// Workspace of the device codebook fit (op 24) per fitted book: the sample's
+// nearest entries (one byte each, padded to 16), entry counts, whole-tensor
+// usage counts and a flag word.
+inline uint64_t fit_workspace_stride(uint32_t samples) { return (uint64_t(samples) + 15) / 16 * 16 + 160; }
 
 // Parse a plan block (32 bytes: schema 1, 64 bytes: schema 2). `slot` receives
 // the offending slot for Capacity.

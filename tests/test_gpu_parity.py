@@ -305,6 +305,40 @@ def test_fused_vqadamw_step_matches_the_reference_flow(backend, shape, group):
         assert r_dev["step"] == r_host["step"]
 
 
+@pytest.mark.parametrize("shape,group,sample", [((37, 29), 8, 4096), ((256, 256), 16, 4096),
+                                                ((1024, 512), 32, 4096), ((4096, 1024), 8, 4096),
+                                                ((512, 384), 16, 1000)])
+def test_device_fit_is_the_cpu_fit_bit_for_bit(backend, shape, group, sample):
+    """fit="device" (op 24) against fit="host" (the CPU Lloyd iterations) on
+    the same steps: step 1 starts the moments from all-zero books (every
+    entry but one empty: reseeds), later steps warm-start; a sample smaller
+    than the tensor exercises the whole-tensor kept-entry rule."""
+    rng = np.random.default_rng(sum(shape) + group + sample)
+    w = o.gaussian(shape, 0.02, 7)
+    weight = vq.encode(w, vq.fit_codebook(w, group=group), group=group)
+    opts = {fit: VQAdamW(backend, weight, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, fit=fit)
+            for fit in ("host", "device")}
+    for _ in range(3):
+        g = (rng.standard_normal(shape) * 1e-3).astype(np.float32)
+        gimg = vq.encode(g, vq.fit_codebook(g, group=group), group=group)
+        reports = {}
+        for fit, opt in opts.items():
+            if sample != 4096:
+                encoded, changed, _ = backend.adamw_fused(opt.weight, opt.momentum, opt.variance, gimg, lr=1e-3,
+                                                          beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
+                                                          step=opt.steps + 1, sample_vectors=sample, fit=fit)
+                opt.weight, opt.momentum, opt.variance = encoded
+                opt.steps += 1
+                reports[fit] = changed
+            else:
+                reports[fit] = opt.step(gimg)["changed_weight_values"]
+        h, d = opts["host"], opts["device"]
+        for a, b in ((h.weight, d.weight), (h.momentum, d.momentum), (h.variance, d.variance)):
+            np.testing.assert_array_equal(bits(a.codebook), bits(b.codebook))
+            assert a.to_bytes() == b.to_bytes()
+        assert reports["host"] == reports["device"]
+
+
 @pytest.mark.parametrize("group,rare_at", [(8, -1), (16, -1), (32, -1), (8, 1)])
 def test_fused_zero_gradient_moves_no_weight(backend, group, rare_at):
     """The reference audit's acceptance test on the device path; with the
@@ -316,11 +350,12 @@ def test_fused_zero_gradient_moves_no_weight(backend, group, rare_at):
     values = atoms[index].reshape(-1)
     weight = vq.encode(values, atoms, group=group)
     zero = VQArray(weight.shape, group, np.zeros_like(weight.codes), np.zeros((16, group), np.float32))
-    opt = VQAdamW(backend, weight, lr=1e-3, weight_decay=0.0)
-    before = opt.weight.decode().copy()
-    report = opt.step(zero)
-    assert report["changed_weight_values"] == 0 == int((before != opt.weight.decode()).sum())
-    assert len(np.unique(opt.weight.codebook.round(6), axis=0)) == 16
+    for fit in ("host", "device"):
+        opt = VQAdamW(backend, weight, lr=1e-3, weight_decay=0.0, fit=fit)
+        before = opt.weight.decode().copy()
+        report = opt.step(zero)
+        assert report["changed_weight_values"] == 0 == int((before != opt.weight.decode()).sum())
+        assert len(np.unique(opt.weight.codebook.round(6), axis=0)) == 16
 
 
 def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device):
