@@ -469,8 +469,12 @@ def run_cfg3(args, world, rank, local):
 
 
 def run_cfg4(args, world, rank, local):
-    """cfg 4: the fused coded-state AdamW pass over 8 experts per GPU, each
-    W, M, V of 4096 x 1024 g8, with fitted books (kernel-only timing)."""
+    """cfg 4: the VQAdamW step of 8 experts per GPU, each W, M, V of
+    4096 x 1024 g8 with a coded gradient: the AdamW values of the
+    calibration sample (op 18), fit_codebook of W', M', V' on the device
+    (op 24, bit for bit the CPU fit), then decode -> AdamW -> encode of all
+    three states (op 20). The whole step is device-timed; the encode pass
+    alone is reported beside it."""
     import torch
 
     from alelyon_compute_kit import cuda, vq
@@ -495,27 +499,85 @@ def run_cfg4(args, world, rank, local):
             cuda.encode(v, b, group, out=codes[e, s], status=status)
     coefs = torch.from_numpy(np.tile(np.array([1e-3, 0.9, 0.999, 1e-8, 0.01, 1 - 0.9 ** 2, 1 - 0.999 ** 2],
                                               np.float32), (experts, 1))).to(device)
-    new_books = books[:, :3].contiguous()
+    positions = torch.from_numpy(np.linspace(0, count // group - 1, 4096, dtype=np.int64).astype(np.uint32)
+                                 .view(np.int32)).to(device)
+    samples = torch.empty((experts, 3, 4096, group), dtype=torch.float32, device=device)
+    new_books = torch.empty((experts, 3, 16, group), dtype=torch.float32, device=device)
+    workspace = torch.empty(experts * 3 * cuda.fit_workspace_bytes(4096), dtype=torch.uint8, device=device)
     out = torch.empty((experts, 3, words), dtype=torch.int32, device=device)
     changed = torch.empty(experts, dtype=torch.int32, device=device)
-    fn = lambda: cuda.adamw_encode(codes, books, coefs, new_books, count, group, batch=experts,  # noqa: E731
-                                   out=out, changed=changed, status=status)
-    ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
+
+    def step():
+        cuda.adamw_sample(codes, books, coefs, positions, count, group, batch=experts, out=samples, status=status)
+        cuda.adamw_fit(codes, books, coefs, samples, count, group, iterations=4, batch=experts, out=new_books,
+                       workspace=workspace, status=status)
+        cuda.adamw_encode(codes, books, coefs, new_books, count, group, batch=experts, out=out, changed=changed,
+                          status=status)
+
+    encode_pass = lambda: cuda.adamw_encode(codes, books, coefs, new_books, count, group,  # noqa: E731
+                                            batch=experts, out=out, changed=changed, status=status)
+    ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local)
+    cuda.check(status)
+    ms_encode, _ = _timed(torch, encode_pass, args.steps, args.warmup, world, device, local)
     cuda.check(status)
     byts = codes.numel() * 4 + out.numel() * 4
     peak = measured_peaks().get("hbm_gbs") or 6650.0
-    return {
-        "metric": "vq4 fused VQAdamW update Gvalues/s (cfg4, 3 x 4096x1024 g8 per expert, kernel only)",
+    result = {
+        "metric": "vq4 VQAdamW step Gvalues/s (cfg4, 3 x 4096x1024 g8 per expert: sample, device fit, re-encode)",
         "value": round(world * experts * count / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg4-adamw-encode", "experts_per_gpu": experts, "rows": rows, "cols": cols,
-                   "group": group, "parallelism": f"expert-sharded x{world}, no collective"},
-        "roofline": {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "k_adamw_encode",
-                     "note": "compute-bound (three certified 16-entry searches per value)"},
-        "gpu_launches": args.steps, "clocks": clocks,
+        "config": {"workload": "cfg4-vqadamw-step", "experts_per_gpu": experts, "rows": rows, "cols": cols,
+                   "group": group, "sample_vectors": 4096, "fit_iterations": 4, "fit": "device",
+                   "parallelism": f"expert-sharded x{world}, no collective"},
+        "encode_pass": {"ms": round(ms_encode, 4),
+                        "gvalues_per_s": round(world * experts * count / (ms_encode / 1e3) / 1e9, 3)},
+        "roofline": {"bound": "hbm", "achieved": round(byts / (ms_encode / 1e3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(byts / (ms_encode / 1e3) / 1e9 / peak, 4), "traffic": None,
+                     "kernel": "k_adamw_encode",
+                     "note": "compute-bound (three certified 16-entry searches per value); coded bytes only"},
+        # per step: sample 1, fit 1 + 4 x 3, encode pass 2 per expert (book staging + pass)
+        "gpu_launches": args.steps * (1 + 13 + 2 * experts), "clocks": clocks,
     }
+    if rank == 0 and not args.no_e2e:
+        result["e2e"] = run_cfg4_e2e(args, torch, vq, codes, books, experts, count, group, local)
+    return result
+
+
+def run_cfg4_e2e(args, torch, vq, codes, books, experts, count, group, local):
+    """VQAdamW.step through the public API with host VQArrays (every step
+    uploads W, M, V, G and downloads W', M', V'): fit on the device, and one
+    step with the CPU fit beside it."""
+    from alelyon_compute_kit import ack
+    host_codes = codes.cpu().numpy().view(np.uint32)
+    host_books = books.cpu().numpy()
+    shape = (4096, 1024)
+    arrays = [[vq.VQArray(shape, group, host_codes[e, s], host_books[e, s]) for s in range(4)] for e in range(experts)]
+    os.environ.setdefault("ACK_DEVICE", f"gpu:{local}")
+    timings = {}
+    with ack.Device() as dev:
+        backend = vq.VQDevice(dev)
+        for fit, steps in (("device", max(3, min(args.steps, 5))), ("host", 1)):
+            opts = []
+            for e in range(experts):
+                opt = vq.VQAdamW(backend, arrays[e][0], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                                 fit=fit)
+                opt.momentum, opt.variance, opt.steps = arrays[e][1], arrays[e][2], 1
+                opts.append(opt)
+            if fit == "device":
+                for e in range(experts):
+                    opts[e].step(arrays[e][3])
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                for e in range(experts):
+                    opts[e].step(arrays[e][3])
+            timings[fit] = (time.perf_counter() - t0) / steps
+    h2d = experts * 4 * (host_codes[0, 0].nbytes + host_books[0, 0].nbytes)
+    d2h = experts * 3 * (host_codes[0, 0].nbytes + host_books[0, 0].nbytes)
+    return {"value": round(experts * count / timings["device"] / 1e9, 4), "unit": "Gvalues/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(timings["device"] * 1e3, 2),
+            "api": "VQAdamW.step (fit='device') per expert, host VQArrays",
+            "host_fit_ms_per_step": round(timings["host"] * 1e3, 1)}
 
 
 def run_reference(args, world, rank):
