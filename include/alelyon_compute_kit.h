@@ -189,6 +189,7 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
 #define ACK_VQ2_ENCODE 21u       /* encode with a 64-bit value count */
 #define ACK_VQ2_DECODE 22u       /* decode with a 64-bit value count */
 #define ACK_VQ2_REPACK_TILE32 23u /* canonical N x K images -> the tile32 layout op 16 reads */
+#define ACK_VQ2_ADAMW_FIT 24u    /* fit_codebook of W', M', V' on the device (warm start), bit for bit the CPU fit */
 
 /* Flags of ACK_VQ2_DENSE: bit 1 = W stored N x K (vectors along K); bit 2 =
  * W given in the tile32 layout (requires bit 1 and (K / group) % 32 == 0):
@@ -220,7 +221,11 @@ int32_t ack_kernel_manifest(char *out, size_t len, size_t *needed);
  *   20 encode     as 18, new books (batch x 3 x 16 x g) -> codes
  *                 (batch x 3 x words), changed (batch u32)
  *   21/22         values or codes, book -> codes or values
- *   23 repack     canonical codes (batch x words) -> tile32 codes */
+ *   23 repack     canonical codes (batch x words) -> tile32 codes
+ *   24 fit        as 18, op 18's samples (batch x 3 x S x g), in4 = workspace
+ *                 (batch x 3 x (ceil16(S) + 160) bytes, written); flags = 1
+ *                 (warm start), aux0 = S, aux1 = iterations -> fitted books
+ *                 (batch x 3 x 16 x g) */
 int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslots,
                 const uint8_t *plan, size_t plan_len);
 
