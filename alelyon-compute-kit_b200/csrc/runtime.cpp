@@ -209,6 +209,7 @@ uint64_t fnv1a(const void* data, size_t len, uint64_t h = 0xcbf29ce484222325ull)
 uint64_t shader_identity() { return fnv1a(kManifestJson, sizeof(kManifestJson) - 1); }
 
 constexpr const char* kVersion = "alelyon-compute-kit-b200 0.1.0";
+constexpr uint64_t kPoolKeepBytes = uint64_t(1) << 30;  // freed buffer memory the pool keeps cached
 
 int32_t plan_refused(const char* entry, ack::PlanError e, int schema, int slot) {
   set_error(format("%s: plan refused: %s", entry, ack::plan_error_name(e, schema, slot).c_str()));
@@ -305,6 +306,19 @@ ACK_EXPORT AckDevice* ack_open(void) {
       set_error(format("ack_open: stream: %s", cudaGetErrorString(e)));
       return nullptr;
     }
+    // Buffers come from the device's stream-ordered pool (cudaMallocAsync on
+    // the device stream): a free neither waits for the whole device nor, up
+    // to this much cached memory, hands pages back to the driver.
+    cudaMemPool_t pool = nullptr;
+    if (cudaDeviceGetDefaultMemPool(&pool, ordinal) == cudaSuccess) {
+      uint64_t threshold = 0;
+      if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold) == cudaSuccess &&
+          threshold < kPoolKeepBytes) {
+        threshold = kPoolKeepBytes;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+      }
+    }
+    cudaGetLastError();
   }
   Registry& r = registry();
   std::lock_guard<std::mutex> lk(r.mu);
@@ -461,10 +475,11 @@ ACK_EXPORT AckBuffer* ack_buffer_alloc(const AckDevice* handle, uint64_t bytes) 
   }
   DeviceScope scope(dev->ordinal);
   void* ptr = nullptr;
-  cudaError_t e = cudaMalloc(&ptr, bytes);
+  // stream-ordered: usable by everything later enqueued on the device stream
+  cudaError_t e = cudaMallocAsync(&ptr, bytes, dev->stream);
   if (e == cudaSuccess && dev->inject_alloc) {
     dev->inject_alloc = false;
-    cudaFree(ptr);
+    cudaFreeAsync(ptr, dev->stream);
     ptr = nullptr;
     e = cudaErrorMemoryAllocation;
   }
@@ -501,7 +516,7 @@ ACK_EXPORT int32_t ack_buffer_free(const AckDevice* handle, AckBuffer* buf) {
     return ACK_ERR_POISONED;
   }
   DeviceScope scope(dev->ordinal);
-  cudaError_t e = cudaFree(ptr);  // waits for enqueued work that may still use it
+  cudaError_t e = cudaFreeAsync(ptr, dev->stream);  // after the enqueued work that may still use it
   if (e != cudaSuccess) return cuda_fail(*dev, e, "buffer free");
   return ACK_OK;
 }
