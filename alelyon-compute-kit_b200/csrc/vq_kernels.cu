@@ -688,17 +688,21 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
 
 // C[m, n] = sum_t L[a(m,t)][b(n,t)] with L = C_A C_B^T (16 x 16, each entry
 // summed in float64 and rounded once). A stored M x K, B stored N x K,
-// K % G == 0 and (K/G) % 8 == 0 so every row starts on a code word. A warp
-// owns 8 rows (warp-uniform A codes) and 256 columns (8 per lane), so every
-// lookup of an instruction reads one 16-entry row of L: distinct columns hit
-// distinct banks, equal columns broadcast.
+// K % G == 0 and (K/G) % 8 == 0 so every row starts on a code word. A block
+// owns kCodedRows rows of A (the same for all its warps, so A's indices are
+// block-uniform) and 8 x 32 x kCodedCols columns; each lane kCodedRows x
+// kCodedCols outputs. Every lookup of an instruction reads one 16-entry row
+// of L: distinct columns hit distinct banks, equal columns broadcast. (16 x 4
+// per lane measured fastest of 8x8, 4x8, 8x4, 4x4, 16x4, 4x16.)
+constexpr int kCodedRows = 16, kCodedCols = 4;
+
 template <int G>
-__global__ void __launch_bounds__(kThreads) k_coded_lut(const uint32_t* __restrict__ ac,
-                                                        const float* __restrict__ ab,
-                                                        const uint32_t* __restrict__ bc,
-                                                        const float* __restrict__ bb, float* __restrict__ C,
-                                                        uint32_t M, uint32_t N, uint32_t K,
-                                                        uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(kThreads, 2) k_coded_lut(const uint32_t* __restrict__ ac,
+                                                           const float* __restrict__ ab,
+                                                           const uint32_t* __restrict__ bc,
+                                                           const float* __restrict__ bb, float* __restrict__ C,
+                                                           uint32_t M, uint32_t N, uint32_t K,
+                                                           uint32_t* __restrict__ status) {
   __shared__ float L[16 * 16];
   __shared__ float sa[16 * 32], sbk[16 * 32];
   for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) {
@@ -719,46 +723,44 @@ __global__ void __launch_bounds__(kThreads) k_coded_lut(const uint32_t* __restri
     flag_warp(status, bits);
   }
   __syncthreads();
+  constexpr int RI = kCodedRows, RJ = kCodedCols;
   const uint32_t TW = K / G / 8;  // code words per row
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // block tile: 64 rows (8 warps x 8 rows) x 256 columns
-  const uint32_t row0 = blockIdx.y * 64 + warp * 8;
-  const uint32_t col0 = blockIdx.x * 256 + lane;
-  const uint32_t* arow[8];
-  const uint32_t* bcol[8];
+  const uint32_t row0 = blockIdx.x * RI;  // rows on x: up to 2^16 row blocks
+  const uint32_t col0 = blockIdx.y * (8 * 32 * RJ) + warp * (32 * RJ) + lane;
+  const uint32_t* bcol[RJ];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) arow[i] = ac + uint64_t(min(row0 + i, M - 1)) * TW;
+  for (int j = 0; j < RJ; ++j) bcol[j] = bc + uint64_t(min(col0 + 32 * j, N - 1)) * TW;
+  float acc[RI][RJ];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) bcol[j] = bc + uint64_t(min(col0 + 32 * j, N - 1)) * TW;
-  float acc[8][8];
+  for (int i = 0; i < RI; ++i)
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < RJ; ++j) acc[i][j] = 0.f;
   for (uint32_t tw = 0; tw < TW; ++tw) {
-    uint32_t aw[8], bw[8];
+    uint32_t aw[RI], bw[RJ];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) aw[i] = __ldg(arow[i] + tw);
+    for (int i = 0; i < RI; ++i) aw[i] = __ldg(ac + uint64_t(min(row0 + i, M - 1)) * TW + tw);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bw[j] = __ldg(bcol[j] + tw);
+    for (int j = 0; j < RJ; ++j) bw[j] = __ldg(bcol[j] + tw);
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
-      uint32_t a16[8], b1[8];
+      const float* Lr[RI];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a16[i] = ((aw[i] >> (4 * s)) & 15u) << 4;
+      for (int i = 0; i < RI; ++i) Lr[i] = L + (((aw[i] >> (4 * s)) & 15u) << 4);
+      uint32_t b1[RJ];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) b1[j] = (bw[j] >> (4 * s)) & 15u;
+      for (int j = 0; j < RJ; ++j) b1[j] = (bw[j] >> (4 * s)) & 15u;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < RI; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] += L[a16[i] + b1[j]];
+        for (int j = 0; j < RJ; ++j) acc[i][j] += Lr[i][b1[j]];
     }
   }
   uint32_t bits = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < RI; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < RJ; ++j) {
       const uint32_t r = row0 + i, c = col0 + 32 * j;
       if (r < M && c < N) {
         C[uint64_t(r) * N + c] = acc[i][j];
@@ -1342,7 +1344,7 @@ struct RunCoded {
     uint32_t* status = static_cast<uint32_t*>(ptr[7]);
     const uint32_t M = uint32_t(p.m), N = uint32_t(p.n), K = uint32_t(p.k);
     if (p.flags == 2u && K % G == 0 && (K / G) % 8 == 0) {
-      dim3 grid((N + 255) / 256, (M + 63) / 64);
+      dim3 grid((M + kCodedRows - 1) / kCodedRows, (N + 8 * 32 * kCodedCols - 1) / (8 * 32 * kCodedCols));
       k_coded_lut<G><<<grid, kThreads, 0, s>>>(ac, ab, bc, bb, C, M, N, K, status);
       return cudaGetLastError();
     }
