@@ -21,7 +21,8 @@ from . import ack
 
 ENTRIES = 16
 OP_ENCODE1, OP_DECODE1, OP_MATMUL1, OP_ADAMW1 = 0, 1, 2, 3
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT = range(16, 25)
+(OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT,
+ OP_FIT_VALUES) = range(16, 26)
 
 
 def words_for(count: int, group: int) -> int:
@@ -207,4 +208,25 @@ def adamw_fit(codes, books, coefs, samples, count: int, group: int, *, iteration
     status = status_word(dev) if status is None else status
     launch(plan2(OP_FIT, count, 1, 1, group, flags=1, batch=batch, aux0=s, aux1=iterations),
            [codes, books, coefs, samples, workspace, out, None, status])
+    return out, status
+
+
+def fit_codebook(x, group: int, *, iterations: int = 4, sample_vectors: int = 4096, init=None, out=None, status=None):
+    """`fit_codebook` of a float32 CUDA tensor on its device, bit for bit the
+    CPU function's book (16, group); `init` (16, group) warm-starts it."""
+    import numpy as np
+    count = x.numel()
+    complete = count // group
+    if complete < 1:
+        raise ack.AckError("codebook calibration needs at least one complete vector")
+    s = min(complete, sample_vectors)
+    positions = np.linspace(0, complete - 1, s, dtype=np.int64)
+    rows = np.linspace(0, s - 1, ENTRIES, dtype=np.int64)
+    index = torch.from_numpy(np.concatenate([positions, rows]).astype(np.uint32).view(np.int32)).to(x.device)
+    out = torch.empty((ENTRIES, group), dtype=torch.float32, device=x.device) if out is None else out
+    workspace = torch.empty(s * group * 4 + fit_workspace_bytes(s), dtype=torch.uint8, device=x.device)
+    status = status_word(x.device) if status is None else status
+    launch(plan2(OP_FIT_VALUES, count & 0xFFFFFFFF, 1, 1, group, flags=0 if init is None else 1, aux0=s,
+                 aux1=iterations, aux2=count >> 32),
+           [x, init, index, None, workspace, out, None, status])
     return out, status

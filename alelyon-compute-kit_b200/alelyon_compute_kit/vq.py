@@ -42,8 +42,8 @@ _HEADER = struct.Struct("<8sIIIIQQ")
 _MAGIC = b"ACKVQ4\0\0"
 
 # schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
-OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT = \
-    range(16, 25)
+OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT, \
+    OP_FIT_VALUES = range(16, 26)
 
 
 def _integer(value, name: str, minimum: int, maximum: int) -> int:
@@ -602,6 +602,50 @@ class VQDevice:
         result is `x @ decode(w)`. `x` is (M, K) float32."""
         return self.matmul_dense_grouped(np.asarray(x)[None], VQStack.from_arrays([w]),
                                          transpose_b=transpose_b)[0]
+
+    def fit_codebook(self, values, *, group: int = 16, iterations: int = 4, sample_vectors: int = 4096,
+                     init=None) -> np.ndarray:
+        """`fit_codebook` computed on the device: the same arguments, the
+        same refusals and bit for bit the same book as the CPU function (the
+        sample's nearest entries by the certified search, float64 means in
+        sample order, the farthest-point reseed, the warm start's kept-entry
+        rule over the whole tensor)."""
+        group = _group(group)
+        iterations = _integer(iterations, "iterations", 0, 32)
+        sample_vectors = _integer(sample_vectors, "sample_vectors", ENTRIES, 65536)
+        x = _float_array(values, "values").reshape(-1)
+        if x.size < group:
+            raise ValueError("codebook calibration needs at least one complete vector")
+        complete = x.size // group
+        positions = _sample_positions(complete, sample_vectors)
+        s = len(positions)
+        rows = np.linspace(0, s - 1, ENTRIES, dtype=np.int64)
+        index = np.concatenate([positions, rows]).astype(np.uint32)
+        book = None if init is None else _book(init, group)
+        flags = 0 if book is None else 1
+        plan = self._plan2(OP_FIT_VALUES, x.size & 0xFFFFFFFF, 1, 1, group, flags=flags, aux0=s, aux1=iterations,
+                           aux2=x.size >> 32)
+        device = self.device
+        with device._lock, ExitStack() as cleanup:
+            device._require_open()
+
+            def buffer_of(array):
+                b = device.buffer(array.nbytes)
+                cleanup.callback(b.free)
+                b.upload(array)
+                return b
+
+            slots = [buffer_of(x), buffer_of(book) if book is not None else None, buffer_of(index), None]
+            workspace = device.buffer(s * group * 4 + (s + 15) // 16 * 16 + 160)
+            cleanup.callback(workspace.free)
+            out = device.buffer(ENTRIES * group * 4)
+            cleanup.callback(out.free)
+            status = buffer_of(np.zeros(1, dtype=np.uint32))
+            self._launch2(plan, slots + [workspace, out, None, status])
+            flags = int(status.download(np.uint32)[0])
+            if flags:
+                raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            return out.download(np.float32).reshape(ENTRIES, group)
 
     def resident(self, stack: "VQStack", *, layout: str = "tile32") -> "ResidentStack":
         """Upload a `VQStack` once and keep it on the device: the weights of

@@ -733,7 +733,7 @@ ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const Ack
     if (p.required[i] && (ids[i] & 3u)) return plan_refused(entry, ack::PlanError::Misaligned, 2, i);
   const int first_out = p.first_output();
   // the fit's workspace (in4) is written too
-  const int first_written = (p.schema == 2 && p.op == ack::Op::AdamwFit) ? 4 : first_out;
+  const int first_written = (p.schema == 2 && (p.op == ack::Op::AdamwFit || p.op == ack::Op::Fit)) ? 4 : first_out;
   for (int o = first_written; o < n; ++o) {
     if (!p.required[o]) continue;
     for (int i = 0; i < n; ++i) {

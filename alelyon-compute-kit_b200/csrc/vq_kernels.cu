@@ -1409,8 +1409,9 @@ struct RunAdamwFused {
   }
 };
 
-// Op 24, defined with the shared-memory book access at the end of this file.
+// Ops 24 and 25, defined with the shared-memory book access at the end of this file.
 cudaError_t run_adamw_fit(const Plan& p, void* const* ptr, cudaStream_t s);
+cudaError_t run_fit_values(const Plan& p, void* const* ptr, cudaStream_t s);
 
 }  // namespace
 
@@ -1448,6 +1449,9 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
     case Op::DecodeLarge:
       return by_group<RunDecode>(g, static_cast<const uint32_t*>(ptr[0]), static_cast<const float*>(ptr[1]),
                                  static_cast<float*>(ptr[5]), p.m, static_cast<uint32_t*>(ptr[7]), s);
+    case Op::Fit:
+      if (!aligned16(ptr[4])) return cudaErrorMisalignedAddress;  // the gathered sample is read in quads
+      return run_fit_values(p, ptr, s);
     case Op::AdamwFit:
       if (!aligned16(ptr[3])) return cudaErrorMisalignedAddress;  // sample rows are read in 16-byte quads
       return run_adamw_fit(p, ptr, s);
@@ -1633,6 +1637,7 @@ struct FitArgs {
   float* books;          // [E][3][16][G]: the books being fitted
   unsigned char* ws;     // per problem: idx[S padded] | counts[16] | usage[16] | flag
   uint64_t stride;       // workspace bytes per problem
+  uint32_t warm;         // warm start: the kept-entry rule applies
 };
 
 __device__ __forceinline__ uint8_t* fit_idx(const FitArgs& f, uint32_t p) { return f.ws + uint64_t(p) * f.stride; }
@@ -1695,7 +1700,7 @@ __global__ void __launch_bounds__(256) k_fit_assign(FitArgs f, uint64_t complete
     uint32_t empty = 0;
     for (int e = 0; e < 16; ++e) empty |= cnt[e] ? 0u : (1u << e);
     const uint32_t reachable = empty & Book::uniq();
-    words[32] = (f.S < complete && reachable) ? 1u : 0u;
+    words[32] = (f.warm && f.S < complete && reachable) ? 1u : 0u;
   }
 }
 
@@ -1836,6 +1841,7 @@ cudaError_t run_fit_group(const Plan& p, void* const* ptr, cudaStream_t s) {
   f.ws = static_cast<unsigned char*>(ptr[4]);
   f.stride = fit_workspace_stride(p.aux0);
   f.books = static_cast<float*>(ptr[5]);
+  f.warm = 1;
   uint32_t* status = static_cast<uint32_t*>(ptr[7]);
   const uint32_t problems = p.batch * 3;
   const uint64_t complete = p.m / G;
@@ -1854,6 +1860,85 @@ cudaError_t run_adamw_fit(const Plan& p, void* const* ptr, cudaStream_t s) {
   if (p.group == 8) return run_fit_group<8>(p, ptr, s);
   if (p.group == 16) return run_fit_group<16>(p, ptr, s);
   return run_fit_group<32>(p, ptr, s);
+}
+
+// Op 25: one tensor's fit. The sample is gathered into the workspace; the
+// book starts from the caller's (warm) or from 16 sample rows (cold).
+template <int G>
+__global__ void k_fit_gather(const float* __restrict__ values, const uint32_t* __restrict__ positions, uint32_t S,
+                             float* __restrict__ sample) {
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < uint64_t(S) * G;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    sample[i] = values[uint64_t(positions[i / G]) * G + i % G];
+}
+
+template <int G>
+__global__ void k_fit_start(const float* __restrict__ init, const float* __restrict__ sample,
+                            const uint32_t* __restrict__ rows, float* __restrict__ book) {
+  for (int i = threadIdx.x; i < 16 * G; i += blockDim.x)
+    book[i] = init ? init[i] : sample[uint64_t(rows[i / G]) * G + i % G];
+}
+
+// Entries the whole tensor's complete vectors select with the current book
+// (the kept-entry rule), where the assign pass asked for it.
+template <int G>
+__global__ void __launch_bounds__(256) k_fit_usage_values(FitArgs f, const float* __restrict__ values, uint64_t full,
+                                                          uint32_t* __restrict__ status) {
+  using Book = SBook<G>;
+  uint32_t* words = fit_words(f, 0);
+  if (!words[32]) return;
+  __shared__ uint32_t hist[16];
+  if (threadIdx.x < 16) hist[threadIdx.x] = 0;
+  sbook_stage<G>(f.books);
+  uint32_t bits = 0;
+  for (uint64_t v = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < full; v += uint64_t(gridDim.x) * blockDim.x) {
+    float x[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) x[j] = values[v * G + j];
+    bool certified;
+    const uint32_t e = enc_vector<G, Book>(x, &certified, values + v * G);
+    if (certified)
+      for (int j = 0; j < G; ++j) bits |= finite32(values[v * G + j]) ? 0u : kNonfinite;
+    atomicAdd(&hist[e], 1u);
+  }
+  flag_warp(status, bits);
+  __syncthreads();
+  if (threadIdx.x < 16 && hist[threadIdx.x]) atomicAdd(words + 16 + threadIdx.x, hist[threadIdx.x]);
+}
+
+template <int G>
+cudaError_t run_fit_values_group(const Plan& p, void* const* ptr, cudaStream_t s) {
+  const float* values = static_cast<const float*>(ptr[0]);
+  const float* init = (p.flags & 1u) ? static_cast<const float*>(ptr[1]) : nullptr;
+  const uint32_t* positions = static_cast<const uint32_t*>(ptr[2]);
+  unsigned char* ws = static_cast<unsigned char*>(ptr[4]);
+  const uint32_t S = p.aux0;
+  const uint64_t sample_bytes = uint64_t(S) * G * 4;  // a multiple of 16
+  FitArgs f{};
+  f.samples = reinterpret_cast<const float*>(ws);
+  f.S = S;
+  f.books = static_cast<float*>(ptr[5]);
+  f.ws = ws + sample_bytes;
+  f.stride = fit_workspace_stride(S);
+  f.warm = init ? 1u : 0u;
+  uint32_t* status = static_cast<uint32_t*>(ptr[7]);
+  const uint64_t full = p.m / G;
+  k_fit_gather<G><<<grid_for(uint64_t(S) * G), kThreads, 0, s>>>(values, positions, S, reinterpret_cast<float*>(ws));
+  k_fit_start<G><<<1, 256, 0, s>>>(init, f.samples, positions + S, f.books);
+  const uint32_t usage_blocks =
+      uint32_t(std::max<uint64_t>(1, std::min<uint64_t>((full + 255) / 256, uint64_t(sm_count()) * 4)));
+  for (uint32_t it = 0; it < p.aux1; ++it) {
+    k_fit_assign<G><<<1, 256, 0, s>>>(f, full, status);
+    k_fit_usage_values<G><<<usage_blocks, 256, 0, s>>>(f, values, full, status);
+    k_fit_update<G><<<1, 512, 0, s>>>(f);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t run_fit_values(const Plan& p, void* const* ptr, cudaStream_t s) {
+  if (p.group == 8) return run_fit_values_group<8>(p, ptr, s);
+  if (p.group == 16) return run_fit_values_group<16>(p, ptr, s);
+  return run_fit_values_group<32>(p, ptr, s);
 }
 
 }  // namespace

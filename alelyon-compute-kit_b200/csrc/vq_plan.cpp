@@ -92,7 +92,7 @@ constexpr uint32_t kMaxSamples = 65536;         // fit_codebook's sample bound (
 PlanError parse_schema2(Plan* p) {
   const auto& w = p->words;
   uint32_t op = w[0], group = w[4], entries = w[5], flags = w[6], reserved = w[7];
-  if (op < 16 || op > 24) return PlanError::Operation;
+  if (op < 16 || op > 25) return PlanError::Operation;
   if (!valid_group(group)) return PlanError::Group;
   if (entries != kEntries) return PlanError::Entries;
   if (reserved != 0 || w[12] || w[13] || w[14] || w[15]) return PlanError::Reserved;
@@ -187,6 +187,25 @@ PlanError parse_schema2(Plan* p) {
                      E * 3 * fit_workspace_stride(p->aux0), E * 3 * book, 0, 4};
       break;
     }
+    case Op::Fit: {
+      // fit_codebook (vq.py:182-257) of one tensor of count = m + aux2 << 32
+      // values: aux0 sample vectors at the positions in in2 (followed by the
+      // 16 cold-start rows of the sample), aux1 Lloyd iterations; flag bit 0:
+      // warm start from the book in in1. in4: workspace (the sample, then the
+      // fit's bookkeeping).
+      if (flags & ~1u) return PlanError::Flags;
+      if (p->n != 1 || p->k != 1) return PlanError::Geometry;
+      if (E != 1) return PlanError::Batch;
+      const uint64_t count = uint64_t(w[1]) | (uint64_t(p->aux2) << 32);
+      if (count < group) return PlanError::Geometry;
+      if (count > kMaxLarge) return PlanError::AddressLimit;
+      p->m = count;
+      if (!p->aux0 || p->aux0 > kMaxSamples || p->aux0 > count / group || p->aux1 > 32) return PlanError::Aux;
+      const uint64_t sample_bytes = uint64_t(p->aux0) * group * 4;
+      p->required = {count * 4, (flags & 1u) ? book : 0, (uint64_t(p->aux0) + 16) * 4, 0,
+                     sample_bytes + fit_workspace_stride(p->aux0), book, 0, 4};
+      break;
+    }
     case Op::EncodeLarge:
     case Op::DecodeLarge: {
       if (flags) return PlanError::Flags;
@@ -258,7 +277,7 @@ PlanError validate_buffers(const Plan& p, const uint64_t* capacities, const uint
     }
   // written: out0, out1, and in4 for the fit (its workspace)
   for (int o = 4; o < 7; ++o) {
-    if (!p.required[o] || (o == 4 && p.op != Op::AdamwFit)) continue;
+    if (!p.required[o] || (o == 4 && p.op != Op::AdamwFit && p.op != Op::Fit)) continue;
     for (int i = 0; i < n; ++i)
       if (i != o && p.required[i] && ids[i] == ids[o] && i != 7) return PlanError::OutputAlias;
   }

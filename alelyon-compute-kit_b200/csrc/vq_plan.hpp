@@ -21,7 +21,7 @@ constexpr int kSlots = 8;                        // schema 2; schema 1 uses the 
 enum class Op : uint32_t {
   Encode = 0, Decode = 1, Matmul = 2, AdamW = 3,
   Dense = 16, Coded = 17, AdamwSample = 18, AdamwUsage = 19, AdamwEncode = 20,
-  EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23, AdamwFit = 24,
+  EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23, AdamwFit = 24, Fit = 25,
 };
 
 // Refusals. The schema-1 names are vq4_ops.rs:66-84; the schema-2 ones are

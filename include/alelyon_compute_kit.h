@@ -190,6 +190,7 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
 #define ACK_VQ2_DECODE 22u       /* decode with a 64-bit value count */
 #define ACK_VQ2_REPACK_TILE32 23u /* canonical N x K images -> the tile32 layout op 16 reads */
 #define ACK_VQ2_ADAMW_FIT 24u    /* fit_codebook of W', M', V' on the device (warm start), bit for bit the CPU fit */
+#define ACK_VQ2_FIT 25u          /* fit_codebook of one tensor on the device, bit for bit the CPU function */
 
 /* Flags of ACK_VQ2_DENSE: bit 1 = W stored N x K (vectors along K); bit 2 =
  * W given in the tile32 layout (requires bit 1 and (K / group) % 32 == 0):
@@ -225,7 +226,11 @@ int32_t ack_kernel_manifest(char *out, size_t len, size_t *needed);
  *   24 fit        as 18, op 18's samples (batch x 3 x S x g), in4 = workspace
  *                 (batch x 3 x (ceil16(S) + 160) bytes, written); flags = 1
  *                 (warm start), aux0 = S, aux1 = iterations -> fitted books
- *                 (batch x 3 x 16 x g) */
+ *                 (batch x 3 x 16 x g)
+ *   25 fit        values (count = m + aux2 << 32), warm book (flags bit 0),
+ *                 u32 sample positions then 16 cold-start sample rows,
+ *                 in4 = workspace (S x g x 4 + ceil16(S) + 160 bytes,
+ *                 written); aux0 = S, aux1 = iterations -> book (16 x g) */
 int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslots,
                 const uint8_t *plan, size_t plan_len);
 

@@ -339,6 +339,29 @@ def test_device_fit_is_the_cpu_fit_bit_for_bit(backend, shape, group, sample):
         assert reports["host"] == reports["device"]
 
 
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_device_fit_codebook_is_the_cpu_function_bit_for_bit(backend, group):
+    """VQDevice.fit_codebook against vq.fit_codebook: cold and warm starts,
+    Gaussian, duplicate-heavy (empty entries, reseeds), a ragged tail, a
+    sample smaller than the tensor (the kept-entry rule), 0 to 6 iterations."""
+    rng = np.random.default_rng(40 + group)
+    atoms = rng.standard_normal((16, group)).astype(np.float32)
+    cases = [
+        (o.gaussian((300, 7 * group + 3), 1.0, 1), {}),
+        (o.block_normalised(o.gaussian((4096, 2 * group), 0.5, 2), group), {"sample_vectors": 1000}),
+        (atoms[np.insert(np.arange(5000) % 12, 4000, 14)].reshape(-1), {}),
+        (atoms[np.insert(np.arange(9000) % 15, 3, 15)].reshape(-1), {"sample_vectors": 512}),
+        (o.gaussian((64, group), 1.0, 3), {"iterations": 0}),
+        (o.gaussian((2000, group), 1.0, 4), {"iterations": 6, "sample_vectors": 16}),
+    ]
+    for values, kw in cases:
+        for init in (None, "warm"):
+            start = None if init is None else vq.fit_codebook(values, group=group, iterations=1, sample_vectors=64)
+            want = vq.fit_codebook(values, group=group, init=start, **kw)
+            got = backend.fit_codebook(values, group=group, init=start, **kw)
+            np.testing.assert_array_equal(bits(got), bits(want))
+
+
 @pytest.mark.parametrize("group,rare_at", [(8, -1), (16, -1), (32, -1), (8, 1)])
 def test_fused_zero_gradient_moves_no_weight(backend, group, rare_at):
     """The reference audit's acceptance test on the device path; with the

@@ -169,7 +169,11 @@ def test_schema2_adamw_and_large_slot_sizes():
     stride = (s + 15) // 16 * 16 + 160  # fit workspace per book: idx bytes, counts, usage, flag
     assert required(plan2(24, n, 1, 1, g, flags=1, batch=e, aux0=s, aux1=4)) == [
         e * 4 * words * 4, e * 4 * 64 * g, e * 28, e * 3 * s * g * 4, e * 3 * stride, e * 3 * 64 * g, 0, 4]
+    # op 25: one tensor's fit, 64-bit count, sample gathered into the workspace
     big = 1 << 30
+    assert required(plan2(25, big & 0xFFFFFFFF, 1, 1, 16, flags=1, aux0=65536, aux1=4, aux2=big >> 32)) == [
+        big * 4, 1024, (65536 + 16) * 4, 0, 65536 * 16 * 4 + 65536 + 160, 1024, 0, 4]
+    assert required(plan2(25, 1000, 1, 1, 8, aux0=100, aux1=4))[1] == 0  # cold start reads no book
     assert required(plan2(21, big & 0xFFFFFFFF, 1, 1, 16, aux0=big >> 32)) == [
         big * 4, 1024, 0, 0, 0, (big // 16 + 7) // 8 * 4, 0, 4]
     assert required(plan2(22, big & 0xFFFFFFFF, 1, 1, 16, aux0=big >> 32)) == [
@@ -193,7 +197,11 @@ def test_schema2_refusals_are_named():
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=9, aux1=4), "vq2-invalid-aux-word"),
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=8, aux1=33), "vq2-invalid-aux-word"),
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=8, aux1=4, batch=0), "vq2-invalid-batch"),
-        (plan2(25, 64, 1, 1, 8), "vq2-operation-out-of-range"),
+        (plan2(26, 64, 1, 1, 8), "vq2-operation-out-of-range"),
+        (plan2(25, 64, 1, 1, 8, flags=2, aux0=8, aux1=4), "vq2-unsupported-flags"),
+        (plan2(25, 64, 1, 1, 8, aux0=9, aux1=4), "vq2-invalid-aux-word"),
+        (plan2(25, 64, 1, 1, 8, aux0=8, aux1=4, batch=2), "vq2-invalid-batch"),
+        (plan2(25, 7, 1, 1, 8, aux0=1, aux1=4), "vq2-invalid-geometry"),
         (plan2(21, 1, 1, 1, 8, aux0=1 << 8), "vq2-address-limit-exceeded"),
         (plan2(16, 1 << 21, 1, 1, 8), "vq2-invalid-geometry"),
     ]
