@@ -79,9 +79,14 @@ class VulkanExpertHarness:
     opens one `ack.Device` (a CUDA device). Importing this module opens
     nothing."""
 
-    def __init__(self, bank: expert_bank.ExpertBank, *, backend=None, device=None):
+    def __init__(self, bank: expert_bank.ExpertBank, *, backend=None, device=None, fit: str = "host"):
+        """`fit="device"` computes every codebook fit of a step (the four
+        encodes and the optimizer's refit) on the device: the same books as
+        the CPU fit, bit for bit. It needs a backend with `fit_codebook`."""
         if not isinstance(bank, expert_bank.ExpertBank):
             raise HarnessError("bank must be an ExpertBank")
+        if fit not in ("host", "device"):
+            raise HarnessError(f"fit must be 'host' or 'device', not {fit!r}")
         if backend is not None and device is not None:
             raise HarnessError("supply backend or device, not both")
         self.bank = bank
@@ -91,12 +96,15 @@ class VulkanExpertHarness:
             self._device = device or ack.Device()
             self._owned_device = device is None
             backend = vq.VQDevice(self._device)
+        if fit == "device" and not hasattr(backend, "fit_codebook"):
+            raise HarnessError("fit='device' needs a backend that fits codebooks on the device")
         self.backend = backend
+        self.fit = fit
 
     @classmethod
-    def open(cls, root, *, device=None, backend=None) -> "VulkanExpertHarness":
+    def open(cls, root, *, device=None, backend=None, fit: str = "host") -> "VulkanExpertHarness":
         """Open an existing bank without creating or initialising payloads."""
-        return cls(expert_bank.ExpertBank.open(root), backend=backend, device=device)
+        return cls(expert_bank.ExpertBank.open(root), backend=backend, device=device, fit=fit)
 
     def __enter__(self) -> "VulkanExpertHarness":
         return self
@@ -127,7 +135,11 @@ class VulkanExpertHarness:
         calibration = values
         if values.size < group:
             calibration = np.pad(values.reshape(-1), (0, group - values.size))
-        return self.backend.encode(values, vq.fit_codebook(calibration, group=group), group=group)
+        if self.fit == "device":
+            book = self.backend.fit_codebook(calibration, group=group)
+        else:
+            book = vq.fit_codebook(calibration, group=group)
+        return self.backend.encode(values, book, group=group)
 
     def forward(self, inputs, *, layer: int = 0, expert: int = 0) -> np.ndarray:
         """`inputs @ weight` through the packed product."""
@@ -169,7 +181,7 @@ class VulkanExpertHarness:
         gradient_image = self._encode(gradient, weight.group)
         try:
             optimizer = vq.VQAdamW(self.backend, weight, lr=lr, betas=(beta1, beta2), eps=eps,
-                                   weight_decay=weight_decay)
+                                   weight_decay=weight_decay, fit=self.fit)
             optimizer.momentum, optimizer.variance = momentum, variance
             optimizer.steps = state.optimizer_step
             update = optimizer.step(gradient_image)
@@ -239,12 +251,14 @@ def main(argv=None) -> int:
     parser.add_argument("--lr", type=float, default=1e-3)
     parser.add_argument("--max-grad-norm", type=float, default=1.0)
     parser.add_argument("--device", action="store_true", help="explicitly open the CUDA device")
+    parser.add_argument("--fit", choices=("host", "device"), default="host",
+                        help="where codebooks are fitted (the same books either way)")
     parser.add_argument("--force", action="store_true")
     args = parser.parse_args(argv)
     if not args.device:
         parser.error("--device is required; execution is never implicit")
     inputs = _load_array(args.input, "input")
-    with VulkanExpertHarness.open(args.bank) as harness:
+    with VulkanExpertHarness.open(args.bank, fit=args.fit) as harness:
         if args.target is None:
             result = harness.forward(inputs, layer=args.layer, expert=args.expert)
             _save_array(args.output, result, force=args.force)

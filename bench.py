@@ -322,8 +322,9 @@ def run_cfg2_e2e(args, torch, vq, codes, books, x, book, local):
                    "X in and Y out through pinned host memory every step)"}
 
 
-def _timed(torch, fn, steps, warmup, world, device, local):
-    """CUDA-event time of `steps` calls after `warmup`, max over ranks (ms/step)."""
+def _timed(torch, fn, steps, warmup, world, device, local, label="timed"):
+    """CUDA-event time of `steps` calls after `warmup`, max over ranks (ms/step).
+    The timed calls run inside the NVTX range `label`."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -332,7 +333,7 @@ def _timed(torch, fn, steps, warmup, world, device, local):
         dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        torch.cuda.nvtx.range_push("timed")
+        torch.cuda.nvtx.range_push(label)
         start.record()
         for _ in range(steps):
             fn()
@@ -518,7 +519,7 @@ def run_cfg4(args, world, rank, local):
                                             batch=experts, out=out, changed=changed, status=status)
     ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local)
     cuda.check(status)
-    ms_encode, _ = _timed(torch, encode_pass, args.steps, args.warmup, world, device, local)
+    ms_encode, _ = _timed(torch, encode_pass, args.steps, args.warmup, world, device, local, label="encode-pass")
     cuda.check(status)
     byts = codes.numel() * 4 + out.numel() * 4
     peak = measured_peaks().get("hbm_gbs") or 6650.0

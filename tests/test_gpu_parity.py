@@ -381,7 +381,8 @@ def test_fused_zero_gradient_moves_no_weight(backend, group, rare_at):
         assert len(np.unique(opt.weight.codebook.round(6), axis=0)) == 16
 
 
-def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device):
+@pytest.mark.parametrize("fit", ["host", "device"])
+def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device, fit):
     from alelyon_compute_kit import expert_bank, harness
     rng = np.random.default_rng(12)
     roots = []
@@ -391,7 +392,7 @@ def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device):
         roots.append(bank)
     x = rng.standard_normal((8, 64)).astype(np.float32)
     t = rng.standard_normal((8, 48)).astype(np.float32)
-    dev_h = harness.VulkanExpertHarness(roots[0], device=device)
+    dev_h = harness.VulkanExpertHarness(roots[0], device=device, fit=fit)
     host_h = harness.VulkanExpertHarness(roots[1], backend=HostShaderBackend())
     for _ in range(2):
         a = dev_h.train_step(x, t, expert=1, beta2=0.999)

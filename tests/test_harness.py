@@ -41,6 +41,14 @@ def test_forward_uses_packed_expert_and_rejects_wrong_width(tmp_path):
         runner.forward(np.zeros((2, 5), dtype=np.float32))
 
 
+def test_device_fit_needs_a_backend_that_fits_on_the_device(tmp_path):
+    bank = _bank(tmp_path)
+    with pytest.raises(harness.HarnessError, match="fit='device'"):
+        harness.VulkanExpertHarness(bank, backend=FakeBackend(), fit="device")
+    with pytest.raises(harness.HarnessError, match="fit must be"):
+        harness.VulkanExpertHarness(bank, backend=FakeBackend(), fit="gpu")
+
+
 def test_train_step_commits_optimizer_state_and_rejects_nonfinite(tmp_path):
     bank = _bank(tmp_path)
     runner = harness.VulkanExpertHarness(bank, backend=FakeBackend())
