@@ -1663,7 +1663,7 @@ __global__ void k_fit_init(const float* __restrict__ books_in, float* __restrict
 }
 
 template <int G>
-__global__ void __launch_bounds__(256) k_fit_assign(FitArgs f, uint64_t complete, uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(256, 2) k_fit_assign(FitArgs f, uint64_t complete, uint32_t* __restrict__ status) {
   using Book = SBook<G>;
   __shared__ uint32_t cnt[16];
   const uint32_t p = blockIdx.x;
@@ -1672,6 +1672,7 @@ __global__ void __launch_bounds__(256) k_fit_assign(FitArgs f, uint64_t complete
   uint8_t* idx = fit_idx(f, p);
   uint32_t bits = Book::bad() ? kNonfinite : 0u;
   for (uint32_t i = threadIdx.x; i < f.S; i += blockDim.x) {
+    asm volatile("" ::: "memory");  // re-read the book from shared memory each vector (no hoisting into registers)
     const float* src = f.samples + (uint64_t(p) * f.S + i) * G;
     float x[G];
 #pragma unroll
@@ -1705,7 +1706,7 @@ __global__ void __launch_bounds__(256) k_fit_assign(FitArgs f, uint64_t complete
 }
 
 template <int G>
-__global__ void __launch_bounds__(256) k_fit_usage(FitArgs f, uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(256, 2) k_fit_usage(FitArgs f, uint32_t* __restrict__ status) {
   using Book = SBook<G>;
   const uint32_t p = blockIdx.y, e = p / 3, w = p % 3;
   uint32_t* words = fit_words(f, p);
@@ -1720,6 +1721,7 @@ __global__ void __launch_bounds__(256) k_fit_usage(FitArgs f, uint32_t* __restri
   uint32_t bits = k.status;
   if (!k.status) {
     for (uint64_t v = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < full; v += uint64_t(gridDim.x) * blockDim.x) {
+      asm volatile("" ::: "memory");  // the book stays in shared memory
       float x[G];
       adamw_vector<G>(f.a, sbooks, k, e, v, G, int(w), x, &bits);
       bool certified;
@@ -1752,12 +1754,16 @@ __device__ __forceinline__ double fit_gap(const float* __restrict__ s, const flo
                    __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
 }
 
+// Dynamic shared memory: S u16 sample indices, grouped by nearest entry in
+// sample order (a stable counting sort), so each entry's mean reads only its
+// own vectors.
 template <int G>
 __global__ void __launch_bounds__(512) k_fit_update(FitArgs f) {
   __shared__ float book[16 * G], mean[16 * G];
-  __shared__ uint32_t cnt[16], kept;
+  __shared__ uint32_t cnt[16], kept, base[17];
   __shared__ double red_gap[16];
   __shared__ uint32_t red_idx[16];
+  extern __shared__ uint16_t order[];
   const uint32_t p = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   float* out = f.books + uint64_t(p) * 16 * G;
   for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) book[i] = out[i];
@@ -1771,15 +1777,39 @@ __global__ void __launch_bounds__(512) k_fit_update(FitArgs f) {
   }
   __syncthreads();
   const float* sample = f.samples + uint64_t(p) * f.S * G;
-  // means: warp = entry, lane = component, the sample in order
+  // stable counting sort of the sample by nearest entry (warp 0, 32 at a time)
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t run = 0;
+      for (int e = 0; e < 16; ++e) {
+        base[e] = run;
+        run += cnt[e];
+      }
+      base[16] = run;
+    }
+    __syncwarp();
+    const uint8_t* idx = fit_idx(f, p);
+    const uint32_t below = (1u << lane) - 1u;
+    for (uint32_t c = 0; c < f.S; c += 32) {
+      const uint32_t i = c + lane;
+      const uint32_t e = i < f.S ? idx[i] : 16u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, e);
+      const uint32_t at = base[e] + __popc(peers & below);
+      if (e < 16) order[at] = uint16_t(i);
+      __syncwarp();
+      if (e < 16 && (peers & below) == 0) base[e] += __popc(peers);  // the group's lowest lane
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // means: warp = entry, lane = component, its vectors in sample order
   {
-    const uint32_t e = warp;
-    if (lane < G && cnt[e]) {
-      const uint8_t* idx = fit_idx(f, p);
+    const uint32_t e = warp, n = cnt[e];
+    if (lane < G && n) {
+      const uint16_t* mine = order + (base[e] - n);  // base[e] now ends entry e's run
       double s = 0.0;
-      for (uint32_t i = 0; i < f.S; ++i)
-        if (idx[i] == e) s = __dadd_rn(s, double(sample[uint64_t(i) * G + lane]));
-      mean[e * G + lane] = __double2float_rn(__ddiv_rn(s, double(cnt[e])));
+      for (uint32_t k = 0; k < n; ++k) s = __dadd_rn(s, double(sample[uint64_t(mine[k]) * G + lane]));
+      mean[e * G + lane] = __double2float_rn(__ddiv_rn(s, double(n)));
     }
   }
   __syncthreads();
@@ -1828,6 +1858,13 @@ __global__ void __launch_bounds__(512) k_fit_update(FitArgs f) {
   for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) out[i] = book[i];
 }
 
+inline size_t fit_update_smem(uint32_t S) { return (size_t(S) * 2 + 15) / 16 * 16; }
+
+template <int G>
+cudaError_t fit_update_attr(uint32_t S) {
+  return cudaFuncSetAttribute(k_fit_update<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(fit_update_smem(S)));
+}
+
 template <int G>
 cudaError_t run_fit_group(const Plan& p, void* const* ptr, cudaStream_t s) {
   FitArgs f;
@@ -1845,13 +1882,15 @@ cudaError_t run_fit_group(const Plan& p, void* const* ptr, cudaStream_t s) {
   uint32_t* status = static_cast<uint32_t*>(ptr[7]);
   const uint32_t problems = p.batch * 3;
   const uint64_t complete = p.m / G;
+  cudaError_t err = fit_update_attr<G>(f.S);
+  if (err != cudaSuccess) return err;
   k_fit_init<G><<<problems, 128, 0, s>>>(f.a.books, f.books, problems);
   const uint32_t usage_blocks =
       uint32_t(std::max<uint64_t>(1, std::min<uint64_t>((complete + 255) / 256, uint64_t(sm_count()) * 4)));
   for (uint32_t it = 0; it < p.aux1; ++it) {
     k_fit_assign<G><<<problems, 256, 0, s>>>(f, complete, status);
     k_fit_usage<G><<<dim3(usage_blocks, problems), 256, 0, s>>>(f, status);
-    k_fit_update<G><<<problems, 512, 0, s>>>(f);
+    k_fit_update<G><<<problems, 512, fit_update_smem(f.S), s>>>(f);
   }
   return cudaGetLastError();
 }
@@ -1882,7 +1921,7 @@ __global__ void k_fit_start(const float* __restrict__ init, const float* __restr
 // Entries the whole tensor's complete vectors select with the current book
 // (the kept-entry rule), where the assign pass asked for it.
 template <int G>
-__global__ void __launch_bounds__(256) k_fit_usage_values(FitArgs f, const float* __restrict__ values, uint64_t full,
+__global__ void __launch_bounds__(256, 2) k_fit_usage_values(FitArgs f, const float* __restrict__ values, uint64_t full,
                                                           uint32_t* __restrict__ status) {
   using Book = SBook<G>;
   uint32_t* words = fit_words(f, 0);
@@ -1892,6 +1931,7 @@ __global__ void __launch_bounds__(256) k_fit_usage_values(FitArgs f, const float
   sbook_stage<G>(f.books);
   uint32_t bits = 0;
   for (uint64_t v = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < full; v += uint64_t(gridDim.x) * blockDim.x) {
+    asm volatile("" ::: "memory");  // the book stays in shared memory
     float x[G];
 #pragma unroll
     for (int j = 0; j < G; ++j) x[j] = values[v * G + j];
@@ -1923,6 +1963,8 @@ cudaError_t run_fit_values_group(const Plan& p, void* const* ptr, cudaStream_t s
   f.warm = init ? 1u : 0u;
   uint32_t* status = static_cast<uint32_t*>(ptr[7]);
   const uint64_t full = p.m / G;
+  cudaError_t err = fit_update_attr<G>(S);
+  if (err != cudaSuccess) return err;
   k_fit_gather<G><<<grid_for(uint64_t(S) * G), kThreads, 0, s>>>(values, positions, S, reinterpret_cast<float*>(ws));
   k_fit_start<G><<<1, 256, 0, s>>>(init, f.samples, positions + S, f.books);
   const uint32_t usage_blocks =
@@ -1930,7 +1972,7 @@ cudaError_t run_fit_values_group(const Plan& p, void* const* ptr, cudaStream_t s
   for (uint32_t it = 0; it < p.aux1; ++it) {
     k_fit_assign<G><<<1, 256, 0, s>>>(f, full, status);
     k_fit_usage_values<G><<<usage_blocks, 256, 0, s>>>(f, values, full, status);
-    k_fit_update<G><<<1, 512, 0, s>>>(f);
+    k_fit_update<G><<<1, 512, fit_update_smem(f.S), s>>>(f);
   }
   return cudaGetLastError();
 }
