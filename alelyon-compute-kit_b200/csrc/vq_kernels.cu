@@ -625,11 +625,11 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
           uint4 q[kPieces];
 #pragma unroll
           for (int pc = 0; pc < kPieces; ++pc) q[pc] = __ldg(src + pc * 32);
-          float acc[MC][4];
+          // acc[m][0] = (sum 0, sum 1), acc[m][1] = (sum 2, sum 3): the even and
+          // odd groups of a word pair add as one packed two-lane add
+          float2 acc[MC][2];
 #pragma unroll
-          for (int m = 0; m < MC; ++m)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) acc[m][r] = 0.f;
+          for (int m = 0; m < MC; ++m) acc[m][0] = acc[m][1] = make_float2(0.f, 0.f);
           const unsigned char* Pb = smem;
 #pragma unroll
           for (int pc = 0; pc < kPieces; ++pc) {
@@ -659,10 +659,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
                   }
                 }
 #pragma unroll
-                for (int m = 0; m < MC; ++m) {
-                  acc[m][(2 * kk) & 3] += vl[m];
-                  acc[m][(2 * kk + 1) & 3] += vh[m];
-                }
+                for (int m = 0; m < MC; ++m) acc[m][kk & 1] = __fadd2_rn(acc[m][kk & 1], make_float2(vl[m], vh[m]));
               }
             }
           }
@@ -671,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
 #pragma unroll
             for (int m = 0; m < MC; ++m) {
               if (m < int(mc)) {
-                const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
+                const float y = (acc[m][0].x + acc[m][0].y) + (acc[m][1].x + acc[m][1].y);
                 float* dst = Yb + uint64_t(m0 + m) * N + row;
                 *dst = t0 ? *dst + y : y;
               }
