@@ -81,11 +81,16 @@ def status_word(device) -> torch.Tensor:
     return torch.zeros(1, dtype=torch.int32, device=device)
 
 
+STATUS_BITS = {1: "nonfinite", 2: "layout", 4: "optimizer", 8: "stalled"}
+
+
 def check(status: torch.Tensor) -> None:
-    """Synchronise on the status word and raise on any set bit."""
+    """Synchronise on the status word and raise on any set bit (vq4.comp:5-8
+    bits 1/2/4; bit 8: a pipelined kernel's bounded wait ran out)."""
     flags = int(status.item()) & 0xFFFFFFFF
     if flags:
-        raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+        names = ", ".join(name for bit, name in STATUS_BITS.items() if flags & bit) or "unknown"
+        raise ack.AckError(f"vq device arithmetic refused: status={flags} ({names})")
 
 
 def decode(codes, book, count: int, group: int, *, out=None, status=None):

@@ -11,6 +11,7 @@ namespace ack {
 constexpr uint32_t kNonfinite = 1u;   // vq4.comp:5-8 status bits
 constexpr uint32_t kLayout = 2u;
 constexpr uint32_t kOptimizer = 4u;
+constexpr uint32_t kStalled = 8u;     // a bounded pipeline wait ran out (no reference counterpart)
 
 // Index of vector `v` in a packed image: nibble v%8 of word v/8, little-endian.
 __device__ __forceinline__ uint32_t code_at(const uint32_t* __restrict__ codes, uint64_t v) {

@@ -2,10 +2,12 @@
 //
 //   decode        HBM-write-bound gather: 128-bit streaming stores, the
 //                 codebook in shared memory (vq4.comp op 1 / vq.py:117-121)
-//   encode        certified nearest entry per vector: FP32 filter on the CUDA
-//                 cores, float64 pass only for near ties; lanes of a warp own
-//                 consecutive vectors and pack nibbles with shuffles
-//                 (vq4.comp op 0 / vq.py:154-179)
+//   encode        certified nearest entry per vector (vq4.comp op 0 /
+//                 vq.py:154-179): aligned input takes k_encode_tc (TMA tiles,
+//                 tcgen05 tf32 filter, deferred FP32 refinement of the few
+//                 near ties, float64 pass for what stays tied); otherwise
+//                 k_encode (FP32 filter on the CUDA cores); lanes of a warp
+//                 own consecutive vectors and pack nibbles with shuffles
 //   matmul_exact  the shader's packed-pair product (vq4.comp:165-176):
 //                 64x64 tiles dequantised into shared memory, each output
 //                 summed in k order with separately rounded multiply and add
@@ -20,6 +22,8 @@
 //                 FP32 FMA
 //   adamw_*       fused coded-state AdamW: sampled values, whole-tensor entry
 //                 usage, and decode -> AdamW -> encode of W', M', V'
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -259,6 +263,394 @@ __global__ void __launch_bounds__(kThreads, 3) k_encode_async(const float* __res
     enc_step<G, SLOT>(x, n, base, xr, codes, status);
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// ------------------------------------------------ encode on the tensor cores --
+//
+// k_encode_tc: the FP32 filter of enc_vector moved onto tcgen05. A producer
+// warp streams tiles of 128 H vectors (raw FP32, TMA-swizzled into the UMMA
+// K-major layout) into an S-stage ring; one thread issues
+// tcgen05.mma.kind::tf32 of each 128-vector sub-tile against the book
+// (rounded to tf32) into TMEM; C consumer quads (quad q owns the block's
+// tiles k = q mod C and its own accumulator columns) read the 16 dot
+// products of each vector with tcgen05.ld and certify the nearest entry.
+//
+// Certificate. The tensor core uses the top 19 bits of each x component
+// (|x - x'| < 2^-10 |x|), the book is rounded to tf32 (2^-11), products are
+// exact and accumulate in FP32. With f_e = ||c_e||^2 - 2 x.c_e and
+// sum_j |x_j c_j| <= (||x||^2 + max ||c||^2) / 2, the computed f'_e obeys
+// |f'_e - f_e| <= eps1 = kappa1 (||x||^2 + max ||c||^2) + 2^-118 with
+// kappa1 = 2^-10 + 2^-11 + (G + 8) 2^-21 (the last term covers the FP32
+// accumulation and the final fused multiply-add; the absolute floor covers
+// flushed subnormal products). The float64 winner lies in
+// {e : f'_e <= min f' + 2 eps1} minus duplicate rows; one entry left is the
+// answer. Otherwise (a few per cent of vectors on smooth data) the vector
+// joins its warp's queue and is refined later: the FP32 filter of enc_vector
+// (its bound kappa2 = (G + 8) 2^-23) over those candidates only, then the
+// float64 pass over what survives, the result OR-ed into the zero nibble the
+// first pass stored. Nonfinite input or books take the float64 pass at once.
+//
+// Every wait on an mbarrier is bounded; one that runs out sets kStalled and
+// the block drains its own copies and returns.
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// FP32 -> tf32, round to nearest (ties away), as cvt.rna.tf32.f32.
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// The UMMA K-major swizzle matching the TMA swizzle of a G-float row
+// (32/64/128-byte rows: SWIZZLE_32B/64B/128B; 16-byte chunk bits [4,7)
+// XOR-ed with row-group bits [7,10)).
+template <int G>
+struct Swz {
+  static constexpr uint32_t kRow = G * 4;
+  static constexpr uint32_t kMask = G == 8 ? 1u : (G == 16 ? 3u : 7u);
+  static constexpr uint64_t kLayout = G == 8 ? 6u : (G == 16 ? 4u : 2u);  // descriptor layout type
+  // byte offset of 16-byte chunk `kc` of row `r` in a 1024-byte aligned tile
+  static __device__ __forceinline__ uint32_t off(uint32_t r, uint32_t kc) {
+    const uint32_t l = r * kRow + kc * 16u;
+    return l ^ (((l >> 7) & kMask) << 4);
+  }
+  // shared-memory matrix descriptor: start >> 4, leading byte offset 16 (unused
+  // by swizzled K-major), stride byte offset = 8 rows, version 1, layout type
+  static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
+    return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(((8u * kRow) >> 4) & 0x3FFFu) << 32) |
+           (uint64_t(1) << 46) | (kLayout << 61);
+  }
+};
+
+// Instruction descriptor: D FP32, A and B tf32, both K-major, N = 16, M = 128.
+constexpr uint32_t kIdescM128N16 = (1u << 4) | (2u << 7) | (2u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void mb_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mb_arrive(uint64_t* b) {
+  asm volatile("{ .reg .b64 t; mbarrier.arrive.shared::cta.b64 t, [%0]; }" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("{ .reg .b64 t; mbarrier.arrive.expect_tx.shared::cta.b64 t, [%0], %1; }" ::"r"(smem_u32(b)),
+               "r"(bytes)
+               : "memory");
+}
+// Wait for the phase of parity `parity` to complete; false after ~2^22 polls
+// (each poll suspends for a hardware-chosen interval), never an endless spin.
+__device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity) {
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// Stages S, consumer quads C, sub-tiles of 128 vectors per tile H (one TMA
+// box holds at most 256 rows). Measured on B200 for 2^30 values.
+template <int G>
+struct Cfg {
+  static constexpr int S = 4, C = 2, H = G == 8 ? 4 : (G == 16 ? 2 : 1);
+  static constexpr int kThreads = 128 * C + 64;
+  static constexpr uint32_t kSub = 128u * G * 4u, kTile = kSub * H;
+  static constexpr uint32_t kBoxRows = H > 2 ? 256u : 128u * H;
+  static constexpr uint32_t kCols = C * H * 16 <= 32 ? 32u : (C * H * 16 <= 64 ? 64u : 128u);
+  static constexpr uint32_t kCap = H == 1 ? 64u : (H == 2 ? 128u : 256u);  // >= 31 + 32 H: a tile never overflows it
+  // dynamic shared memory: 1024-byte alignment slack, the ring, the tf32
+  // book tile (2 KB), the FP32 book and its 16 squared norms
+  static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 2048 + 16 * G * 4 + 64;
+};
+
+// Deferred FP32 refinement of `count` (<= 32) queued vectors, one per lane,
+// ring positions head + lane: x read again from memory, the FP32 filter of
+// enc_vector over the tf32 candidates, the float64 pass if more than one
+// survives; the index is OR-ed into the zero nibble the filter pass stored.
+template <int G, class Book, uint32_t kCap>
+__device__ __noinline__ void refine_queue(const float* __restrict__ x, uint32_t* __restrict__ codes,
+                                          const uint64_t* qv, const uint32_t* qc, uint32_t head, uint32_t count,
+                                          const float* sbk, const float* sq, uint32_t lane) {
+  constexpr float kappa2 = float(G + 8) / 8388608.0f;
+  __syncwarp();  // the nibble stores of the filter pass come first
+  if (lane < count) {
+    const uint32_t i = (head + lane) & (kCap - 1);
+    const uint64_t v = qv[i];
+    const uint32_t cand = qc[i];
+    const float4* src = reinterpret_cast<const float4*>(x + v * G);
+    float xr[G];
+    float2 n2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int kc = 0; kc < G / 4; ++kc) {
+      const float4 t = __ldg(src + kc);
+      xr[4 * kc] = t.x;
+      xr[4 * kc + 1] = t.y;
+      xr[4 * kc + 2] = t.z;
+      xr[4 * kc + 3] = t.w;
+      n2 = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2);
+      n2 = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2);
+    }
+    const float scale = n2.x + n2.y + Book::cmax2();
+    const float inf = __int_as_float(0x7f800000);
+    float f[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = inf;
+    float fb = inf;
+    for (uint32_t m = cand; m; m &= m - 1u) {
+      const int e = __ffs(m) - 1;
+      const float* ce = sbk + e * G;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < G / 4; ++kc) {
+        const float4 c4 = *reinterpret_cast<const float4*>(ce + 4 * kc);
+        a0 = fmaf(xr[4 * kc], c4.x, a0);
+        a1 = fmaf(xr[4 * kc + 1], c4.y, a1);
+        a2 = fmaf(xr[4 * kc + 2], c4.z, a2);
+        a3 = fmaf(xr[4 * kc + 3], c4.w, a3);
+      }
+      const float fe = fmaf(-2.f, (a0 + a1) + (a2 + a3), sq[e]);
+      fb = fminf(fb, fe);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) f[t] = t == e ? fe : f[t];
+    }
+    const float thr = fmaf(2.f, fmaf(kappa2, scale, 1e-37f), fb);
+    uint32_t c2 = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) c2 |= uint32_t(f[e] <= thr) << e;
+    c2 &= cand;
+    uint32_t idx;
+    if (finite32(thr) && c2 != 0u && (c2 & (c2 - 1u)) == 0u)
+      idx = uint32_t(__ffs(c2) - 1);
+    else
+      idx = enc_exact_mem<G, Book>(x + v * G, G, finite32(thr) && c2 ? c2 : cand);
+    if (idx) atomicOr(codes + v / 8, idx << (4 * uint32_t(v % 8)));
+  }
+  __syncwarp();
+}
+
+}  // namespace tc
+
+template <int G, int SLOT>
+__global__ void __launch_bounds__(tc::Cfg<G>::kThreads, 2) k_encode_tc(const __grid_constant__ CUtensorMap tmap,
+                                                                      const float* __restrict__ x, uint64_t n,
+                                                                      uint32_t* __restrict__ codes,
+                                                                      uint32_t* __restrict__ status) {
+  using Book = CBook<G, SLOT, 0>;
+  using W = tc::Swz<G>;
+  using K = tc::Cfg<G>;
+  constexpr int S = K::S, C = K::C, H = K::H, kChunks = G / 4;
+  constexpr uint32_t kCap = K::kCap;
+  extern __shared__ unsigned char tc_smem[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem) + 1023) & ~uintptr_t(1023));
+  unsigned char* ring = base;
+  unsigned char* bmat = base + S * K::kTile;             // 16 tf32 book rows, swizzled
+  float* sbk = reinterpret_cast<float*>(bmat + 2048);    // the FP32 book, row-major
+  float* sq = sbk + 16 * G;                               // its 16 squared norms
+  __shared__ __align__(8) uint64_t full[S], sfree[S], done[C], afree[C];
+  __shared__ uint32_t tmem_base;
+  __shared__ uint64_t q_vec[4 * C][kCap];
+  __shared__ uint32_t q_cand[4 * C][kCap];
+  const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
+  const uint64_t vectors = (n + G - 1) / G, complete = n / G, words = (vectors + 7) / 8;
+  const uint64_t tiles = (vectors + 128 * H - 1) / (128 * H);
+  const uint32_t T = tiles > blockIdx.x ? uint32_t((tiles - blockIdx.x + gridDim.x - 1) / gridDim.x) : 0u;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(&tmem_base)),
+                 "r"(K::kCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      tc::mb_init(&full[s], 1);
+      tc::mb_init(&sfree[s], 128 + 1);  // the owning quad's reads and the MMA's completion
+    }
+    for (int b = 0; b < C; ++b) {
+      tc::mb_init(&done[b], 1);
+      tc::mb_init(&afree[b], 128);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (tid < 16 * kChunks) {
+    const uint32_t e = tid / kChunks, kc = tid % kChunks;
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = Book::at(int(e), int(kc * 4 + i));
+    *reinterpret_cast<float4*>(bmat + W::off(e, kc)) =
+        make_float4(tc::tf32_rna(c[0]), tc::tf32_rna(c[1]), tc::tf32_rna(c[2]), tc::tf32_rna(c[3]));
+    *reinterpret_cast<float4*>(sbk + e * G + kc * 4) = make_float4(c[0], c[1], c[2], c[3]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
+  }
+  if (tid < 4) *reinterpret_cast<float4*>(sq + 4 * tid) = Book::metaq(int(tid));
+  if (blockIdx.x == 0 && tid == 0 && Book::bad()) atomicOr(status, kNonfinite);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  bool ok = true;
+
+  if (warp == 4 * C) {
+    // producer: one TMA tensor load (two for 512-row tiles) per tile
+    if (lane == 0) {
+      uint32_t issued = 0;
+      for (uint32_t k = 0; k < T && ok; ++k) {
+        const uint32_t s = k % S;
+        if (k >= S && !(ok = tc::mb_wait(&sfree[s], ((k / S) - 1) & 1))) break;
+        ++issued;
+        tc::mb_expect(&full[s], K::kTile);
+        const int32_t row = int32_t((blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H);
+#pragma unroll
+        for (int part = 0; part < (H > 2 ? H / 2 : 1); ++part)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+                  "r"(tc::smem_u32(ring + s * K::kTile + part * 2 * K::kSub)),
+              "l"(&tmap), "r"(0), "r"(row + part * 256), "r"(tc::smem_u32(&full[s]))
+              : "memory");
+      }
+      if (!ok) atomicOr(status, kStalled);
+      // the loads in flight land before the block may exit
+      for (uint32_t k = issued > uint32_t(S) ? issued - S : 0u; k < issued; ++k)
+        if (!tc::mb_wait(&full[k % S], (k / S) & 1)) atomicOr(status, kStalled);
+    }
+  } else if (warp == 4 * C + 1) {
+    // MMA issuer
+    if (lane == 0) {
+      const uint32_t b_addr = tc::smem_u32(bmat);
+      for (uint32_t k = 0; k < T && ok; ++k) {
+        const uint32_t s = k % S, q = k % C;
+        if (!(ok = tc::mb_wait(&full[s], (k / S) & 1))) break;
+        if (k >= C && !(ok = tc::mb_wait(&afree[q], ((k / C) - 1) & 1))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          const uint32_t d = tmem + (q * H + h) * 16u;
+          const uint32_t a = tc::smem_u32(ring + s * K::kTile + h * K::kSub);
+#pragma unroll
+          for (int ks = 0; ks < G / 8; ++ks)
+            asm volatile(
+                "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d),
+                "l"(W::desc(a + ks * 32u)), "l"(W::desc(b_addr + ks * 32u)), "r"(tc::kIdescM128N16), "r"(uint32_t(ks))
+                : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         tc::smem_u32(&done[q]))
+                     : "memory");
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         tc::smem_u32(&sfree[s]))
+                     : "memory");
+      }
+      if (!ok) atomicOr(status, kStalled);
+      // the last MMAs complete before TMEM is released
+      for (uint32_t k = T > uint32_t(C) ? T - C : 0u; ok && k < T; ++k)
+        if (!tc::mb_wait(&done[k % C], (k / C) & 1)) atomicOr(status, kStalled);
+    }
+  } else {
+    // consumer quad q: TMEM lanes 32 (warp % 4) .. + 31, one vector per lane per sub-tile
+    const uint32_t q = warp / 4, row = tid & 127, wq = warp & 3;
+    constexpr float kappa1 = 1.0f / 1024 + 1.0f / 2048 + float(G + 8) / 2097152.0f;
+    uint32_t qhead = 0, qtail = 0;
+    for (uint32_t k = q; k < T && ok; k += C) {
+      const uint32_t s = k % S;
+      if (!(ok = tc::mb_wait(&full[s], (k / S) & 1))) break;
+      if (!(ok = tc::mb_wait(&done[q], (k / C) & 1))) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+      for (int h = 0; h < H; ++h) {
+        uint32_t r[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(tmem + ((wq * 32u) << 16) + (q * H + h) * 16u));
+        // ||x||^2 in enc_vector's order, from the swizzled tile (conflict-free)
+        const unsigned char* tile = ring + s * K::kTile + h * K::kSub;
+        float2 n2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int kc = 0; kc < kChunks; ++kc) {
+          const float4 t = *reinterpret_cast<const float4*>(tile + W::off(row, kc));
+          n2 = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2);
+          n2 = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2);
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const uint64_t vbase = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h * 128;
+        const uint64_t v = vbase + row;
+        uint32_t idx = 0, bits = 0, cand = 0;
+        bool defer = false;
+        if (v < complete) {
+          float f[16];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            const float2 t = __ffma2_rn(make_float2(-2.f, -2.f),
+                                        make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1])),
+                                        Book::qpair(p));
+            f[2 * p] = t.x;
+            f[2 * p + 1] = t.y;
+          }
+          float lo[8];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
+#pragma unroll
+          for (int w = 4; w; w >>= 1)
+#pragma unroll
+            for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
+          const float fb = lo[0];
+          const float thr = fmaf(2.f, fmaf(kappa1, n2.x + n2.y + Book::cmax2(), 0x1p-118f), fb);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
+          cand &= Book::uniq();
+          const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
+          if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
+            idx = uint32_t(__ffs(cand) - 1);
+          } else if (clean && cand != 0u) {
+            defer = true;
+          } else {
+            const float* src = x + v * G;
+            for (int j = 0; j < G; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+            idx = enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
+          }
+        } else if (v < vectors) {
+          // the partial last vector: its valid components only (vq.py:171-172)
+          const int valid = int(n - v * G);
+          const float* src = x + v * G;
+          for (int j = 0; j < valid; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+          idx = enc_exact_mem<G, Book>(src, valid, 0xffffu);
+        }
+        const uint32_t dm = __ballot_sync(0xffffffffu, defer);
+        if (defer) {
+          const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
+          q_vec[warp][pos] = v;
+          q_cand[warp][pos] = cand;
+        }
+        qtail += __popc(dm);
+        const uint32_t w = pack_nibbles(idx);
+        const uint64_t word = (vbase + wq * 32) / 8 + lane / 8;
+        if ((lane & 7) == 0 && word < words) codes[word] = w;
+        flag_warp(status, bits);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      tc::mb_arrive(&afree[q]);
+      tc::mb_arrive(&sfree[s]);
+      // refine off the pipeline's critical path, 32 vectors at a time
+      while (qtail - qhead >= 32u) {
+        tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, 32u, sbk, sq, lane);
+        qhead += 32u;
+      }
+    }
+    if (ok && qtail != qhead)
+      tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, qtail - qhead, sbk, sq, lane);
+    if (!ok) atomicOr(status, kStalled);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(K::kCols));
 }
 
 // ------------------------------------------- shader-exact packed-pair matmul --
@@ -1059,9 +1451,9 @@ uint32_t grid_for(uint64_t items, int per_sm = 8) {
 }
 
 template <typename Kernel>
-int resident_per_sm(Kernel k, size_t smem) {
+int resident_per_sm(Kernel k, size_t smem, int threads = kThreads) {
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess || n < 1) n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, smem) != cudaSuccess || n < 1) n = 1;
   return n;
 }
 
@@ -1168,12 +1560,50 @@ struct RunDecode {
   }
 };
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on the driver library); null if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// The tensor map of x as rows of G floats (its complete vectors), boxes of
+// the encode tile's rows, swizzled to the rows' width.
+template <int G>
+bool encode_tensor_map(const float* x, uint64_t complete, CUtensorMap* map) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(G), cuuint64_t(complete)};
+  const cuuint64_t strides[1] = {cuuint64_t(G) * sizeof(float)};
+  const cuuint32_t box[2] = {cuuint32_t(G), tc::Cfg<G>::kBoxRows};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUtensorMapSwizzle sw =
+      G == 8 ? CU_TENSOR_MAP_SWIZZLE_32B : (G == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int G>
 struct RunEncode {
   static cudaError_t run(const float* x, uint64_t n, const float* book, uint32_t* codes, uint32_t* status,
                          cudaStream_t s) {
     const uint64_t vectors = (n + G - 1) / G;
     const bool vec = aligned16(x);
+    // tensor-core path: 16-byte aligned rows, at least one complete vector,
+    // row coordinates within the TMA's signed 32 bits
+    if (vec && n / G >= 1 && vectors < (uint64_t(1) << 31) - 1024) {
+      CUtensorMap map;
+      if (encode_tensor_map<G>(x, n / G, &map)) return run_tc(map, x, n, book, codes, status, s);
+    }
     if constexpr (G == 32) {
       if (vec) return run_async(x, n, book, codes, status, s);
     }
@@ -1183,6 +1613,34 @@ struct RunEncode {
 #define ACK_LAUNCH_ENCODE(S)                                                                 \
   if (vec) k_encode<G, S, true><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status);  \
   else k_encode<G, S, false><<<uint32_t(grid), kThreads, 0, s>>>(x, n, codes, status)
+    ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
+#undef ACK_LAUNCH_ENCODE
+    const cudaError_t e = cudaGetLastError();
+    const cudaError_t r = slot.release();
+    return e != cudaSuccess ? e : r;
+  }
+
+  static cudaError_t run_tc(const CUtensorMap& map, const float* x, uint64_t n, const float* book, uint32_t* codes,
+                            uint32_t* status, cudaStream_t s) {
+    using K = tc::Cfg<G>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+#define ACK_TC_ATTR(S)                                                                                    \
+  if (attr == cudaSuccess)                                                                                \
+    attr = cudaFuncSetAttribute(k_encode_tc<G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(K::kSmem));
+      ACK_TC_ATTR(0) ACK_TC_ATTR(1) ACK_TC_ATTR(2) ACK_TC_ATTR(3)
+      ACK_TC_ATTR(4) ACK_TC_ATTR(5) ACK_TC_ATTR(6) ACK_TC_ATTR(7)
+#undef ACK_TC_ATTR
+    });
+    if (attr != cudaSuccess) return attr;
+    const uint64_t vectors = (n + G - 1) / G;
+    const uint64_t tiles = (vectors + 128 * K::H - 1) / (128 * K::H);
+    const int per_sm = resident_per_sm(k_encode_tc<G, 0>, K::kSmem, K::kThreads);
+    const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sm_count()) * per_sm));
+    BookSlot slot(s, book, 1, G);
+    if (slot.error() != cudaSuccess) return slot.error();
+#define ACK_LAUNCH_ENCODE(S) k_encode_tc<G, S><<<grid, K::kThreads, K::kSmem, s>>>(map, x, n, codes, status)
     ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
 #undef ACK_LAUNCH_ENCODE
     const cudaError_t e = cudaGetLastError();

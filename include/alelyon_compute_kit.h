@@ -61,6 +61,9 @@ typedef struct AckBuffer AckBuffer;
 #define ACK_VQ_STATUS_NONFINITE 1u
 #define ACK_VQ_STATUS_LAYOUT 2u
 #define ACK_VQ_STATUS_OPTIMIZER 4u
+/* B200 extension, no reference counterpart: a pipelined kernel's bounded
+ * wait on one of its own barriers ran out; the outputs are not valid. */
+#define ACK_VQ_STATUS_STALLED 8u
 
 /* What ack_abi_info reports (ffi.rs:1009-1057, 96 bytes, same layout). This
  * library carries none of the reference's twelve dense operator families, so
