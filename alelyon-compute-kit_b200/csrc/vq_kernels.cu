@@ -360,7 +360,7 @@ __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity) {
 template <int G>
 struct Cfg {
   static constexpr int S = 4, C = 2, H = G == 8 ? 4 : (G == 16 ? 2 : 1);
-  static constexpr int kThreads = 128 * C + 64;
+  static constexpr int kThreads = 128 * C + 64, kBlocksPerSm = 2;
   static constexpr uint32_t kSub = 128u * G * 4u, kTile = kSub * H;
   static constexpr uint32_t kBoxRows = H > 2 ? 256u : 128u * H;
   static constexpr uint32_t kCols = C * H * 16 <= 32 ? 32u : (C * H * 16 <= 64 ? 64u : 128u);
@@ -438,10 +438,9 @@ __device__ __noinline__ void refine_queue(const float* __restrict__ x, uint32_t*
 }  // namespace tc
 
 template <int G, int SLOT>
-__global__ void __launch_bounds__(tc::Cfg<G>::kThreads, 2) k_encode_tc(const __grid_constant__ CUtensorMap tmap,
-                                                                      const float* __restrict__ x, uint64_t n,
-                                                                      uint32_t* __restrict__ codes,
-                                                                      uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm)
+    k_encode_tc(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ x, uint64_t n,
+                uint32_t* __restrict__ codes, uint32_t* __restrict__ status) {
   using Book = CBook<G, SLOT, 0>;
   using W = tc::Swz<G>;
   using K = tc::Cfg<G>;
@@ -1626,9 +1625,12 @@ struct RunEncode {
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
-#define ACK_TC_ATTR(S)                                                                                    \
-  if (attr == cudaSuccess)                                                                                \
-    attr = cudaFuncSetAttribute(k_encode_tc<G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(K::kSmem));
+#define ACK_TC_ATTR(S)                                                                                      \
+  if (attr == cudaSuccess)                                                                                  \
+    attr = cudaFuncSetAttribute(k_encode_tc<G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(K::kSmem)); \
+  if (attr == cudaSuccess)                                                                                  \
+    attr = cudaFuncSetAttribute(k_encode_tc<G, S>, cudaFuncAttributePreferredSharedMemoryCarveout,          \
+                                int(cudaSharedmemCarveoutMaxShared));
       ACK_TC_ATTR(0) ACK_TC_ATTR(1) ACK_TC_ATTR(2) ACK_TC_ATTR(3)
       ACK_TC_ATTR(4) ACK_TC_ATTR(5) ACK_TC_ATTR(6) ACK_TC_ATTR(7)
 #undef ACK_TC_ATTR
@@ -1636,8 +1638,10 @@ struct RunEncode {
     if (attr != cudaSuccess) return attr;
     const uint64_t vectors = (n + G - 1) / G;
     const uint64_t tiles = (vectors + 128 * K::H - 1) / (128 * K::H);
-    const int per_sm = resident_per_sm(k_encode_tc<G, 0>, K::kSmem, K::kThreads);
-    const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sm_count()) * per_sm));
+    // two blocks per SM by design (registers and shared memory both allow
+    // exactly two); blocks are independent, so an SM that holds fewer only
+    // runs the rest later
+    const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sm_count()) * K::kBlocksPerSm));
     BookSlot slot(s, book, 1, G);
     if (slot.error() != cudaSuccess) return slot.error();
 #define ACK_LAUNCH_ENCODE(S) k_encode_tc<G, S><<<grid, K::kThreads, K::kSmem, s>>>(map, x, n, codes, status)
