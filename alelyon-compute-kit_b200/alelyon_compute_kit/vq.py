@@ -652,7 +652,10 @@ class VQDevice:
         a grouped product that runs many times (serving, a training step).
         `layout="tile32"` (matrices stored N x K with (K / group) % 32 == 0)
         repacks the codes on the device into the layout whose rows a warp
-        reads as coalesced lines; "canonical" keeps the wire layout."""
+        reads as coalesced lines; "canonical" keeps the wire layout. For
+        single-row products (M = 1) with K a multiple of 256 * group the
+        canonical layout is the faster one: it feeds the byte-pair table
+        kernel (one lookup per code byte); tile32 is faster for M >= 2."""
         return ResidentStack(self, stack, layout)
 
     def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True, out: np.ndarray | None = None) -> np.ndarray:

@@ -1072,6 +1072,191 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
   }
 }
 
+// ------------------------------- dense X times coded W^T, M = 1: byte table --
+//
+// k_dense_pair: one lookup per code BYTE. For a K-chunk of 256 groups (128
+// code bytes per row), Q[p][b] = P[2p][b & 15] + P[2p+1][b >> 4] with
+// P[t][e] = x_t . c_e (256 x 16 FP32 dot products), 128 pairs x 256 bytes =
+// 128 KB of shared memory. A warp takes 32 rows at a time; lane i loads word
+// i of every row (one coalesced 128-byte line per row) and so always looks up
+// pairs 4i..4i+3. Q is laid out so that lane i's entries live in bank i:
+// word(i, j, b) = 64 b + 32 (j & 1) + i + 16384 (j >> 1) for pair 4i + j,
+// and one byte permute of the code word with a per-lane base forms each
+// byte address. Lane sums are folded across the warp by a 32 x 32
+// transpose-reduction (31 shuffles), after which lane r holds row r.
+//
+// One block of 16 warps per SM, persistent over (expert, 32-row batch)
+// units; the next unit range's x chunk and book are prefetched with
+// cp.async while the current one is looked up. Each row sums its 128 pair
+// values per chunk in a fixed order (pairs, then a tree over lanes); chunks
+// add in order, so the result does not depend on the grid.
+namespace pair {
+
+constexpr int kWarps = 16, kThreads = kWarps * 32, kRows = 32;
+constexpr uint32_t kQFloats = 128u * 256u;         // the byte table
+constexpr uint32_t kPFloats = 256u * 16u + 32u;    // P, one pad word per 8 groups
+__device__ __forceinline__ uint32_t p_index(uint32_t t, uint32_t c) { return t * 16u + c + (t >> 3); }
+
+template <int G>
+constexpr size_t smem_bytes() {
+  return (size_t(kQFloats) + kPFloats + 2 * (256 * G + 16 * G)) * sizeof(float);
+}
+
+}  // namespace pair
+
+template <int G>
+__global__ void __launch_bounds__(pair::kThreads, 1)
+    k_dense_pair(const float* __restrict__ X, const uint32_t* __restrict__ codes, const float* __restrict__ books,
+                 float* __restrict__ Y, uint32_t N, uint32_t K, uint32_t E, uint64_t words_per_expert,
+                 uint32_t* __restrict__ status) {
+  constexpr uint32_t kChunkX = 256u * G, kBook = 16u * G;
+  extern __shared__ __align__(16) float pair_smem[];
+  float* Q = pair_smem;
+  float* P = Q + pair::kQFloats;
+  float* xbuf = P + pair::kPFloats;  // [2][kChunkX + kBook]: x chunk, then the book
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t chunks = K / kChunkX, row_words = K / G / 8;
+  const uint32_t nb = (N + pair::kRows - 1) / pair::kRows;  // 32-row batches per expert
+  const uint64_t U = uint64_t(E) * nb;
+  const uint64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+  if (u0 >= u1) return;
+  // byte 0: 4 i (slots 0, 2) or 4 i + 128 (slots 1, 3); byte 2: 0 or 1 (x 64 KB)
+  const uint32_t base = (lane * 4u) | ((lane * 4u + 128u) << 8) | (1u << 24);
+
+  // the work list: (segment of one expert's units, chunk) in order
+  auto seg_end = [&](uint64_t s) { return min(u1, (s / nb + 1) * nb); };
+  auto prefetch = [&](uint64_t s, uint32_t c, int buf) {
+    const uint32_t e = uint32_t(s / nb);
+    float* dst = xbuf + buf * (kChunkX + kBook);
+    const float* xs = X + uint64_t(e) * K + uint64_t(c) * kChunkX;
+    const float* bs = books + uint64_t(e) * kBook;
+    for (uint32_t i = tid; i < (kChunkX + kBook) / 4; i += pair::kThreads) {
+      const float* src = i < kChunkX / 4 ? xs + 4 * i : bs + 4 * (i - kChunkX / 4);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                       __cvta_generic_to_shared(dst + 4 * i))),
+                   "l"(src)
+                   : "memory");
+    }
+  };
+  uint64_t s0 = u0;
+  uint32_t c = 0;
+  int buf = 0;
+  prefetch(s0, 0, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  while (s0 < u1) {
+    const uint64_t s1 = seg_end(s0);
+    const uint32_t e = uint32_t(s0 / nb);
+    // the next (segment, chunk)'s x and book, in flight during this one
+    {
+      uint64_t ns = s0;
+      uint32_t nc = c + 1;
+      if (nc == chunks) {
+        nc = 0;
+        ns = s1;
+      }
+      if (ns < u1) prefetch(ns, nc, buf ^ 1);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();  // this chunk's x and book are in; Q is no longer read
+    const float* xs = xbuf + buf * (kChunkX + kBook);
+    const float* bk = xs + kChunkX;
+    if (c == 0 && s0 % nb == 0) {  // the expert's first unit reports a nonfinite book
+      uint32_t bits = 0;
+      for (uint32_t i = tid; i < kBook; i += pair::kThreads) bits |= finite32(bk[i]) ? 0u : kNonfinite;
+      flag_warp(status, bits);
+    }
+    {
+      // P[t][e]: thread owns entry tid % 16 (its book row in registers)
+      const uint32_t ce = tid & 15;
+      float br[G];
+#pragma unroll
+      for (int j = 0; j < G; ++j) br[j] = bk[ce * G + j];
+      for (uint32_t t = tid >> 4; t < 256u; t += pair::kThreads / 16) {
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < G; j += 4) {
+          const float4 x4 = *reinterpret_cast<const float4*>(xs + t * G + j);
+          a = fmaf(x4.x, br[j], a);
+          a = fmaf(x4.y, br[j + 1], a);
+          a = fmaf(x4.z, br[j + 2], a);
+          a = fmaf(x4.w, br[j + 3], a);
+        }
+        P[pair::p_index(t, ce)] = a;
+      }
+    }
+    __syncthreads();
+    // Q: a thread holds P[2p][0..15] and fills one high nibble; lane = slot i,
+    // so both the P loads and the Q stores are conflict-free
+    for (uint32_t task = tid; task < 128u * 16u; task += pair::kThreads) {
+      const uint32_t i = task & 31, j = (task >> 5) & 3, hi = task >> 7;
+      const uint32_t p = 4 * i + j;
+      float lo[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) lo[k] = P[pair::p_index(2 * p, k)];
+      const float hv = P[pair::p_index(2 * p + 1, hi)];
+      float* q = Q + (j & 1u) * 32u + i + (j >> 1) * 16384u + hi * 16u * 64u;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) q[k * 64] = lo[k] + hv;
+    }
+    __syncthreads();
+
+    // codes of this (expert, chunk): a warp-uniform base, 32-bit lane offsets
+    const uint32_t* cb = codes + uint64_t(e) * words_per_expert + uint64_t(c) * 32u;
+    float* ye = Y + uint64_t(e) * N;
+    uint64_t u = s0 + warp;
+    uint32_t w[pair::kRows];
+    auto load = [&](uint64_t unit) {
+      const uint32_t n0 = uint32_t(unit % nb) * pair::kRows;
+      const uint32_t off = n0 * row_words + lane;
+      if (n0 + pair::kRows <= N) {
+#pragma unroll
+        for (int r = 0; r < pair::kRows; ++r) w[r] = __ldcs(cb + off + uint32_t(r) * row_words);
+      } else {
+#pragma unroll
+        for (int r = 0; r < pair::kRows; ++r) w[r] = n0 + r < N ? __ldcs(cb + off + uint32_t(r) * row_words) : 0u;
+      }
+    };
+    if (u < s1) load(u);
+    for (; u < s1; u += pair::kWarps) {
+      const uint32_t n0 = uint32_t(u % nb) * pair::kRows;
+      float v[pair::kRows];
+#pragma unroll
+      for (int r = 0; r < pair::kRows; ++r) {
+        const char* qb = reinterpret_cast<const char*>(Q);
+        const float q0 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6604));
+        const float q1 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6615));
+        const float q2 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6724));
+        const float q3 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6735));
+        v[r] = (q0 + q1) + (q2 + q3);
+      }
+      if (u + pair::kWarps < s1) load(u + pair::kWarps);  // in flight during the folding
+      // fold lanes: each step halves the rows a lane keeps; after five, lane l holds row l
+#pragma unroll
+      for (int off = pair::kRows / 2; off; off >>= 1) {
+        const bool up = lane & off;
+#pragma unroll
+        for (int k = 0; k < off; ++k) {
+          const float send = up ? v[k] : v[k + off];
+          const float keep = up ? v[k + off] : v[k];
+          v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      if (n0 + lane < N) {  // lane l now holds row n0 + l
+        float* y = ye + n0 + lane;
+        *y = c == 0 ? v[0] : *y + v[0];
+      }
+    }
+    // advance: the next chunk of this segment, or the next segment
+    if (++c == chunks) {
+      c = 0;
+      s0 = s1;
+    }
+    buf ^= 1;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------ coded A times coded B^T (LUT) --
 
 // C[m, n] = sum_t L[a(m,t)][b(n,t)] with L = C_A C_B^T (16 x 16, each entry
@@ -1760,6 +1945,35 @@ cudaError_t launch_t32_mc(const float* X, const uint4* codes, const float* books
   return launch_dense_t32<G, MC, 32>(X, codes, books, Y, M, N, K, batch, status, s);
 }
 
+// M = 1 with K a multiple of 256 g: the byte-table kernel, one block per SM.
+// Worth its 128 KB table per (expert, K-chunk) only with enough rows: at
+// least 4 batches of 32 rows per block and 256 rows per expert.
+template <int G>
+bool dense_pair_fits(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, const float* X, const float* books) {
+  const uint64_t units = uint64_t(batch) * ((N + pair::kRows - 1) / pair::kRows);
+  return M == 1 && K % (256u * G) == 0 && N >= 256 && units >= 4ull * uint64_t(sm_count()) && aligned16(X) &&
+         aligned16(books) && uint64_t(N) * (K / G / 8) < (uint64_t(1) << 31);  // 32-bit word offsets
+}
+
+template <int G>
+cudaError_t launch_dense_pair(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t N,
+                              uint32_t K, uint32_t batch, uint64_t words, uint32_t* status, cudaStream_t s) {
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(k_dense_pair<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(pair::smem_bytes<G>()));
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(k_dense_pair<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  int(cudaSharedmemCarveoutMaxShared));
+  });
+  if (attr != cudaSuccess) return attr;
+  const uint64_t units = uint64_t(batch) * ((N + pair::kRows - 1) / pair::kRows);
+  const uint32_t grid = uint32_t(std::min<uint64_t>(units, uint64_t(sm_count())));
+  k_dense_pair<G><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words, status);
+  return cudaGetLastError();
+}
+
 template <int G>
 struct RunDense {
   static cudaError_t run(const Plan& p, void* const* ptr, cudaStream_t s) {
@@ -1778,6 +1992,8 @@ struct RunDense {
       if (M == 2) return launch_t32_mc<G, 2>(X, c4, books, Y, M, N, K, p.batch, status, s);
       return launch_t32_mc<G, 4>(X, c4, books, Y, M, N, K, p.batch, status, s);  // M > 4: chunks of 4 rows
     }
+    if (nt && dense_pair_fits<G>(M, N, K, p.batch, X, books))
+      return launch_dense_pair<G>(X, codes, books, Y, N, K, p.batch, words, status, s);
     if (nt && K % G == 0 && (K / G) % 32 == 0 && aligned16(codes) && (words * 4) % 16 == 0) {
       if (M == 1) return launch_dense_mc<G, 1>(X, codes, books, Y, M, N, K, p.batch, words, status, s);
       if (M == 2) return launch_dense_mc<G, 2>(X, codes, books, Y, M, N, K, p.batch, words, status, s);

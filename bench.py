@@ -210,7 +210,8 @@ def run_cfg2(args, world, rank, local):
     codes, books, x, book = make_cfg2(torch, cuda, vq, experts, m, device)
     y = torch.empty((experts, m, N_ROWS), dtype=torch.float32, device=device)
     status = cuda.status_word(device)
-    layout = args.layout
+    layout = args.layout if args.layout != "auto" else ("canonical" if m == 1 else "tile32")
+    args.layout = layout
     if layout == "tile32":
         # resident weights are repacked once into the tile32 layout (outside the timed region)
         codes_canonical = codes
@@ -252,7 +253,7 @@ def run_cfg2(args, world, rank, local):
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
     achieved = algorithmic / (ms_step / 1e3) / 1e9
-    kernel = "k_dense_t32" if layout == "tile32" else "k_dense_lut"
+    kernel = "k_dense_t32" if layout == "tile32" else ("k_dense_pair" if m == 1 else "k_dense_lut")
     traffic_name = f"{kernel}_cfg2_m{m}"
     traffic = profile_traffic(traffic_name)
     result = {
@@ -633,7 +634,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--group", type=int, default=16)
-    ap.add_argument("--layout", choices=("tile32", "canonical"), default="tile32")
+    ap.add_argument("--layout", choices=("auto", "tile32", "canonical"), default="auto",
+                    help="auto: canonical for M = 1 (the byte-table kernel), tile32 otherwise")
     ap.add_argument("--values", type=int, default=1 << 30)
     ap.add_argument("--dist", choices=("gauss", "heavy"), default="gauss")
     ap.add_argument("--experts-cfg4", type=int, default=8)
