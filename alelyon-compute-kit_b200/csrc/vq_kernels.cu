@@ -1097,14 +1097,18 @@ constexpr uint32_t kQFloats = 128u * 256u;         // the byte table
 constexpr uint32_t kPFloats = 256u * 16u + 32u;    // P, one pad word per 8 groups
 __device__ __forceinline__ uint32_t p_index(uint32_t t, uint32_t c) { return t * 16u + c + (t >> 3); }
 
+// Table, P and one x-chunk buffer (the next chunk is prefetched into it once
+// P is built): 161 KB for g16, so the 164 KB shared-memory configuration
+// leaves ~92 KB of L1 for the code loads in flight (the largest carveout
+// measured 6% slower).
 template <int G>
 constexpr size_t smem_bytes() {
-  return (size_t(kQFloats) + kPFloats + 2 * (256 * G + 16 * G)) * sizeof(float);
+  return (size_t(kQFloats) + kPFloats + 256 * G + 16 * G) * sizeof(float);
 }
 
 }  // namespace pair
 
-template <int G>
+template <int G, bool ONE>  // ONE: K = 256 G, one chunk (32-word rows, a compile-time stride)
 __global__ void __launch_bounds__(pair::kThreads, 1)
     k_dense_pair(const float* __restrict__ X, const uint32_t* __restrict__ codes, const float* __restrict__ books,
                  float* __restrict__ Y, uint32_t N, uint32_t K, uint32_t E, uint64_t words_per_expert,
@@ -1113,9 +1117,9 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   extern __shared__ __align__(16) float pair_smem[];
   float* Q = pair_smem;
   float* P = Q + pair::kQFloats;
-  float* xbuf = P + pair::kPFloats;  // [2][kChunkX + kBook]: x chunk, then the book
+  float* xbuf = P + pair::kPFloats;  // x chunk, then the book
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t chunks = K / kChunkX, row_words = K / G / 8;
+  const uint32_t chunks = ONE ? 1u : K / kChunkX, row_words = ONE ? 32u : K / G / 8;
   const uint32_t nb = (N + pair::kRows - 1) / pair::kRows;  // 32-row batches per expert
   const uint64_t U = uint64_t(E) * nb;
   const uint64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
@@ -1125,9 +1129,9 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
 
   // the work list: (segment of one expert's units, chunk) in order
   auto seg_end = [&](uint64_t s) { return min(u1, (s / nb + 1) * nb); };
-  auto prefetch = [&](uint64_t s, uint32_t c, int buf) {
+  auto prefetch = [&](uint64_t s, uint32_t c) {
     const uint32_t e = uint32_t(s / nb);
-    float* dst = xbuf + buf * (kChunkX + kBook);
+    float* dst = xbuf;
     const float* xs = X + uint64_t(e) * K + uint64_t(c) * kChunkX;
     const float* bs = books + uint64_t(e) * kBook;
     for (uint32_t i = tid; i < (kChunkX + kBook) / 4; i += pair::kThreads) {
@@ -1140,26 +1144,14 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   };
   uint64_t s0 = u0;
   uint32_t c = 0;
-  int buf = 0;
-  prefetch(s0, 0, 0);
+  prefetch(s0, 0);
   asm volatile("cp.async.commit_group;" ::: "memory");
   while (s0 < u1) {
     const uint64_t s1 = seg_end(s0);
     const uint32_t e = uint32_t(s0 / nb);
-    // the next (segment, chunk)'s x and book, in flight during this one
-    {
-      uint64_t ns = s0;
-      uint32_t nc = c + 1;
-      if (nc == chunks) {
-        nc = 0;
-        ns = s1;
-      }
-      if (ns < u1) prefetch(ns, nc, buf ^ 1);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // this chunk's x and book are in; Q is no longer read
-    const float* xs = xbuf + buf * (kChunkX + kBook);
+    const float* xs = xbuf;
     const float* bk = xs + kChunkX;
     if (c == 0 && s0 % nb == 0) {  // the expert's first unit reports a nonfinite book
       uint32_t bits = 0;
@@ -1186,6 +1178,18 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       }
     }
     __syncthreads();
+    {
+      // x is read: the next (segment, chunk)'s x and book, in flight during
+      // the table build and the lookups
+      uint64_t ns = s0;
+      uint32_t nc = c + 1;
+      if (nc == chunks) {
+        nc = 0;
+        ns = s1;
+      }
+      if (ns < u1) prefetch(ns, nc);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     // Q: a thread holds P[2p][0..15] and fills one high nibble; lane = slot i,
     // so both the P loads and the Q stores are conflict-free
     for (uint32_t task = tid; task < 128u * 16u; task += pair::kThreads) {
@@ -1206,8 +1210,9 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     float* ye = Y + uint64_t(e) * N;
     uint64_t u = s0 + warp;
     uint32_t w[pair::kRows];
+    const uint64_t first = uint64_t(e) * nb;  // units of this segment are one expert's
     auto load = [&](uint64_t unit) {
-      const uint32_t n0 = uint32_t(unit % nb) * pair::kRows;
+      const uint32_t n0 = uint32_t(unit - first) * pair::kRows;
       const uint32_t off = n0 * row_words + lane;
       if (n0 + pair::kRows <= N) {
 #pragma unroll
@@ -1219,7 +1224,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     };
     if (u < s1) load(u);
     for (; u < s1; u += pair::kWarps) {
-      const uint32_t n0 = uint32_t(u % nb) * pair::kRows;
+      const uint32_t n0 = uint32_t(u - first) * pair::kRows;
       float v[pair::kRows];
 #pragma unroll
       for (int r = 0; r < pair::kRows; ++r) {
@@ -1252,7 +1257,6 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       c = 0;
       s0 = s1;
     }
-    buf ^= 1;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
@@ -1961,16 +1965,21 @@ cudaError_t launch_dense_pair(const float* X, const uint32_t* codes, const float
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(k_dense_pair<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(pair::smem_bytes<G>()));
-    if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(k_dense_pair<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                  int(cudaSharedmemCarveoutMaxShared));
+    // no carveout preference: the driver takes the smallest shared-memory
+    // configuration that fits, the rest stays L1 for the code stream
+    for (auto fn : {k_dense_pair<G, true>, k_dense_pair<G, false>})
+      if (attr == cudaSuccess)
+        attr = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pair::smem_bytes<G>()));
   });
   if (attr != cudaSuccess) return attr;
   const uint64_t units = uint64_t(batch) * ((N + pair::kRows - 1) / pair::kRows);
   const uint32_t grid = uint32_t(std::min<uint64_t>(units, uint64_t(sm_count())));
-  k_dense_pair<G><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words, status);
+  if (K == 256u * G)
+    k_dense_pair<G, true><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words,
+                                                                               status);
+  else
+    k_dense_pair<G, false><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words,
+                                                                                status);
   return cudaGetLastError();
 }
 
