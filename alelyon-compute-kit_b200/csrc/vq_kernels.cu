@@ -290,6 +290,14 @@ __global__ void __launch_bounds__(kThreads, 3) k_encode_async(const float* __res
 // float64 pass over what survives, the result OR-ed into the zero nibble the
 // first pass stored. Nonfinite input or books take the float64 pass at once.
 //
+// Group 32 tightens the bound (Cfg::TIGHT, Cfg::RESID): the book enters as
+// tf32 hi and lo halves (N = 32, summed), so only x is truncated, and that
+// error is bounded by 2 ||x - trunc(x)|| max ||c|| (Cauchy-Schwarz; the
+// tensor core's operand is trunc(x) or its nearer tf32 neighbour, so the
+// residual is at most this) plus (g + 9) 2^-21 (||x||^2 + max ||c||^2) +
+// 2^-118 for accumulation, the book remainder, rounding and flushed
+// subnormals. That leaves about a quarter of the near ties.
+//
 // Every wait on an mbarrier is bounded; one that runs out sets kStalled and
 // the block drains its own copies and returns.
 namespace tc {
@@ -328,6 +336,7 @@ struct Swz {
 
 // Instruction descriptor: D FP32, A and B tf32, both K-major, N = 16, M = 128.
 constexpr uint32_t kIdescM128N16 = (1u << 4) | (2u << 7) | (2u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescM128N32 = (1u << 4) | (2u << 7) | (2u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
 
 __device__ __forceinline__ void mb_init(uint64_t* b, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
@@ -357,17 +366,24 @@ __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity) {
 
 // Stages S, consumer quads C, sub-tiles of 128 vectors per tile H (one TMA
 // box holds at most 256 rows). Measured on B200 for 2^30 values.
+// TIGHT: the book as tf32 hi and lo halves (N = 32 columns, the two summed);
+// RESID: the measured truncation residual of x in the bound instead of its
+// worst case. Both pay on g32 (4.7% near ties on smooth data otherwise);
+// on g16 and g8, with 2x and 4x the vectors per byte, the extra work per
+// vector measured slower than the refinements it saves.
 template <int G>
 struct Cfg {
   static constexpr int S = 4, C = 2, H = G == 8 ? 4 : (G == 16 ? 2 : 1);
+  static constexpr bool TIGHT = G == 32, RESID = G == 32;
+  static constexpr uint32_t kN = TIGHT ? 32u : 16u;  // accumulator columns per sub-tile
   static constexpr int kThreads = 128 * C + 64, kBlocksPerSm = 2;
   static constexpr uint32_t kSub = 128u * G * 4u, kTile = kSub * H;
   static constexpr uint32_t kBoxRows = H > 2 ? 256u : 128u * H;
-  static constexpr uint32_t kCols = C * H * 16 <= 32 ? 32u : (C * H * 16 <= 64 ? 64u : 128u);
+  static constexpr uint32_t kCols = C * H * kN <= 32 ? 32u : (C * H * kN <= 64 ? 64u : 128u);
   static constexpr uint32_t kCap = H == 1 ? 64u : (H == 2 ? 128u : 256u);  // >= 31 + 32 H: a tile never overflows it
   // dynamic shared memory: 1024-byte alignment slack, the ring, the tf32
-  // book tile (2 KB), the FP32 book and its 16 squared norms
-  static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 2048 + 16 * G * 4 + 64;
+  // book tile (kN rows, at most 4 KB), the FP32 book and its 16 squared norms
+  static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 4096 + 16 * G * 4 + 64;
 };
 
 // Deferred FP32 refinement of `count` (<= 32) queued vectors, one per lane,
@@ -450,7 +466,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem) + 1023) & ~uintptr_t(1023));
   unsigned char* ring = base;
   unsigned char* bmat = base + S * K::kTile;             // 16 tf32 book rows, swizzled
-  float* sbk = reinterpret_cast<float*>(bmat + 2048);    // the FP32 book, row-major
+  float* sbk = reinterpret_cast<float*>(bmat + 4096);    // the FP32 book, row-major
   float* sq = sbk + 16 * G;                               // its 16 squared norms
   __shared__ __align__(8) uint64_t full[S], sfree[S], done[C], afree[C];
   __shared__ uint32_t tmem_base;
@@ -482,8 +498,14 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     float c[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) c[i] = Book::at(int(e), int(kc * 4 + i));
-    *reinterpret_cast<float4*>(bmat + W::off(e, kc)) =
-        make_float4(tc::tf32_rna(c[0]), tc::tf32_rna(c[1]), tc::tf32_rna(c[2]), tc::tf32_rna(c[3]));
+    float hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hi[i] = tc::tf32_rna(c[i]);
+    *reinterpret_cast<float4*>(bmat + W::off(e, kc)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    if constexpr (K::TIGHT)  // rows 16..31: the tf32 remainder, c - hi exact in FP32
+      *reinterpret_cast<float4*>(bmat + W::off(16 + e, kc)) =
+          make_float4(tc::tf32_rna(c[0] - hi[0]), tc::tf32_rna(c[1] - hi[1]), tc::tf32_rna(c[2] - hi[2]),
+                      tc::tf32_rna(c[3] - hi[3]));
     *reinterpret_cast<float4*>(sbk + e * G + kc * 4) = make_float4(c[0], c[1], c[2], c[3]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
   }
@@ -529,13 +551,14 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
         for (int h = 0; h < H; ++h) {
-          const uint32_t d = tmem + (q * H + h) * 16u;
+          const uint32_t d = tmem + (q * H + h) * K::kN;
           const uint32_t a = tc::smem_u32(ring + s * K::kTile + h * K::kSub);
 #pragma unroll
           for (int ks = 0; ks < G / 8; ++ks)
             asm volatile(
                 "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d),
-                "l"(W::desc(a + ks * 32u)), "l"(W::desc(b_addr + ks * 32u)), "r"(tc::kIdescM128N16), "r"(uint32_t(ks))
+                "l"(W::desc(a + ks * 32u)), "l"(W::desc(b_addr + ks * 32u)),
+                "r"(K::TIGHT ? tc::kIdescM128N32 : tc::kIdescM128N16), "r"(uint32_t(ks))
                 : "memory");
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -554,6 +577,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     // consumer quad q: TMEM lanes 32 (warp % 4) .. + 31, one vector per lane per sub-tile
     const uint32_t q = warp / 4, row = tid & 127, wq = warp & 3;
     constexpr float kappa1 = 1.0f / 1024 + 1.0f / 2048 + float(G + 8) / 2097152.0f;
+    constexpr float kappa_t = float(G + 9) / 2097152.0f;  // TIGHT: all but the x residual
     uint32_t qhead = 0, qtail = 0;
     for (uint32_t k = q; k < T && ok; k += C) {
       const uint32_t s = k % S;
@@ -562,22 +586,50 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
       for (int h = 0; h < H; ++h) {
-        uint32_t r[16];
+        uint32_t r[K::kN];
+        const uint32_t taddr = tmem + ((wq * 32u) << 16) + (q * H + h) * K::kN;
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(tmem + ((wq * 32u) << 16) + (q * H + h) * 16u));
-        // ||x||^2 in enc_vector's order, from the swizzled tile (conflict-free)
+            : "r"(taddr));
+        if constexpr (K::TIGHT)
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+                "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                "=r"(r[30]), "=r"(r[31])
+              : "r"(taddr + 16u));
+        // ||x||^2 in enc_vector's order, from the swizzled tile (conflict-free);
+        // TIGHT also ||x - trunc(x)||^2, x truncated to its top 19 bits: the
+        // tensor core's operand is that or the nearer tf32 neighbour, so this
+        // bounds its residual either way
         const unsigned char* tile = ring + s * K::kTile + h * K::kSub;
-        float2 n2 = make_float2(0.f, 0.f);
+        float2 n2 = make_float2(0.f, 0.f), r2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int kc = 0; kc < kChunks; ++kc) {
           const float4 t = *reinterpret_cast<const float4*>(tile + W::off(row, kc));
           n2 = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2);
           n2 = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2);
+          if constexpr (K::RESID) {
+            const float2 a = make_float2(t.x - __uint_as_float(__float_as_uint(t.x) & 0xFFFFE000u),
+                                         t.y - __uint_as_float(__float_as_uint(t.y) & 0xFFFFE000u));
+            const float2 b = make_float2(t.z - __uint_as_float(__float_as_uint(t.z) & 0xFFFFE000u),
+                                         t.w - __uint_as_float(__float_as_uint(t.w) & 0xFFFFE000u));
+            r2 = __ffma2_rn(a, a, r2);
+            r2 = __ffma2_rn(b, b, r2);
+          }
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if constexpr (K::TIGHT) {
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float2 t = __fadd2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])),
+                                        make_float2(__uint_as_float(r[16 + e]), __uint_as_float(r[17 + e])));
+            r[e] = __float_as_uint(t.x);
+            r[e + 1] = __float_as_uint(t.y);
+          }
+        }
         const uint64_t vbase = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h * 128;
         const uint64_t v = vbase + row;
         uint32_t idx = 0, bits = 0, cand = 0;
@@ -600,7 +652,20 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
 #pragma unroll
             for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
           const float fb = lo[0];
-          const float thr = fmaf(2.f, fmaf(kappa1, n2.x + n2.y + Book::cmax2(), 0x1p-118f), fb);
+          float eps;
+          if constexpr (K::TIGHT && !K::RESID) {
+            // x truncated (2^-10) against the exactly represented book
+            eps = fmaf(1.0f / 1024 + kappa_t, n2.x + n2.y + Book::cmax2(), 0x1p-118f);
+          } else if constexpr (K::RESID) {
+            // 2 ||r|| max||c|| (rounded up, 2^-16 margin for the FP32 sum of
+            // squares) + the accumulation, book-remainder, rounding and
+            // flushed-subnormal terms
+            const float rc = __fsqrt_ru(__fmul_ru(r2.x + r2.y, Book::cmax2()));
+            eps = fmaf(2.0f + 0x1p-15f, rc, fmaf(kappa_t, n2.x + n2.y + Book::cmax2(), 0x1p-118f));
+          } else {
+            eps = fmaf(kappa1, n2.x + n2.y + Book::cmax2(), 0x1p-118f);
+          }
+          const float thr = fmaf(2.f, eps, fb);
 #pragma unroll
           for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
           cand &= Book::uniq();
