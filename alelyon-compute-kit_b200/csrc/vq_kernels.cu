@@ -1,7 +1,9 @@
 // sm_100a kernels of the vq4/v1 path and their launcher.
 //
-//   decode        HBM-write-bound gather: 128-bit streaming stores, the
-//                 codebook in shared memory (vq4.comp op 1 / vq.py:117-121)
+//   decode        HBM-write-bound gather: 128-bit streaming stores, warp
+//                 steps of 256 vectors whose code words arrive as one line
+//                 and move by shuffle, the codebook in shared memory
+//                 (vq4.comp op 1 / vq.py:117-121)
 //   encode        certified nearest entry per vector (vq4.comp op 0 /
 //                 vq.py:154-179): aligned input takes k_encode_tc (TMA tiles,
 //                 tcgen05 tf32 filter, deferred FP32 refinement of the few
@@ -40,6 +42,11 @@ constexpr int kThreads = 256;
 
 // ------------------------------------------------------------------ decode --
 
+// Warp-cooperative decode, 16-byte aligned output. A warp step covers 256
+// vectors: lane l loads code word l of the step (one coalesced 128-byte line,
+// prefetched a step ahead) and writes output quads l + 32 k (each warp store
+// a full 512-byte line). The word of quad Q comes by shuffle; its nibble
+// position and the quad within the vector depend on the lane only.
 template <int G>
 __global__ void __launch_bounds__(kThreads) k_decode(const uint32_t* __restrict__ codes,
                                                      const float* __restrict__ book, float* __restrict__ out,
@@ -54,28 +61,41 @@ __global__ void __launch_bounds__(kThreads) k_decode(const uint32_t* __restrict_
   }
   const float4* sb4 = reinterpret_cast<const float4*>(sb);
   float4* out4 = reinterpret_cast<float4*>(out);
-  constexpr uint32_t kQ = G / 4;  // float4 per vector
-  const uint64_t nq = n / 4;
-  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-  uint64_t q = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; q + 3 * stride < nq; q += 4 * stride) {
-    uint32_t c[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) c[u] = code_at(codes, (q + u * stride) / kQ);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint64_t qq = q + u * stride;
-      __stcs(out4 + qq, sb4[c[u] * kQ + uint32_t(qq % kQ)]);
+  constexpr uint32_t kQV = G / 4;          // float4 per vector
+  constexpr uint32_t kQuads = 256 * kQV;   // quads per warp step
+  constexpr uint32_t kPer = kQuads / 32;   // stores per lane per step
+  const uint32_t lane = threadIdx.x & 31, qv = lane % kQV;
+  const uint64_t nq = n / 4;               // complete quads
+  const uint64_t steps = (nq + kQuads - 1) / kQuads, words = ((n + G - 1) / G + 7) / 8;
+  const uint64_t warps = uint64_t(gridDim.x) * (blockDim.x / 32);
+  uint64_t st = uint64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  auto word = [&](uint64_t step) { return step < steps && step * 32 + lane < words ? __ldg(codes + step * 32 + lane) : 0u; };
+  uint32_t cur = word(st);
+  for (; st < steps; st += warps) {
+    const uint32_t next = word(st + warps);
+    const uint64_t q0 = st * kQuads;
+    if (q0 + kQuads <= nq) {
+#pragma unroll 4
+      for (uint32_t k = 0; k < kPer; ++k) {
+        const uint32_t Q = lane + 32 * k, v = Q / kQV;
+        const uint32_t c = (__shfl_sync(0xffffffffu, cur, v >> 3) >> (4 * (v & 7))) & 15u;
+        __stcs(out4 + q0 + Q, sb4[c * kQV + qv]);
+      }
+    } else {
+      for (uint32_t k = 0; k < kPer; ++k) {
+        const uint32_t Q = lane + 32 * k, v = Q / kQV;
+        const uint32_t c = (__shfl_sync(0xffffffffu, cur, v >> 3) >> (4 * (v & 7))) & 15u;
+        if (q0 + Q < nq) __stcs(out4 + q0 + Q, sb4[c * kQV + qv]);
+      }
     }
+    cur = next;
   }
-  for (; q < nq; q += stride) __stcs(out4 + q, sb4[code_at(codes, q / kQ) * kQ + uint32_t(q % kQ)]);
-  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {  // the values after the last complete quad
     const uint64_t i = nq * 4 + threadIdx.x;
     out[i] = sb[code_at(codes, i / G) * G + uint32_t(i % G)];
   }
 }
 
-// Scalar variant for an output that is not 16-byte aligned (device-pointer callers).
 template <int G>
 __global__ void __launch_bounds__(kThreads) k_decode_scalar(const uint32_t* __restrict__ codes,
                                                             const float* __restrict__ book, float* __restrict__ out,
@@ -1805,7 +1825,10 @@ struct RunDecode {
   static cudaError_t run(const uint32_t* codes, const float* book, float* out, uint64_t n, uint32_t* status,
                          cudaStream_t s) {
     if (aligned16(out)) {
-      k_decode<G><<<grid_for(n / 4 + 1), kThreads, 0, s>>>(codes, book, out, n, status);
+      // 16 blocks of 8 warps per SM (two rounds of residency), measured best
+      const uint64_t steps = (n / 4 + 256 * (G / 4) - 1) / (256 * (G / 4));
+      const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>((steps + 7) / 8, uint64_t(sm_count()) * 16));
+      k_decode<G><<<uint32_t(grid), kThreads, 0, s>>>(codes, book, out, n, status);
     } else {
       k_decode_scalar<G><<<grid_for(n), kThreads, 0, s>>>(codes, book, out, n, status);
     }
