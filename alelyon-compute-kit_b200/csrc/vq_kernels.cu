@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       if (!(ok = tc::mb_wait(&full[s], (k / S) & 1))) break;
       if (!(ok = tc::mb_wait(&done[q], (k / C) & 1))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll 1
+#pragma unroll(G == 8 ? 2 : 1)
       for (int h = 0; h < H; ++h) {
         uint32_t r[K::kN];
         const uint32_t taddr = tmem + ((wq * 32u) << 16) + (q * H + h) * K::kN;
