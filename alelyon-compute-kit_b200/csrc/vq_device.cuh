@@ -1,6 +1,7 @@
 // Device-side building blocks shared by the vq4 kernels: code access, status
 // flags, constant-bank codebook slots and the certified nearest-entry search.
-// Included by vq_kernels.cu only (it defines the constant-bank array).
+// The constant-bank array and CBook exist only where ACK_VQ_CONSTANT_BOOKS is
+// defined (vq_codec.cu), so exactly one unit owns the array.
 #pragma once
 
 #include <cstdint>
@@ -47,10 +48,12 @@ constexpr int kBookSlots = 8;
 constexpr int kSlotBookFloats = 3 * 16 * 32;
 constexpr int kMetaFloats = 32;  // one BookMeta (19 words used), per book
 constexpr int kSlotFloats = kSlotBookFloats + 3 * kMetaFloats;
-__constant__ float4 c_books[kBookSlots][kSlotFloats / 4];
-
 template <int G>
 __host__ __device__ constexpr int book_pos(int e, int j) { return ((e >> 1) * G + j) * 2 + (e & 1); }
+
+#ifdef ACK_VQ_CONSTANT_BOOKS
+__constant__ float4 c_books[kBookSlots][kSlotFloats / 4];
+
 
 // Book B (0..2) of slot SLOT and its BookMeta, which the staging kernel
 // stores after the books (float kSlotBookFloats + B * kMetaFloats).
@@ -74,6 +77,7 @@ struct CBook {
   static __device__ __forceinline__ uint32_t uniq() { return __float_as_uint(metaq(4).y); }
   static __device__ __forceinline__ bool bad() { return __float_as_uint(metaq(4).z) != 0; }
 };
+#endif  // ACK_VQ_CONSTANT_BOOKS
 
 // Facts about a codebook the search needs, computed once per launch by the
 // staging kernel and stored in the slot beside the book:

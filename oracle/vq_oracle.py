@@ -24,10 +24,11 @@ It restates, in plain numpy, the reference's algorithms for the path:
 Pinning: the format, `encode`, `decode` and `fit_codebook` restatements are
 checked against golden vectors produced by the reference's own Python code
 (`tests/golden/gen_golden.py`, run in a container that has the reference).
-The shader restatements (matmul op 2, AdamW op 3, FP32 encode) cannot be
-pinned: no reference test executes the shader and no Vulkan stack exists on
-these machines. They are restated from `vq4.comp` and marked "parity unpinned"
-wherever they are used.
+The shader restatements (matmul op 2, AdamW op 3, FP32 encode op 0, decode
+op 1, the status bits) are checked bit for bit against the reference's own
+`vq4.comp` source compiled for the host CPU (`oracle/vq4_ref.py`,
+`oracle/vq4_shim.h`) on every case the GPU tests use. That build performs
+each FP32 operation once, IEEE-rounded, in the shader's source order.
 """
 from __future__ import annotations
 
@@ -146,7 +147,7 @@ def encode(values: np.ndarray, book: np.ndarray, group: int) -> np.ndarray:
 def nearest_fp32_shader(values: np.ndarray, book: np.ndarray, group: int) -> np.ndarray:
     """The shader's FP32 encode (vq4.comp:118-144): sequential `precise`
     float32 sum of rounded squares, strict `<` so ties keep the lowest index.
-    Parity unpinned (no reference test runs the shader)."""
+    Pinned to the compiled shader (`vq4_ref.encode`)."""
     x = np.asarray(values, dtype=np.float32).reshape(-1)
     vectors = (x.size + group - 1) // group
     padded = np.zeros(vectors * group, dtype=np.float32)
@@ -217,7 +218,8 @@ def fit_codebook(values, group: int = 16, iterations: int = 4, sample_vectors: i
 def matmul_shader(a_codes, a_book, b_codes, b_book, m, n, k, group, flags) -> np.ndarray:
     """vq4.comp op 2 (165-176): C[row,col] = sum over inner in order of
     fl32(a*b), accumulated with a separately rounded FP32 add. Flag bit 0: A
-    is stored K x M; bit 1: B is stored N x K. Parity unpinned."""
+    is stored K x M; bit 1: B is stored N x K. Pinned to the compiled shader
+    (`vq4_ref.matmul`)."""
     a = decode(a_codes, a_book, m * k, group)
     b = decode(b_codes, b_book, k * n, group)
     A = a.reshape(k, m).T if flags & 1 else a.reshape(m, k)
@@ -233,7 +235,8 @@ def matmul_shader(a_codes, a_book, b_codes, b_book, m, n, k, group, flags) -> np
 def adamw_shader(w, m, v, g, coefficients) -> tuple:
     """vq4.comp op 3, `adamw_value` (87-116), in FP32 with every operation
     rounded on its own (`precise`, no fused multiply-add): returns
-    (w', m', v') as float32 arrays. Parity unpinned."""
+    (w', m', v') as float32 arrays. Pinned to the compiled shader
+    (`vq4_ref.adamw`)."""
     f32 = np.float32
     lr, b1, b2, eps, decay, c1, c2 = (f32(c) for c in coefficients)
     one = f32(1.0)

@@ -57,8 +57,9 @@ def test_kernel_manifest_names_the_sources_the_library_was_built_from():
     for name, entry in m["sources"].items():
         path = next(p for p in [pkg / "csrc" / name, ROOT / "include" / name] if p.exists())
         assert entry["source_sha256"] == hashlib.sha256(path.read_bytes()).hexdigest(), name
-    kernels = set(m["sources"]["vq_kernels.cu"]["kernels"])
-    assert {"k_decode", "k_encode", "k_dense_t32", "k_coded_lut", "k_adamw_encode"} <= kernels
+    kernels = set().union(*(set(entry["kernels"]) for entry in m["sources"].values()))
+    assert {"k_decode", "k_encode", "k_encode_tc", "k_dense_t32", "k_dense_pair", "k_coded_lut", "k_adamw_encode",
+            "k_fit_assign", "k_encode_static"} <= kernels
     c = lib().cdll
     need = ctypes.c_size_t()
     assert c.ack_kernel_manifest(None, 0, ctypes.byref(need)) == ack.ACK_OK

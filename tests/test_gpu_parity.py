@@ -8,6 +8,8 @@ import json
 import numpy as np
 import pytest
 
+import shader_cases as sc
+import vq4_ref
 import vq_oracle as o
 import vq_oracle_c as oc
 from alelyon_compute_kit import ack, vq
@@ -95,17 +97,13 @@ def test_encode_bit_exact_at_scale_with_near_ties_counted(backend, group):
     """2^20 values of each cfg-5 distribution against the C oracle (float64,
     the reference's encoder); disagreements with the FP32 shader encoder are
     counted and must all be float64 near ties."""
-    n = 1 << 20
-    gauss = o.block_normalised(o.gaussian(n, 1.0, 10), group)
-    heavy = o.duplicate_heavy(n // group, group)
-    for values in (gauss, heavy):
-        book = vq.fit_codebook(values, group=group, sample_vectors=65536)
+    for name, values, book, head in sc.fp32_encode_cases(group):
         got = backend.encode_large(values, book, group=group)
         want = oc.encode(values, book, group)
-        np.testing.assert_array_equal(got, want)
-        fp32 = o.nearest_fp32_shader(values[:1 << 16], book, group)
-        mism = np.nonzero(fp32 != o.unpack(want, (1 << 16) // group))[0]
-        ties = set(o.near_ties(values[:1 << 16], book, group, rel=1e-4).tolist())
+        np.testing.assert_array_equal(got, want, err_msg=name)
+        fp32 = o.nearest_fp32_shader(values[:head], book, group)
+        mism = np.nonzero(fp32 != o.unpack(want, head // group))[0]
+        ties = set(o.near_ties(values[:head], book, group, rel=1e-4).tolist())
         assert set(mism.tolist()) <= ties, "an FP32-vs-FP64 disagreement that is not a near tie"
 
 
@@ -122,16 +120,16 @@ def test_encode_decode_round_trip_is_idempotent(backend):
 
 @pytest.mark.parametrize("flags", [0, 1, 2, 3])
 def test_packed_pair_matmul_is_the_shader_bit_for_bit(backend, flags):
-    rng = np.random.default_rng(40 + flags)
-    for (m, n, k, group) in ((3, 5, 7, 8), (33, 65, 129, 16), (64, 17, 96, 32), (1, 256, 256, 16)):
-        ab, bb = rand_book(rng, group), rand_book(rng, group)
-        ac = o.pack(rng.integers(0, 16, (m * k + group - 1) // group))
-        bc = o.pack(rng.integers(0, 16, (k * n + group - 1) // group))
+    for (m, n, k, group, ac, ab, bc, bb) in sc.matmul_cases(flags):
         a = VQArray((k, m) if flags & 1 else (m, k), group, ac, ab)
         b = VQArray((n, k) if flags & 2 else (k, n), group, bc, bb)
         y = backend.matmul(a, b, transpose_a=bool(flags & 1), transpose_b=bool(flags & 2))
         want = o.matmul_shader(ac, ab, bc, bb, m, n, k, group, flags)
         np.testing.assert_array_equal(bits(y), bits(want), err_msg=str((m, n, k, group)))
+        if vq4_ref.available():
+            ref, status = vq4_ref.matmul(ac, ab, bc, bb, m, n, k, group, flags)
+            assert status == 0
+            np.testing.assert_array_equal(bits(y), bits(ref), err_msg=str((m, n, k, group)))
 
 
 def test_schema1_bounds_are_the_references(backend):
@@ -142,44 +140,23 @@ def test_schema1_bounds_are_the_references(backend):
 
 
 def test_adamw_op3_is_the_shader_bit_for_bit(backend):
-    rng = np.random.default_rng(77)
-    for (n, group) in ((129, 16), (4096, 8), (50_001, 32)):
-        states = []
-        for scale in (0.02, 0.01, 1e-4, 1e-3):
-            book = rand_book(rng, group, scale)
-            if scale == 1e-4:
-                book = np.abs(book)
-            states.append(VQArray((n,), group, o.pack(rng.integers(0, 16, (n + group - 1) // group)), book))
-        for step in (1, 7):
-            got = backend.adamw(*states, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step)
-            coefs = o.adamw_coefficients(1e-3, 0.9, 0.999, 1e-8, 0.01, step)
-            want = o.adamw_shader(*(s.decode() for s in states), coefs)
-            for g_, w_ in zip(got, want):
-                np.testing.assert_array_equal(bits(g_), bits(w_))
+    for (n, group, codes, books, step) in sc.adamw_cases():
+        states = [VQArray((n,), group, c, b) for c, b in zip(codes, books)]
+        got = backend.adamw(*states, step=step, **sc.ADAMW_HYPER)
+        want = o.adamw_shader(*(s.decode() for s in states), sc.adamw_coefficients(step))
+        for g_, w_ in zip(got, want):
+            np.testing.assert_array_equal(bits(g_), bits(w_))
+        if vq4_ref.available():
+            ref, status = vq4_ref.adamw(codes, books, sc.adamw_coefficients(step), n, group)
+            assert status == 0
+            for g_, r_ in zip(got, ref):
+                np.testing.assert_array_equal(bits(g_), bits(r_))
 
 
 def test_status_bits_refuse_outputs(backend):
-    rng = np.random.default_rng(3)
-    n, group = 64, 8
-    codes = o.pack(rng.integers(0, 16, n // group))
-    negative = -np.abs(rand_book(rng, group))
-    states = np.concatenate([codes] * 4)
-    books = np.concatenate([rand_book(rng, group).reshape(-1), rand_book(rng, group).reshape(-1),
-                            negative.reshape(-1), rand_book(rng, group).reshape(-1)])
-    coefs = o.adamw_coefficients(1e-3, 0.9, 0.999, 1e-8, 0.0, 1)
-    with pytest.raises(ack.AckError, match="status=4"):   # a negative variance (vq4.comp:102)
-        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, books, coefs), n * 12, np.float32)
-    bad = coefs.copy()
-    bad[1] = 1.5                                          # beta1 outside [0, 1)
-    with pytest.raises(ack.AckError, match="status=4"):
-        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, np.abs(books), bad), n * 12, np.float32)
-    bad[1] = np.inf
-    with pytest.raises(ack.AckError, match="status=1"):
-        backend._run((3, n, 1, 1, group, 16, 0, 0), (states, np.abs(books), bad), n * 12, np.float32)
-    nan_book = rand_book(rng, group)
-    nan_book[5, 2] = np.nan
-    with pytest.raises(ack.AckError, match="status=1"):
-        backend._run((1, n, 1, 1, group, 16, 0, 0), (codes, nan_book), n * 4, np.float32)
+    for name, plan, bindings, out_values, status in sc.status_cases():
+        with pytest.raises(ack.AckError, match=f"status={status}"):
+            backend._run(plan, bindings, out_values * 4, np.float32)
 
 
 @pytest.mark.parametrize("group", [8, 16, 32])

@@ -1,6 +1,7 @@
 """The encode entry that allocates nothing (`ack_vq_encode_noalloc`), called
 through the C ABI with device pointers, against the library's regular
-device-pointer encode (`ack_vq_launch`, op 21) on the same inputs.
+device-pointer encode (`ack_vq_launch`, op 21) on the same inputs, and
+against the reference's float64 encoder restated in C (`oracle/`).
 
 It exists for callers that cannot allocate device memory at the point of
 the call (a host whose own allocator owns all device memory, or code where an
@@ -13,6 +14,8 @@ import ctypes
 
 import numpy as np
 import pytest
+
+import vq_oracle_c as oc
 
 pytestmark = pytest.mark.gpu
 
@@ -75,6 +78,44 @@ def test_noalloc_encode_equals_the_regular_entry_on_two_calls_in_a_row(group):
             want, st = cuda.encode(x[b].contiguous(), books[b].contiguous(), group)
             cuda.check(st)
             np.testing.assert_array_equal(codes[b].cpu().numpy(), want.cpu().numpy())
+            # and the reference's float64 encoder, restated in C on the host
+            host = oc.encode(x[b].cpu().numpy(), books[b].cpu().numpy(), group)
+            np.testing.assert_array_equal(codes[b].cpu().numpy().view(np.uint32), host)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_noalloc_encode_flags_nonfinite_values_and_books_like_the_regular_entry(group):
+    """A NaN in a complete vector, an infinity in the partial last vector and
+    a NaN in one tensor's book: per tensor, the codes and the status word
+    equal the regular entry's; a batch call's status is their OR."""
+    from alelyon_compute_kit import ack, cuda
+    lib, fn = _entry()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    batch, count = 4, 37 * group + 5
+    x, books = _inputs(90 + group, batch, count, group, device)
+    x[0, 3 * group + 1] = float("nan")      # a complete vector
+    x[1, count - 2] = float("inf")          # the partial last vector
+    books[2, 7, group - 1] = float("nan")   # a book entry
+    want_all = 0
+    for b in range(batch):
+        rc, codes, status = _run_noalloc(fn, x[b:b + 1].contiguous(), books[b:b + 1].contiguous(), group, stream)
+        assert rc == ack.ACK_OK, lib.last_error()
+        want, st = cuda.encode(x[b].contiguous(), books[b].contiguous(), group)
+        torch.cuda.synchronize()
+        assert int(status.item()) == int(st.item()), b
+        want_all |= int(st.item())
+        np.testing.assert_array_equal(codes[0].cpu().numpy(), want.cpu().numpy())
+    assert want_all == 1
+    rc, codes, status = _run_noalloc(fn, x, books, group, stream)
+    assert rc == ack.ACK_OK, lib.last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == want_all
+    for b in range(batch):
+        want, _ = cuda.encode(x[b].contiguous(), books[b].contiguous(), group)
+        np.testing.assert_array_equal(codes[b].cpu().numpy(), want.cpu().numpy())
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
