@@ -22,7 +22,8 @@ from . import ack
 ENTRIES = 16
 OP_ENCODE1, OP_DECODE1, OP_MATMUL1, OP_ADAMW1 = 0, 1, 2, 3
 (OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT,
- OP_FIT_VALUES) = range(16, 26)
+ OP_FIT_VALUES, OP_RESIDUAL, OP_CLIP) = range(16, 28)
+REDUCE_WORKSPACE_BYTES = (1024 + 1) * 8   # float64 partials of ops 26 and 27, then their total
 
 
 def words_for(count: int, group: int) -> int:
@@ -124,11 +125,42 @@ def repack_tile32(codes, n: int, k: int, group: int, *, out=None, status=None):
     return out, status
 
 
+# The dense product runs on the tensor cores from this many activation rows
+# (canonical layout, W stored n x k, (k / group) % 32 == 0). Each tcgen05.mma
+# there costs about the same whatever its N (2 x the rows of X), so below
+# this the shared-memory lookup-table kernels are faster (cfg2 measured: M=16
+# 4.3 ms LUT against 14.5 ms; M=64 16.9 ms LUT against 15.4 ms).
+DENSE_TC_MIN_ROWS = 64
+DENSE_TC_MAX_ROWS = 128   # rows of X per pass of the tensor-core kernel
+
+
+def dense_tc_workspace_bytes(m: int, k: int, group: int, batch: int) -> int:
+    """Bytes of the tensor-core dense product's workspace: the projections of
+    one pass of at most 128 rows of X on every codebook entry, as bf16 hi and
+    lo halves, (2 * roundup(rows, 8)) x (16 k / group) per expert."""
+    rows = min(m, DENSE_TC_MAX_ROWS)
+    return batch * 2 * ((rows + 7) // 8 * 8) * 16 * (k // group) * 2
+
+
+def dense_engine(m: int, k: int, group: int, *, transpose_b: bool = True, layout: str = "canonical") -> str:
+    """"tensor" when the tensor-core kernel applies and pays, else "lut"."""
+    if (transpose_b and layout == "canonical" and m >= DENSE_TC_MIN_ROWS and k % group == 0
+            and (k // group) % 32 == 0):
+        return "tensor"
+    return "lut"
+
+
 def dense(x, codes, books, n: int, group: int, *, transpose_b: bool = True, layout: str = "canonical", out=None,
-          status=None):
+          status=None, engine: str = "auto", workspace=None):
     """Y[e] = X[e] @ decode(W[e]).T (W[e] stored n x k) for e < E, one launch.
     `x` (E, M, K) float32; `codes` (E, words) int32, canonical or (layout
-    "tile32", from `repack_tile32`); `books` (E, 16, group)."""
+    "tile32", from `repack_tile32`); `books` (E, 16, group).
+
+    `engine`: "tensor" runs the tcgen05 kernel (one-hot codes times the
+    entries' projections, needs the canonical layout, transpose_b and
+    (k / group) % 32 == 0; its workspace, `dense_tc_workspace_bytes`, is
+    allocated here unless given); "lut" the lookup-table kernels; "auto"
+    picks by `dense_engine`."""
     e, m, k = x.shape
     out = torch.empty((e, m, n), dtype=torch.float32, device=x.device) if out is None else out
     status = status_word(x.device) if status is None else status
@@ -139,7 +171,17 @@ def dense(x, codes, books, n: int, group: int, *, transpose_b: bool = True, layo
         flags |= 4
     elif layout != "canonical":
         raise ack.AckError(f"unknown code layout {layout!r}")
-    launch(plan2(OP_DENSE, m, n, k, group, flags=flags, batch=e), [x, codes, books, None, None, out, None, status])
+    if engine == "auto":
+        engine = dense_engine(m, k, group, transpose_b=transpose_b, layout=layout)
+    if engine == "tensor":
+        flags |= 8
+        if workspace is None:
+            workspace = torch.empty(dense_tc_workspace_bytes(m, k, group, e), dtype=torch.uint8, device=x.device)
+    elif engine != "lut":
+        raise ack.AckError(f"unknown dense engine {engine!r}")
+    else:
+        workspace = None
+    launch(plan2(OP_DENSE, m, n, k, group, flags=flags, batch=e), [x, codes, books, None, workspace, out, None, status])
     return out, status
 
 
@@ -235,3 +277,40 @@ def fit_codebook(x, group: int, *, iterations: int = 4, sample_vectors: int = 40
                  aux1=iterations, aux2=count >> 32),
            [x, init, index, None, workspace, out, None, status])
     return out, status
+
+
+def _f32_bits(value: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", value))[0]
+
+
+def residual(prediction, target_codes, target_book, group: int, scale: float, *, out=None, sumsq=None,
+             workspace=None, status=None):
+    """The harness residual on the device: r = prediction - decode(target)
+    (FP32, elementwise), returned scaled by fl32(scale), and the float64 sum
+    of r^2 in `sumsq` (one value): the MSE loss is sumsq / count."""
+    count = prediction.numel()
+    dev = prediction.device
+    out = torch.empty_like(prediction) if out is None else out
+    sumsq = torch.empty(1, dtype=torch.float64, device=dev) if sumsq is None else sumsq
+    workspace = torch.empty(REDUCE_WORKSPACE_BYTES // 8, dtype=torch.float64, device=dev) if workspace is None \
+        else workspace
+    status = status_word(dev) if status is None else status
+    launch(plan2(OP_RESIDUAL, count, 1, 1, group, aux0=_f32_bits(scale)),
+           [prediction, target_codes, target_book, None, workspace, out, sumsq, status])
+    return out, sumsq, status
+
+
+def clip_norm(gradient, max_norm: float, *, out=None, stats=None, workspace=None, status=None):
+    """The harness's global-norm clip on the device: norm = ||g||_2 in
+    float64, scale = min(1, max_norm / (norm + 1e-6)), out = g * fl32(scale);
+    `stats` (two float64) receives [norm, scale]."""
+    count = gradient.numel()
+    dev = gradient.device
+    out = torch.empty_like(gradient) if out is None else out
+    stats = torch.empty(2, dtype=torch.float64, device=dev) if stats is None else stats
+    workspace = torch.empty(REDUCE_WORKSPACE_BYTES // 8, dtype=torch.float64, device=dev) if workspace is None \
+        else workspace
+    status = status_word(dev) if status is None else status
+    lo, hi = struct.unpack("<II", struct.pack("<d", float(max_norm)))
+    launch(plan2(OP_CLIP, count, 1, 1, 8, aux0=lo, aux1=hi), [gradient, None, None, None, workspace, out, stats, status])
+    return out, stats, status

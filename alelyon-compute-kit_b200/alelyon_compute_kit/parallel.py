@@ -60,31 +60,50 @@ def expert_range(experts: int, rank: int, world: int) -> tuple[int, int]:
     return min(experts, rank * per), min(experts, (rank + 1) * per)
 
 
-def gather_columns(y_local, n_total: int, ranges, group=None):
-    """All-gather the column shards Y_r (..., M, n_r) of every rank into the
-    full (..., M, n_total) on every rank (one NCCL all-gather of padded
-    shards; works with gloo on CPU tensors too)."""
-    import torch
+def gather_columns(y_local, n_total: int, ranges, group=None, *, layout: str = "columns", out=None):
+    """All-gather the column shards Y_r (..., M, n_r) of every rank with one
+    NCCL all-gather (gloo on CPU tensors too).
+
+    layout="rank-major": the collective lands in place in a (world, ...,
+    M, width) buffer (`out` when given), each rank's slice padded to the
+    widest range; nothing is copied after the collective.
+    layout="columns": the usual (..., M, n_total), made from the rank-major
+    buffer by one strided copy."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     width = max(b - a for a, b in ranges)
-    lead = y_local.shape[:-1]
-    padded = y_local.new_zeros(lead + (width,))
-    padded[..., : y_local.shape[-1]] = y_local
-    flat = y_local.new_empty(world * padded.numel())
-    dist.all_gather_into_tensor(flat, padded.contiguous().view(-1), group=group)
-    out = flat.view((world,) + lead + (width,))
-    parts = [out[r][..., : b - a] for r, (a, b) in enumerate(ranges)]
-    full = torch.cat(parts, dim=-1)
+    lead = tuple(y_local.shape[:-1])
+    if y_local.shape[-1] == width and y_local.is_contiguous():
+        send = y_local.view(-1)
+    else:
+        padded = y_local.new_zeros(lead + (width,))
+        padded[..., : y_local.shape[-1]] = y_local
+        send = padded.view(-1)
+    if out is None:
+        out = y_local.new_empty((world,) + lead + (width,))
+    dist.all_gather_into_tensor(out.view(-1), send, group=group)
+    if layout == "rank-major":
+        return out
+    if layout != "columns":
+        raise ValueError(f"unknown gather layout {layout!r}")
+    if all(b - a == width for a, b in ranges):
+        # (world, ..., width) -> (..., world, width): one copy, columns in rank order
+        order = tuple(range(1, len(lead) + 1)) + (0, len(lead) + 1)
+        full = out.permute(order).reshape(lead + (world * width,))
+    else:
+        full = y_local.new_empty(lead + (n_total,))
+        for r, (a, b) in enumerate(ranges):
+            full[..., a:b] = out[r][..., : b - a]
     assert full.shape[-1] == n_total
     return full
 
 
-def dense_sharded(x, codes, book, n_total: int, k: int, group: int, *, gather: bool = True, status=None):
+def dense_sharded(x, codes, book, n_total: int, k: int, group: int, *, gather: bool = True, status=None,
+                  layout: str = "columns"):
     """Y = X @ decode(W).T with W (n_total x k) row-sharded over the ranks:
     `codes` is this rank's word slice (from `row_ranges` + `code_slice`),
     `book` the shared codebook, `x` (M, k) replicated. Returns the full Y
-    (gather=True) or this rank's columns."""
+    (gather=True; `layout` as in `gather_columns`) or this rank's columns."""
     import torch.distributed as dist
 
     from . import cuda
@@ -95,7 +114,7 @@ def dense_sharded(x, codes, book, n_total: int, k: int, group: int, *, gather: b
     y = y[0]
     if not gather:
         return y, status
-    return gather_columns(y, n_total, ranges), status
+    return gather_columns(y, n_total, ranges, layout=layout), status
 
 
 def coded_sharded(a_codes, a_book, b_codes, b_book, m: int, n_total: int, k: int, group: int, *,

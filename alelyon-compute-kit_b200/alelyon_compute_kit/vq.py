@@ -36,88 +36,130 @@ from . import ack
 SCHEMA = 1
 GROUPS = (8, 16, 32)
 ENTRIES = 16
-MAX_ELEMENTS = 268_435_456
-MAX_MATMUL_MACS = 268_435_456
-_HEADER = struct.Struct("<8sIIIIQQ")
-_MAGIC = b"ACKVQ4\0\0"
+MAX_ELEMENTS = 1 << 28          # values of one coded tensor (the reference's bound)
+MAX_MATMUL_MACS = 1 << 28       # multiply-adds of one schema-1 product
 
 # schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
 OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT, \
     OP_FIT_VALUES = range(16, 26)
+DENSE_TC_MIN_ROWS = 64   # rows of X from which the dense product runs on the tensor cores
 
+
+# ------------------------------------------------------------ argument checks ----
 
 def _integer(value, name: str, minimum: int, maximum: int) -> int:
+    """An integral value (bools refused) within [minimum, maximum]."""
     if isinstance(value, (bool, np.bool_)):
         raise ValueError(f"{name} must be an integer")
     try:
-        result = operator.index(value)
+        number = operator.index(value)
     except TypeError as exc:
         raise ValueError(f"{name} must be an integer") from exc
-    if not minimum <= result <= maximum:
+    if number < minimum or number > maximum:
         raise ValueError(f"{name} must be in {minimum}..{maximum}")
-    return result
+    return number
 
 
 def _shape(shape) -> tuple[int, ...]:
-    result = tuple(_integer(x, "dimension", 1, MAX_ELEMENTS) for x in shape)
-    if not 1 <= len(result) <= 6 or math.prod(result) > MAX_ELEMENTS:
+    dims = tuple(_integer(d, "dimension", 1, MAX_ELEMENTS) for d in shape)
+    if len(dims) < 1 or len(dims) > 6 or math.prod(dims) > MAX_ELEMENTS:
         raise ValueError("vq shape requires rank 1..6 and a bounded element count")
-    return result
+    return dims
 
 
 def _group(group) -> int:
-    group = _integer(group, "group", 8, 32)
-    if group not in GROUPS:
+    g = _integer(group, "group", 8, 32)
+    if g not in GROUPS:
         raise ValueError("vq group must be 8, 16 or 32")
-    return group
+    return g
 
 
 def _float_array(value, name: str) -> np.ndarray:
-    result = np.asarray(value)
-    if result.dtype != np.dtype("float32") or not np.isfinite(result).all():
+    a = np.asarray(value)
+    if a.dtype != np.float32 or not np.isfinite(a).all():
         raise ValueError(f"{name} must contain finite float32 values")
-    return np.ascontiguousarray(result)
+    return np.ascontiguousarray(a)
 
 
 def _book(value, group: int) -> np.ndarray:
-    result = _float_array(value, "codebook")
-    if result.shape != (ENTRIES, group):
+    book = _float_array(value, "codebook")
+    if book.shape != (ENTRIES, group):
         raise ValueError(f"codebook must have shape (16, {group})")
-    return result
+    return book
 
+
+# -------------------------------------------------------------- the format ----
+#
+# A coded tensor of n values in groups of g: V = ceil(n / g) vectors, one
+# 4-bit entry index each; index v is nibble v % 8 (bits 4 (v % 8) ..) of the
+# little-endian u32 word v // 8; the unused high nibbles of the last word are
+# zero. Its wire image is a 40-byte header (<8sIIIIQQ: magic "ACKVQ4\0\0",
+# schema 1, group, rank, reserved 0, n, code bytes), the rank dimensions as
+# u64, the 16 x g FP32 codebook and the code words, all little-endian.
 
 def storage_layout(shape, group: int = 16) -> dict:
     """Byte accounting of one coded tensor, padding and codebook included."""
     shape, group = _shape(shape), _group(group)
-    elements = math.prod(shape)
-    vectors = (elements + group - 1) // group
-    codes = ((vectors + 7) // 8) * 4
-    book = ENTRIES * group * 4
-    metadata = _HEADER.size + 8 * len(shape)
-    total = codes + book + metadata
-    return {"elements": elements, "vectors": vectors, "code_bytes": codes,
-            "codebook_bytes": book, "metadata_bytes": metadata,
-            "serialized_bytes": total, "payload_bytes": codes + book,
-            "bits_per_value": 8 * total / elements,
-            "sub_bit": 8 * total < elements}
+    n = math.prod(shape)
+    vectors = -(-n // group)
+    code_bytes = 4 * -(-vectors // 8)
+    book_bytes = 4 * ENTRIES * group
+    meta = _WireHeader.SIZE + 8 * len(shape)
+    total = code_bytes + book_bytes + meta
+    return {"elements": n, "vectors": vectors, "code_bytes": code_bytes, "codebook_bytes": book_bytes,
+            "metadata_bytes": meta, "serialized_bytes": total, "payload_bytes": code_bytes + book_bytes,
+            "bits_per_value": 8 * total / n, "sub_bit": 8 * total < n}
+
+
+class _WireHeader:
+    """The fixed header of a wire image."""
+
+    LAYOUT = struct.Struct("<8sIIIIQQ")
+    SIZE = LAYOUT.size
+    MAGIC = b"ACKVQ4\0\0"
+
+    @classmethod
+    def pack(cls, shape: tuple, group: int, layout: dict) -> bytes:
+        head = cls.LAYOUT.pack(cls.MAGIC, SCHEMA, group, len(shape), 0, layout["elements"], layout["code_bytes"])
+        return head + struct.pack(f"<{len(shape)}Q", *shape)
+
+    @classmethod
+    def unpack(cls, view: memoryview) -> tuple[tuple, int, dict, int]:
+        """(shape, group, layout, offset of the codebook) of a whole image."""
+        magic, schema, group, rank, reserved, n, code_bytes = cls.LAYOUT.unpack_from(view)
+        if magic != cls.MAGIC or schema != SCHEMA or reserved or rank < 1 or rank > 6:
+            raise ValueError("unsupported vq artifact header")
+        start = cls.SIZE + 8 * rank
+        if view.nbytes < start:
+            raise ValueError("truncated vq dimensions")
+        shape = struct.unpack_from(f"<{rank}Q", view, cls.SIZE)
+        layout = storage_layout(shape, group)
+        if n != layout["elements"] or code_bytes != layout["code_bytes"]:
+            raise ValueError("vq header disagrees with its dimensions")
+        if view.nbytes != layout["serialized_bytes"]:
+            raise ValueError("vq artifact length mismatch")
+        return shape, group, layout, start
+
+
+def _pack(indices: np.ndarray) -> np.ndarray:
+    """Entry indices -> u32 code words (eight nibbles per word, vector v in
+    nibble v % 8 of word v // 8; the last word zero-padded)."""
+    idx = np.zeros(-(-indices.size // 8) * 8, dtype=np.uint32)
+    idx[:indices.size] = indices
+    shifts = np.arange(0, 32, 4, dtype=np.uint32)
+    return np.bitwise_or.reduce(idx.reshape(-1, 8) << shifts, axis=1).astype(np.uint32)
 
 
 def _indices(codes: np.ndarray, vectors: int) -> np.ndarray:
-    pos = np.arange(vectors, dtype=np.int64)
-    return (codes[pos // 8] >> ((pos % 8) * 4).astype(np.uint32)) & np.uint32(15)
-
-
-def _pack(chosen: np.ndarray) -> np.ndarray:
-    words = np.zeros((chosen.size + 7) // 8, dtype=np.uint32)
-    for lane in range(8):
-        part = chosen[lane::8]
-        words[:part.size] |= part.astype(np.uint32) << np.uint32(4 * lane)
-    return words
+    """The first `vectors` entry indices of a code-word image."""
+    shifts = np.arange(0, 32, 4, dtype=np.uint32)
+    return ((np.asarray(codes, np.uint32)[:, None] >> shifts) & np.uint32(15)).reshape(-1)[:vectors]
 
 
 @dataclass(frozen=True, init=False)
 class VQArray:
-    """Owned CPU wire image: shape, group, packed codes, codebook."""
+    """An owned, read-only coded tensor on the host: shape, group, the code
+    words and the codebook (the reference's `VQArray`)."""
 
     shape: tuple[int, ...]
     group: int
@@ -127,59 +169,45 @@ class VQArray:
     def __init__(self, shape, group, codes, codebook):
         shape, group = _shape(shape), _group(group)
         layout = storage_layout(shape, group)
-        raw = np.asarray(codes)
-        if raw.dtype != np.dtype("uint32") or raw.shape != (layout["code_bytes"] // 4,):
+        words = np.asarray(codes)
+        if words.dtype != np.uint32 or words.shape != (layout["code_bytes"] // 4,):
             raise ValueError("vq codes must be the exact uint32 word image")
-        book = _book(codebook, group)
-        tail = layout["vectors"] % 8
-        if tail and int(raw[-1]) >> (4 * tail):
+        used = layout["vectors"] % 8
+        if used and int(words[-1]) >> (4 * used):
             raise ValueError("vq unused codeword bits must be zero")
-        owned_codes, owned_book = raw.copy(), book.copy()
-        owned_codes.flags.writeable = False
-        owned_book.flags.writeable = False
-        object.__setattr__(self, "shape", shape)
-        object.__setattr__(self, "group", group)
-        object.__setattr__(self, "codes", owned_codes)
-        object.__setattr__(self, "codebook", owned_book)
+        book = _book(codebook, group)
+        frozen = []
+        for a in (words, book):
+            a = a.copy()
+            a.flags.writeable = False
+            frozen.append(a)
+        for name, value in (("shape", shape), ("group", group), ("codes", frozen[0]), ("codebook", frozen[1])):
+            object.__setattr__(self, name, value)
 
     @property
     def layout(self) -> dict:
         return storage_layout(self.shape, self.group)
 
     def decode(self) -> np.ndarray:
-        layout = self.layout
-        idx = _indices(self.codes, layout["vectors"])
-        return self.codebook[idx].reshape(-1)[:layout["elements"]].copy().reshape(self.shape)
+        lay = self.layout
+        values = self.codebook[_indices(self.codes, lay["vectors"])].reshape(-1)
+        return values[:lay["elements"]].reshape(self.shape).copy()
 
     def to_bytes(self) -> bytes:
-        layout = self.layout
-        header = _HEADER.pack(_MAGIC, SCHEMA, self.group, len(self.shape), 0,
-                              layout["elements"], layout["code_bytes"])
-        dims = struct.pack("<" + "Q" * len(self.shape), *self.shape)
-        return header + dims + self.codebook.astype("<f4").tobytes() + self.codes.astype("<u4").tobytes()
+        return (_WireHeader.pack(self.shape, self.group, self.layout) + self.codebook.astype("<f4").tobytes()
+                + self.codes.astype("<u4").tobytes())
 
     @classmethod
     def from_bytes(cls, data, *, max_bytes: int = 128 * 1024 * 1024) -> "VQArray":
-        limit = _integer(max_bytes, "max_bytes", _HEADER.size, 1 << 32)
+        limit = _integer(max_bytes, "max_bytes", _WireHeader.SIZE, 1 << 32)
         view = memoryview(data).cast("B")
-        if not _HEADER.size <= view.nbytes <= limit:
+        if view.nbytes < _WireHeader.SIZE or view.nbytes > limit:
             raise ValueError("vq artifact byte limit or truncated header")
-        magic, schema, group, rank, reserved, elements, code_bytes = _HEADER.unpack_from(view)
-        if magic != _MAGIC or schema != SCHEMA or reserved or not 1 <= rank <= 6:
-            raise ValueError("unsupported vq artifact header")
-        dims_end = _HEADER.size + rank * 8
-        if view.nbytes < dims_end:
-            raise ValueError("truncated vq dimensions")
-        shape = struct.unpack_from("<" + "Q" * rank, view, _HEADER.size)
-        layout = storage_layout(shape, group)
-        if elements != layout["elements"] or code_bytes != layout["code_bytes"]:
-            raise ValueError("vq header disagrees with its dimensions")
-        if view.nbytes != layout["serialized_bytes"]:
-            raise ValueError("vq artifact length mismatch")
-        book_end = dims_end + layout["codebook_bytes"]
-        book = np.frombuffer(view[dims_end:book_end], dtype="<f4").reshape(ENTRIES, group)
-        codes = np.frombuffer(view[book_end:], dtype="<u4")
-        return cls(shape, group, codes.astype(np.uint32), book.astype(np.float32))
+        shape, group, layout, at = _WireHeader.unpack(view)
+        book_end = at + layout["codebook_bytes"]
+        book = np.frombuffer(view[at:book_end], dtype="<f4").astype(np.float32).reshape(ENTRIES, group)
+        codes = np.frombuffer(view[book_end:], dtype="<u4").astype(np.uint32)
+        return cls(shape, group, codes, book)
 
 
 def _nearest(vectors: np.ndarray, book: np.ndarray, valid_last: int | None = None) -> np.ndarray:
@@ -295,7 +323,6 @@ class ResidentStack:
             raise ValueError("the tile32 layout needs (K / group) % 32 == 0 for a stored N x K matrix")
         self.backend, self.shape, self.group, self.layout = backend, stack.shape, stack.group, layout
         self.count = len(stack)
-        self._io: dict = {}
         device = backend.device
         self._buffers = []
         with device._lock:
@@ -336,7 +363,15 @@ class ResidentStack:
         if flags:
             raise ack.AckError(f"vq device arithmetic refused: status={flags}")
 
-    def matmul(self, xs, *, transpose_b: bool = True, out: np.ndarray | None = None) -> np.ndarray:
+    def matmul(self, xs, *, transpose_b: bool = True, out: np.ndarray | None = None,
+               parts: int = 0) -> np.ndarray:
+        """Y = X . op(decode W) for every resident matrix, X and Y in host
+        memory. One pipelined library call (`ack_vq2_dense_host`): the
+        experts run in `parts` ranges (0: the library's choice) whose copies
+        in, products and copies out overlap; page-locked `xs` and `out`
+        (e.g. from a pinned allocator) let the copies run asynchronously.
+        With 64 or more rows of X on canonical codes the product runs on the
+        tensor cores."""
         if self.layout == "tile32" and not transpose_b:
             raise ValueError("the tile32 layout holds W stored N x K (transpose_b=True)")
         backend, device = self.backend, self.backend.device
@@ -348,33 +383,34 @@ class ResidentStack:
         if k != k2:
             raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
         flags = (2 if transpose_b else 0) | (4 if self.layout == "tile32" else 0)
-        plan = backend._plan2(OP_DENSE, m, n, k, self.group, flags=flags, batch=e)
+        if (self.layout == "canonical" and transpose_b and m >= DENSE_TC_MIN_ROWS and k % self.group == 0
+                and (k // self.group) % 32 == 0):
+            flags |= 8
+        y = np.empty((e, m, n), dtype=np.float32) if out is None else out
+        if y.dtype != np.float32 or y.shape != (e, m, n) or not y.flags.c_contiguous:
+            raise ValueError("out must be a C-contiguous (count, M, N) float32 array")
+        plan = struct.pack("<16I", *backend._plan2(OP_DENSE, m, n, k, self.group, flags=flags, batch=e))
+        status = ctypes.c_uint32(0)
         with device._lock:
             device._require_open()
             if not self.codes._handle:
                 raise ack.AckError("resident stack has been freed")
-            io = self._io.get((m, k, n))
-            if io is None:
-                xb, yb = device.buffer(x.nbytes), device.buffer(e * m * n * 4)
-                status = device.buffer(4)
-                self._buffers += [xb, yb, status]
-                io = self._io[(m, k, n)] = (xb, yb, status)
-            xb, yb, status = io
-            xb.upload(x)
-            status.upload(np.zeros(1, dtype=np.uint32))
-            backend._launch2(plan, [xb, self.codes, self.books, None, None, yb, None, status])
-            self._check(status)
-            if out is not None:
-                yb.download(np.float32, out.reshape(-1))
-                return out
-            y = yb.download(np.float32)
-        return y.reshape(e, m, n)
+            fn = device._lib.cdll.ack_vq2_dense_host
+            fn.restype = ctypes.c_int32
+            fn.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32)]
+            rc = fn(device._handle, plan, len(plan), self.codes._handle, self.books._handle, x.ctypes.data,
+                    y.ctypes.data, int(parts), ctypes.byref(status))
+            if rc != ack.ACK_OK:
+                raise ack._kit_error("vq2", rc, device._lib.last_error())
+        if status.value:
+            raise ack.AckError(f"vq device arithmetic refused: status={status.value}")
+        return y
 
     def free(self) -> None:
         for b in self._buffers:
             b.free()
         self._buffers = []
-        self._io = {}
 
     def __enter__(self) -> "ResidentStack":
         return self
@@ -448,31 +484,39 @@ class VQDevice:
 
     # -- transport ------------------------------------------------------------------
 
+    @staticmethod
+    def _refuse_status(status) -> None:
+        """Raise if the kernel set a status bit (vq4.comp:5-8): the output
+        must not be used."""
+        flags = int(status.download(np.uint32)[0])
+        if flags:
+            raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+
     def _run(self, words, inputs, output_bytes: int, dtype):
-        device = self.device
-        with device._lock, ExitStack() as cleanup:
-            device._require_open()
-            buffers = []
-            for array in inputs:
-                b = device.buffer(array.nbytes)
-                cleanup.callback(b.free)
-                b.upload(array)
-                buffers.append(b)
-            out = device.buffer(output_bytes)
-            cleanup.callback(out.free)
-            status = device.buffer(4)
-            cleanup.callback(status.free)
-            status.upload(np.zeros(1, dtype=np.uint32))
-            while len(buffers) < 4:
-                buffers.append(buffers[0])  # unread slots still hold a live input
+        """One schema-1 `ack_vq` call on fresh device buffers: the inputs
+        staged (an unread input slot names the first input again: the ABI
+        wants every slot live), the output and a cleared status word
+        allocated, the status checked, the output downloaded."""
+        dev = self.device
+        with dev._lock, ExitStack() as owned:
+            dev._require_open()
+
+            def fresh(nbytes: int, content=None):
+                b = dev.buffer(nbytes)
+                owned.callback(b.free)
+                if content is not None:
+                    b.upload(content)
+                return b
+
+            slots = [fresh(a.nbytes, a) for a in inputs]
+            slots += [slots[0]] * (4 - len(slots))
+            out = fresh(output_bytes)
+            status = fresh(4, np.zeros(1, dtype=np.uint32))
             plan = struct.pack("<8I", *words)
-            rc = self._call(device._handle, *(b._handle for b in buffers), out._handle, status._handle,
-                            plan, len(plan))
+            rc = self._call(dev._handle, *(b._handle for b in slots), out._handle, status._handle, plan, len(plan))
             if rc != ack.ACK_OK:
-                raise ack._kit_error("vq", rc, device._lib.last_error())
-            flags = int(status.download(np.uint32)[0])
-            if flags:
-                raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+                raise ack._kit_error("vq", rc, dev._lib.last_error())
+            self._refuse_status(status)
             return out.download(dtype)
 
     def _launch2(self, plan_words, slots) -> None:
@@ -514,58 +558,64 @@ class VQDevice:
             status.upload(np.zeros(1, dtype=np.uint32))
             slots[7] = status
             self._launch2(plan_words, slots)
-            flags = int(status.download(np.uint32)[0])
-            if flags:
-                raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            self._refuse_status(status)
             return tuple(b.download(dtype) for b, (_, dtype) in zip(outs, outputs))
 
     # -- the reference's operations (schema 1) ----------------------------------
+    #
+    # Each is one `ack_vq` call with the reference's 8-word plan [op, m, n, k,
+    # group, 16, flags, 0] and bounds (2^28 values, 2^28 multiply-adds).
+
+    def _op1(self, op: int, m: int, n: int, k: int, group: int, flags: int, inputs, out_bytes: int, dtype):
+        return self._run((op, m, n, k, group, ENTRIES, flags, 0), inputs, out_bytes, dtype)
 
     def encode(self, values, codebook, *, group: int = 16) -> VQArray:
         group = _group(group)
         x = _float_array(values, "values")
-        layout = storage_layout(x.shape, group)
         book = _book(codebook, group)
-        result = self._run((0, x.size, 1, 1, group, ENTRIES, 0, 0),
-                           (x, book), layout["code_bytes"], np.uint32)
-        return VQArray(x.shape, group, result, book)
+        words = self._op1(0, x.size, 1, 1, group, 0, (x, book), storage_layout(x.shape, group)["code_bytes"],
+                          np.uint32)
+        return VQArray(x.shape, group, words, book)
 
     def decode(self, value: VQArray) -> np.ndarray:
-        layout = value.layout
-        return self._run((1, layout["elements"], 1, 1, value.group, ENTRIES, 0, 0),
-                         (value.codes, value.codebook), layout["elements"] * 4,
-                         np.float32).reshape(value.shape)
+        n = value.layout["elements"]
+        out = self._op1(1, n, 1, 1, value.group, 0, (value.codes, value.codebook), 4 * n, np.float32)
+        return out.reshape(value.shape)
 
-    def matmul(self, a: VQArray, b: VQArray, *, transpose_a=False, transpose_b=False) -> np.ndarray:
+    @staticmethod
+    def _product_geometry(a: VQArray, b: VQArray, transpose_a, transpose_b) -> tuple[int, int, int, int]:
+        """(m, n, k, flags) of op(a) @ op(b), refused as the reference refuses."""
         if type(transpose_a) is not bool or type(transpose_b) is not bool:
             raise ValueError("transpose flags must be boolean")
         if len(a.shape) != 2 or len(b.shape) != 2 or a.group != b.group:
             raise ValueError("vq matmul requires two matrices using the same vector group")
-        m, k = a.shape[::-1] if transpose_a else a.shape
-        k2, n = b.shape[::-1] if transpose_b else b.shape
-        if k != k2 or max(m, n, k) > 65536 or m * n > MAX_ELEMENTS:
+        (m, k) = (a.shape[1], a.shape[0]) if transpose_a else a.shape
+        (k_b, n) = (b.shape[1], b.shape[0]) if transpose_b else b.shape
+        return m, n, k if k == k_b else -1, int(transpose_a) | (int(transpose_b) << 1)
+
+    def matmul(self, a: VQArray, b: VQArray, *, transpose_a=False, transpose_b=False) -> np.ndarray:
+        m, n, k, flags = self._product_geometry(a, b, transpose_a, transpose_b)
+        if k < 0 or max(m, n, k) > 65536 or m * n > MAX_ELEMENTS:
             raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
         if m * n * k > MAX_MATMUL_MACS:
             raise ValueError("vq-matmul-work-limit: split the product into bounded calls")
-        flags = int(transpose_a) | (int(transpose_b) << 1)
-        return self._run((2, m, n, k, a.group, ENTRIES, flags, 0),
-                         (a.codes, a.codebook, b.codes, b.codebook), m * n * 4,
-                         np.float32).reshape(m, n)
+        out = self._op1(2, m, n, k, a.group, flags, (a.codes, a.codebook, b.codes, b.codebook), 4 * m * n,
+                        np.float32)
+        return out.reshape(m, n)
 
     def adamw(self, weight: VQArray, momentum: VQArray, variance: VQArray,
               gradient: VQArray, *, lr: float, beta1: float, beta2: float,
               eps: float, weight_decay: float, step: int) -> tuple[np.ndarray, ...]:
-        """Native update from four coded states into FP32 scratch (vq4.comp op 3)."""
+        """vq4.comp op 3: W', M', V' as FP32 arrays from the four coded states."""
         states = (weight, momentum, variance, gradient)
         coefficients = _adamw_coefficients(states, lr, beta1, beta2, eps, weight_decay, step)
-        count = weight.layout["elements"]
-        if count * 3 > MAX_ELEMENTS:
+        n = weight.layout["elements"]
+        if 3 * n > MAX_ELEMENTS:
             raise ValueError("vq AdamW active scratch exceeds element bound")
-        codes = np.concatenate([s.codes for s in states])
-        books = np.concatenate([s.codebook.reshape(-1) for s in states])
-        result = self._run((3, count, 1, 1, weight.group, ENTRIES, 0, 0),
-                           (codes, books, coefficients), count * 3 * 4, np.float32)
-        return tuple(x.reshape(weight.shape) for x in np.split(result, 3))
+        inputs = (np.concatenate([s.codes for s in states]),
+                  np.concatenate([s.codebook.reshape(-1) for s in states]), coefficients)
+        out = self._op1(3, n, 1, 1, weight.group, 0, inputs, 12 * n, np.float32)
+        return tuple(part.reshape(weight.shape) for part in out.reshape(3, n))
 
     # -- B200 extension operations (schema 2) ----------------------------------
 
@@ -690,15 +740,9 @@ class VQDevice:
         With `a` stored (M, K) and `b` stored (N, K) (`transpose_b=True`) and
         K a multiple of the group, each group's dot product is a lookup in the
         16x16 table of codebook inner products."""
-        if type(transpose_a) is not bool or type(transpose_b) is not bool:
-            raise ValueError("transpose flags must be boolean")
-        if len(a.shape) != 2 or len(b.shape) != 2 or a.group != b.group:
-            raise ValueError("vq matmul requires two matrices using the same vector group")
-        m, k = a.shape[::-1] if transpose_a else a.shape
-        k2, n = b.shape[::-1] if transpose_b else b.shape
-        if k != k2:
+        m, n, k, flags = self._product_geometry(a, b, transpose_a, transpose_b)
+        if k < 0:
             raise ValueError("vq matmul dimensions are incompatible or exceed bounds")
-        flags = int(transpose_a) | (int(transpose_b) << 1)
         plan = self._plan2(OP_CODED, m, n, k, a.group, flags=flags)
         (y,) = self._run2(plan, (a.codes, a.codebook, b.codes, b.codebook), [(m * n * 4, np.float32)])
         return y.reshape(m, n)

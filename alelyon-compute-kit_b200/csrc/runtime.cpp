@@ -16,6 +16,7 @@
 //   * the last error message is per thread (ffi.rs:1368).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -65,6 +66,9 @@ struct Device {
   cudaDeviceProp prop{};
   int inject_sync = 0;       // test-only: error reported by the next synchronisation
   bool inject_alloc = false; // test-only: the next allocation reports failure
+  // the copy streams and events of ack_vq2_dense_host, created on first use
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev[7] = {};    // allocated, h_done[2], k_done[2], d_done[2]
 };
 
 struct Registry {
@@ -348,10 +352,15 @@ ACK_EXPORT int32_t ack_close(AckDevice* handle) {
     if (!dev->poisoned) {
       DeviceScope scope(dev->ordinal);
       cudaError_t e = sync_stream(*dev);
-      if (e != cudaSuccess)
+      if (e != cudaSuccess) {
         set_error(format("close waited for enqueued work and it failed: %s", cudaGetErrorString(e)));
-      else
+      } else {
         cudaStreamDestroy(dev->stream);
+        for (cudaStream_t st : {dev->copy_in, dev->copy_out})
+          if (st) cudaStreamDestroy(st);
+        for (cudaEvent_t ev : dev->ev)
+          if (ev) cudaEventDestroy(ev);
+      }
     }
     dev->closed = true;
   }
@@ -695,6 +704,135 @@ ACK_EXPORT int32_t ack_vq2(const AckDevice* dev, const AckBuffer* const* slots, 
   return run_handles("vq2", dev, slots, p);
 }
 
+// ---------------------------------------------- pipelined host-memory product --
+
+namespace {
+
+// Create the device's copy streams and events on first use.
+cudaError_t pipeline_streams(Device& d) {
+  cudaError_t e = cudaSuccess;
+  if (!d.copy_in) e = cudaStreamCreateWithFlags(&d.copy_in, cudaStreamNonBlocking);
+  if (e == cudaSuccess && !d.copy_out) e = cudaStreamCreateWithFlags(&d.copy_out, cudaStreamNonBlocking);
+  for (cudaEvent_t& ev : d.ev)
+    if (e == cudaSuccess && !ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  return e;
+}
+
+}  // namespace
+
+ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* plan, size_t plan_len,
+                                      const AckBuffer* codes, const AckBuffer* books, const float* x, float* y,
+                                      uint32_t parts, uint32_t* status_out) {
+  const char* entry = "vq2-dense-host";
+  if (!plan || !x || !y || !status_out) {
+    set_error(format("%s: null plan, host array or status pointer", entry));
+    return ACK_ERR_NULL;
+  }
+  if (plan_len != ACK_VQ2_PLAN_BYTES) {
+    set_error(format("%s: plan has %zu bytes, expected %u", entry, plan_len, ACK_VQ2_PLAN_BYTES));
+    return ACK_ERR_SIZE;
+  }
+  ack::Plan p;
+  ack::PlanError pe = ack::parse_plan(plan, plan_len, &p);
+  if (pe != ack::PlanError::None) return plan_refused(entry, pe, 2, 0);
+  if (p.op != ack::Op::Dense) {
+    set_error(format("%s: the plan is not the dense product (op 16)", entry));
+    return ACK_ERR_UNSUPPORTED_OP;
+  }
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  if (dev->poisoned) {
+    set_error(format("%s: device poisoned by an earlier failed CUDA operation", entry));
+    return ACK_ERR_POISONED;
+  }
+  BufferRec *bc = nullptr, *bb = nullptr;
+  if ((rc = buffer_of(*dev, codes, &bc)) || (rc = buffer_of(*dev, books, &bb))) return rc;
+  // admission of the whole product: the host arrays stand in for in0 and out0
+  // (their sizes are the caller's promise), the workspace for in4
+  const uint64_t kHostX = ~uint64_t(0) - 1, kHostY = ~uint64_t(0) - 2, kWork = ~uint64_t(0) - 3,
+                 kStatus = ~uint64_t(0) - 4;
+  uint64_t caps[ack::kSlots] = {p.required[0], bc->bytes, bb->bytes, 0, p.required[4], p.required[5], 0, 4};
+  uint64_t ids[ack::kSlots] = {kHostX, bc->id, bb->id, 0, p.required[4] ? kWork : 0, kHostY, 0, kStatus};
+  int slot = 0;
+  pe = ack::validate_buffers(p, caps, ids, &slot);
+  if (pe != ack::PlanError::None) return plan_refused(entry, pe, 2, slot);
+  const uint32_t E = p.batch;
+  const uint64_t M = p.m, N = p.n, K = p.k;
+  if (parts == 0) parts = uint32_t(std::min<uint64_t>(8, E));
+  parts = uint32_t(std::min<uint64_t>(parts, E));
+  const uint32_t per = (E + parts - 1) / parts;
+  const uint64_t x_part = uint64_t(per) * M * K * 4, y_part = uint64_t(per) * M * N * 4;
+  const uint64_t w_bytes = bc->bytes / E, book_bytes = bb->bytes / E;
+  const uint64_t ws_part = (p.flags & 8u) ? ack::dense_tc_workspace_bytes(M, K, p.group, per) : 0;
+  DeviceScope scope(dev->ordinal);
+  cudaError_t e = pipeline_streams(*dev);
+  if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
+  cudaStream_t cs = dev->stream, in = dev->copy_in, out = dev->copy_out;
+  cudaEvent_t allocated = dev->ev[0], *h_done = dev->ev + 1, *k_done = dev->ev + 3, *d_done = dev->ev + 5;
+  void *xb[2] = {}, *yb[2] = {}, *wb[2] = {};
+  uint32_t* status = nullptr;
+  auto fail = [&](cudaError_t err) {
+    for (void* q : {xb[0], xb[1], yb[0], yb[1], wb[0], wb[1], static_cast<void*>(status)})
+      if (q) cudaFreeAsync(q, cs);
+    return cuda_fail(*dev, err, entry);
+  };
+  for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+    e = cudaMallocAsync(&xb[b], x_part, cs);
+    if (e == cudaSuccess) e = cudaMallocAsync(&yb[b], y_part, cs);
+    if (e == cudaSuccess && ws_part) e = cudaMallocAsync(&wb[b], ws_part, cs);
+  }
+  if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&status), 4, cs);
+  if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, 4, cs);
+  if (e == cudaSuccess) e = cudaEventRecord(allocated, cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(in, allocated, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(out, allocated, 0);
+  if (e != cudaSuccess) return fail(e);
+  const char* xh = reinterpret_cast<const char*>(x);
+  char* yh = reinterpret_cast<char*>(y);
+  for (uint32_t c = 0; c < parts && e == cudaSuccess; ++c) {
+    const uint32_t b = c & 1u, e0 = c * per, ec = std::min<uint32_t>(per, E - std::min<uint32_t>(E, e0));
+    if (!ec) break;
+    // in: part c's X once the product of part c - 2 no longer reads its buffer
+    if (c >= 2) e = cudaStreamWaitEvent(in, k_done[b], 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(xb[b], xh + uint64_t(e0) * M * K * 4, uint64_t(ec) * M * K * 4,
+                                              cudaMemcpyHostToDevice, in);
+    if (e == cudaSuccess) e = cudaEventRecord(h_done[b], in);
+    // compute: once part c's X is in and part c - 2's Y is out of the buffer
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, h_done[b], 0);
+    if (e == cudaSuccess && c >= 2) e = cudaStreamWaitEvent(cs, d_done[b], 0);
+    if (e == cudaSuccess) {
+      ack::Plan q = p;
+      q.batch = ec;
+      void* ptr[ack::kSlots] = {xb[b], static_cast<char*>(bc->ptr) + uint64_t(e0) * w_bytes,
+                                static_cast<char*>(bb->ptr) + uint64_t(e0) * book_bytes, nullptr, wb[b], yb[b],
+                                nullptr, status};
+      e = ack::launch(q, ptr, cs);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(k_done[b], cs);
+    // out: part c's Y once its product is done
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(out, k_done[b], 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(yh + uint64_t(e0) * M * N * 4, yb[b], uint64_t(ec) * M * N * 4,
+                                              cudaMemcpyDeviceToHost, out);
+    if (e == cudaSuccess) e = cudaEventRecord(d_done[b], out);
+  }
+  // the scratch is freed on the compute stream after the last copies out
+  if (e == cudaSuccess) e = cudaEventRecord(d_done[0], out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, d_done[0], 0);
+  uint32_t host_status = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&host_status, status, 4, cudaMemcpyDeviceToHost, cs);
+  if (e != cudaSuccess) return fail(e);
+  for (void* q : {xb[0], xb[1], yb[0], yb[1], wb[0], wb[1], static_cast<void*>(status)})
+    if (q) cudaFreeAsync(q, cs);
+  e = sync_stream(*dev);
+  if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
+  *status_out = host_status;
+  return ACK_OK;
+}
+
 ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops, void* stream) {
   if (!plan || !ops) {
     set_error(!plan ? "vq: null plan" : "vq: null operands");
@@ -733,7 +871,7 @@ ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const Ack
     if (p.required[i] && (ids[i] & 3u)) return plan_refused(entry, ack::PlanError::Misaligned, 2, i);
   const int first_out = p.first_output();
   // the fit's workspace (in4) is written too
-  const int first_written = (p.schema == 2 && (p.op == ack::Op::AdamwFit || p.op == ack::Op::Fit)) ? 4 : first_out;
+  const int first_written = p.writes_in4() ? 4 : first_out;
   for (int o = first_written; o < n; ++o) {
     if (!p.required[o]) continue;
     for (int i = 0; i < n; ++i) {

@@ -386,13 +386,15 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
+    // consumers arrive once per warp (a quad's four warps): per-lane
+    // arrivals on one mbarrier serialise
     for (int s = 0; s < S; ++s) {
       tc::mb_init(&full[s], 1);
-      tc::mb_init(&sfree[s], 128 + 1);  // the owning quad's reads and the MMA's completion
+      tc::mb_init(&sfree[s], 4 + 1);  // the owning quad's reads and the MMA's completion
     }
     for (int b = 0; b < C; ++b) {
       tc::mb_init(&done[b], 1);
-      tc::mb_init(&afree[b], 128);
+      tc::mb_init(&afree[b], 4);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -489,8 +491,9 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     uint32_t qhead = 0, qtail = 0;
     for (uint32_t k = q; k < T && ok; k += C) {
       const uint32_t s = k % S;
-      if (!(ok = tc::mb_wait(&full[s], (k / S) & 1))) break;
-      if (!(ok = tc::mb_wait(&done[q], (k / C) & 1))) break;
+      // warp-uniform outcomes: tcgen05.ld below is .sync.aligned
+      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&full[s], (k / S) & 1)))) break;
+      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&done[q], (k / C) & 1)))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll(G == 8 ? 2 : 1)
       for (int h = 0; h < H; ++h) {
@@ -607,8 +610,11 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
         flag_warp(status, bits);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      tc::mb_arrive(&afree[q]);
-      tc::mb_arrive(&sfree[s]);
+      __syncwarp();
+      if (lane == 0) {
+        tc::mb_arrive(&afree[q]);
+        tc::mb_arrive(&sfree[s]);
+      }
       // refine off the pipeline's critical path, 32 vectors at a time
       while (qtail - qhead >= 32u) {
         tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, 32u, sbk, sq, lane);
@@ -900,21 +906,6 @@ struct RunDecode {
     return cudaGetLastError();
   }
 };
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no
-// link-time dependency on the driver library); null if unavailable.
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
 
 // The tensor map of x as rows of G floats (its complete vectors), boxes of
 // the encode tile's rows, swizzled to the rows' width.

@@ -3,10 +3,13 @@
 // Everything here has internal linkage: each unit gets its own copy.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "vq_device.cuh"
 #include "vq_internal.hpp"
@@ -183,6 +186,21 @@ cudaError_t current_device(int* dev) {
   cudaError_t e = cudaGetDevice(dev);
   if (e == cudaSuccess && (*dev < 0 || *dev >= kMaxDevices)) e = cudaErrorInvalidDevice;
   return e;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on the driver library); null if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
 }  // namespace

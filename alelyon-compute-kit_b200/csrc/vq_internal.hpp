@@ -26,6 +26,13 @@ cudaError_t launch_dense(const Plan& p, void* const* ptr, cudaStream_t s);
 cudaError_t launch_coded(const Plan& p, void* const* ptr, cudaStream_t s);
 cudaError_t launch_repack(const Plan& p, void* const* ptr, cudaStream_t s);
 
+// vq_gemm_tc.cu: the dense product on the tensor cores (op 16, flag 8).
+cudaError_t launch_dense_tc(const Plan& p, void* const* ptr, cudaStream_t s);
+
+// vq_harness.cu: the expert harness's residual and gradient clip (ops 26, 27).
+cudaError_t launch_residual(const Plan& p, void* const* ptr, cudaStream_t s);
+cudaError_t launch_clip(const Plan& p, void* const* ptr, cudaStream_t s);
+
 // vq_fit.cu: fit_codebook on the device (ops 24, 25).
 cudaError_t launch_adamw_fit(const Plan& p, void* const* ptr, cudaStream_t s);
 cudaError_t launch_fit_values(const Plan& p, void* const* ptr, cudaStream_t s);

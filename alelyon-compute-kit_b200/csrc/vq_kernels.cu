@@ -53,7 +53,7 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
     }
   }
   switch (p.op) {
-    case Op::Dense: return launch_dense(p, ptr, s);
+    case Op::Dense: return (p.flags & 8u) ? launch_dense_tc(p, ptr, s) : launch_dense(p, ptr, s);
     case Op::Coded: return launch_coded(p, ptr, s);
     case Op::AdamwSample:
     case Op::AdamwUsage:
@@ -67,6 +67,8 @@ cudaError_t launch(const Plan& p, void* const* ptr, cudaStream_t s) {
     case Op::Fit: return launch_fit_values(p, ptr, s);
     case Op::AdamwFit: return launch_adamw_fit(p, ptr, s);
     case Op::RepackTile32: return launch_repack(p, ptr, s);
+    case Op::Residual: return launch_residual(p, ptr, s);
+    case Op::ClipNorm: return launch_clip(p, ptr, s);
     default:
       return cudaErrorInvalidValue;
   }

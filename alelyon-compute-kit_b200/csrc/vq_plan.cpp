@@ -92,7 +92,7 @@ constexpr uint32_t kMaxSamples = 65536;         // fit_codebook's sample bound (
 PlanError parse_schema2(Plan* p) {
   const auto& w = p->words;
   uint32_t op = w[0], group = w[4], entries = w[5], flags = w[6], reserved = w[7];
-  if (op < 16 || op > 25) return PlanError::Operation;
+  if (op < 16 || op > 27) return PlanError::Operation;
   if (!valid_group(group)) return PlanError::Group;
   if (entries != kEntries) return PlanError::Entries;
   if (reserved != 0 || w[12] || w[13] || w[14] || w[15]) return PlanError::Reserved;
@@ -113,8 +113,12 @@ PlanError parse_schema2(Plan* p) {
       // flag bit 1: W stored N x K (groups along K); clear: W stored K x N.
       // flag bit 2: W is in the tile32 layout (needs bit 1, K % G == 0 and
       // (K / G) % 32 == 0).
-      if (flags & ~6u) return PlanError::Flags;
+      // flag bit 3: the tensor-core kernel, with its workspace in in4 (needs
+      // bit 1, the canonical layout, K % G == 0 and (K / G) % 32 == 0).
+      if (flags & ~14u) return PlanError::Flags;
       if ((flags & 4u) && (!(flags & 2u) || p->k % group || (p->k / group) % 32)) return PlanError::Flags;
+      if ((flags & 8u) && (!(flags & 2u) || (flags & 4u) || p->k % group || (p->k / group) % 32))
+        return PlanError::Flags;
       if (p->aux0 || p->aux1 || p->aux2) return PlanError::Aux;
       if (!p->m || !p->n || !p->k) return PlanError::Geometry;
       if (!E) return PlanError::Batch;
@@ -122,7 +126,8 @@ PlanError parse_schema2(Plan* p) {
       if (p->m * p->k > kMaxOperand2 || p->n * p->k > kMaxOperand2 || p->m * p->n > kMaxOperand2)
         return PlanError::AddressLimit;
       uint64_t wb = (flags & 4u) ? tile32_bytes(p->n, p->k, group) : packed_bytes(p->n * p->k, group);
-      p->required = {E * p->m * p->k * 4, E * wb, E * book, 0, 0, E * p->m * p->n * 4, 0, 4};
+      const uint64_t ws = (flags & 8u) ? dense_tc_workspace_bytes(p->m, p->k, group, E) : 0;
+      p->required = {E * p->m * p->k * 4, E * wb, E * book, 0, ws, E * p->m * p->n * 4, 0, 4};
       break;
     }
     case Op::RepackTile32: {
@@ -222,6 +227,34 @@ PlanError parse_schema2(Plan* p) {
         p->required = {packed, book, 0, 0, 0, dense, 0, 4};
       break;
     }
+    case Op::Residual: {
+      // The harness residual (harness.py:186-193): r = prediction -
+      // decode(target) over count = m values (in0 f32, in1/in2 the target's
+      // codes and book); out0 = r * s with s the FP32 bit pattern in aux0
+      // (2 / count), out1 = the float64 sum of r^2 (one value); in4 holds the
+      // reduction's partials.
+      if (flags) return PlanError::Flags;
+      if (!p->m || p->n != 1 || p->k != 1) return PlanError::Geometry;
+      if (E != 1) return PlanError::Batch;
+      if (p->aux1 || p->aux2) return PlanError::Aux;
+      if (p->m > kMaxOperand2) return PlanError::AddressLimit;
+      p->required = {p->m * 4, packed_bytes(p->m, group), book, 0, kReduceWorkspace, p->m * 4, 8, 4};
+      break;
+    }
+    case Op::ClipNorm: {
+      // The harness clip (harness.py:194-200): norm = sqrt(sum g^2) in
+      // float64 over count = m values of in0, scale = min(1, max_norm /
+      // (norm + 1e-6)) with max_norm the float64 whose bits are aux0 (low)
+      // and aux1 (high); out0 = g * fl32(scale), out1 = [norm, scale]
+      // (float64); in4 holds the reduction's partials.
+      if (flags) return PlanError::Flags;
+      if (!p->m || p->n != 1 || p->k != 1) return PlanError::Geometry;
+      if (E != 1) return PlanError::Batch;
+      if (p->aux2) return PlanError::Aux;
+      if (p->m > kMaxOperand2) return PlanError::AddressLimit;
+      p->required = {p->m * 4, 0, 0, 0, kReduceWorkspace, p->m * 4, 16, 4};
+      break;
+    }
     default:
       return PlanError::Operation;
   }
@@ -277,7 +310,7 @@ PlanError validate_buffers(const Plan& p, const uint64_t* capacities, const uint
     }
   // written: out0, out1, and in4 for the fit (its workspace)
   for (int o = 4; o < 7; ++o) {
-    if (!p.required[o] || (o == 4 && p.op != Op::AdamwFit && p.op != Op::Fit)) continue;
+    if (!p.required[o] || (o == 4 && !p.writes_in4())) continue;
     for (int i = 0; i < n; ++i)
       if (i != o && p.required[i] && ids[i] == ids[o] && i != 7) return PlanError::OutputAlias;
   }

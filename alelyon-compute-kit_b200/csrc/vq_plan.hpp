@@ -22,6 +22,7 @@ enum class Op : uint32_t {
   Encode = 0, Decode = 1, Matmul = 2, AdamW = 3,
   Dense = 16, Coded = 17, AdamwSample = 18, AdamwUsage = 19, AdamwEncode = 20,
   EncodeLarge = 21, DecodeLarge = 22, RepackTile32 = 23, AdamwFit = 24, Fit = 25,
+  Residual = 26, ClipNorm = 27,
 };
 
 // Refusals. The schema-1 names are vq4_ops.rs:66-84; the schema-2 ones are
@@ -50,6 +51,12 @@ struct Plan {
   int nslots() const { return schema == 1 ? 6 : 8; }
   int first_output() const { return schema == 1 ? 4 : 5; }
   int status_slot() const { return schema == 1 ? 5 : 7; }
+  // in4 is a workspace the operation writes: the device fits (ops 24, 25)
+  // and the tensor-core dense product (op 16, flag 8)
+  bool writes_in4() const {
+    return schema == 2 && (op == Op::AdamwFit || op == Op::Fit || op == Op::Residual || op == Op::ClipNorm ||
+                           (op == Op::Dense && (flags & 8u)));
+  }
 };
 
 // Bytes of a packed code image of `values` values: ceil(ceil(values/g)/8) u32 words.
@@ -71,6 +78,23 @@ inline uint64_t tile32_bytes(uint64_t rows, uint64_t cols, uint32_t group) {
 // nearest entries (one byte each, padded to 16), entry counts, whole-tensor
 // usage counts and a flag word.
 inline uint64_t fit_workspace_stride(uint32_t samples) { return (uint64_t(samples) + 15) / 16 * 16 + 160; }
+
+// The tensor-core path of the dense product (op 16, flag 8) handles X rows in
+// chunks of at most kDenseTcMaxRows; each chunk's projections P (bf16 hi and
+// lo, 2 x roundup(rows, 8) rows of 16 K / G values per expert) live in the
+// caller's workspace (slot in4).
+constexpr uint32_t kDenseTcMaxRows = 128;
+constexpr uint32_t dense_tc_padded_rows(uint32_t rows) { return (rows + 7) / 8 * 8; }
+inline uint64_t dense_tc_workspace_bytes(uint64_t m, uint64_t k, uint32_t group, uint64_t batch) {
+  const uint32_t mc = uint32_t(m < kDenseTcMaxRows ? m : kDenseTcMaxRows);
+  return batch * 2 * dense_tc_padded_rows(mc) * 16 * (k / group) * 2;
+}
+
+// The harness reductions (ops 26, 27) sum float64 partials of at most
+// kReducePartials blocks, in a fixed order: their workspace (in4) holds the
+// partials and, after them, the total.
+constexpr uint32_t kReducePartials = 1024;
+constexpr uint64_t kReduceWorkspace = (uint64_t(kReducePartials) + 1) * 8;
 
 // Parse a plan block (32 bytes: schema 1, 64 bytes: schema 2). `slot` receives
 // the offending slot for Capacity.

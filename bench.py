@@ -67,7 +67,8 @@ def profile_traffic(name: str):
 
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled through NVML every
-    50 ms during the timed region. Read-only: no setting is changed."""
+    2 ms during the timed region (a few samples even for a region of a few
+    milliseconds). Read-only: no setting is changed."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
@@ -91,21 +92,25 @@ class ClockSampler:
                 continue
         return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.local)
 
+    def _sample(self, nvml) -> bool:
+        try:
+            sm = nvml.nvmlDeviceGetClockInfo(self.handle, nvml.NVML_CLOCK_SM)
+            mx = nvml.nvmlDeviceGetMaxClockInfo(self.handle, nvml.NVML_CLOCK_SM)
+            reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            self.samples.append((sm, mx, reasons))
+            return True
+        except Exception as exc:  # noqa: BLE001
+            self.error = str(exc)
+            return False
+
     def _run(self, nvml):
-        while not self._stop.is_set():
-            try:
-                sm = nvml.nvmlDeviceGetClockInfo(self.handle, nvml.NVML_CLOCK_SM)
-                mx = nvml.nvmlDeviceGetMaxClockInfo(self.handle, nvml.NVML_CLOCK_SM)
-                reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                self.samples.append((sm, mx, reasons))
-            except Exception as exc:  # noqa: BLE001
-                self.error = str(exc)
-                return
-            self._stop.wait(0.05)
+        while not self._stop.is_set() and self._sample(nvml):
+            self._stop.wait(0.002)
 
     def __enter__(self):
         try:
             nvml, self.handle = self._open()
+            self._sample(nvml)  # one sample as the region starts, then every 2 ms
             self.thread = threading.Thread(target=self._run, args=(nvml,), daemon=True)
             self.thread.start()
         except Exception as exc:  # noqa: BLE001
@@ -149,10 +154,10 @@ def dist_setup(args):
 
 # ------------------------------------------------------------------ workload --
 
-def make_cfg2(torch, cuda, vq, experts: int, m: int, device):
+def make_cfg2(torch, cuda, vq, experts: int, device):
     """E distinct coded 11008 x 4096 g16 matrices in HBM, built on the device:
     each W_e ~ N(0, 0.02^2) with 16-value blocks L2-normalised, encoded with
-    one codebook fitted on the CPU from a sample of W_0; X_e ~ N(0, 1)."""
+    one codebook fitted on the CPU from a sample of W_0."""
     gen = torch.Generator(device=device)
     gen.manual_seed(7)
     w0 = torch.randn(N_ROWS * K_COLS, generator=gen, device=device) * 0.02
@@ -173,9 +178,14 @@ def make_cfg2(torch, cuda, vq, experts: int, m: int, device):
         cuda.encode(w0, tbook, GROUP, out=codes[e], status=status)
     cuda.check(status)
     del w0, blocks
+    return codes, books, book
+
+
+def make_cfg2_x(torch, experts: int, m: int, device):
+    """X_e ~ N(0, 1), (E, M, 4096)."""
+    gen = torch.Generator(device=device)
     gen.manual_seed(8)
-    x = torch.randn((experts, m, K_COLS), generator=gen, device=device)
-    return codes, books, x, book
+    return torch.randn((experts, m, K_COLS), generator=gen, device=device)
 
 
 def bytes_per_expert(m: int) -> int:
@@ -199,6 +209,80 @@ def cpu_dense_sample(codes_np, books_np, x_np, budget_s: float):
     return done * (CODE_BYTES + BOOK_BYTES) / elapsed / 1e9, done, oc.threads(), elapsed
 
 
+def roofline(bound: str, achieved: float, kernel: str, algorithmic, traffic_name: str | None, **extra) -> dict:
+    """The roofline object of one workload against the measured peak of its
+    bound ("hbm": GB/s copy bandwidth; "tensor": cuBLAS bf16 TFLOP/s)."""
+    peaks = measured_peaks()
+    if bound == "hbm":
+        peak, unit = peaks.get("hbm_gbs"), "GB/s"
+        fallback = 6650.0
+    else:
+        peak, unit = peaks.get("bf16_tflops"), "TFLOP/s"
+        fallback = 1590.0
+    out = {"bound": bound, "achieved": round(achieved, 2), "peak": peak or fallback, "unit": unit,
+           "frac": round(achieved / (peak or fallback), 4),
+           "traffic": profile_traffic(traffic_name) if traffic_name else None,
+           "peak_source": "measured" if peak else "fallback", "kernel": kernel,
+           "algorithmic_per_launch": algorithmic}
+    out.update(extra)
+    return out
+
+
+def time_cfg2(args, torch, cuda, codes, books, m, device, world, local, engine="auto", layout="auto"):
+    """Device time of the grouped product for M activation rows over the
+    resident experts (one launch per step; inputs exceed L2)."""
+    experts = codes.shape[0]
+    x = make_cfg2_x(torch, experts, m, device)
+    y = torch.empty((experts, m, N_ROWS), dtype=torch.float32, device=device)
+    status = cuda.status_word(device)
+    engine = engine if engine != "auto" else cuda.dense_engine(m, K_COLS, GROUP)
+    layout = layout if layout != "auto" else ("canonical" if m == 1 or engine == "tensor" else "tile32")
+    if layout != "canonical":
+        engine = "lut"
+    run_codes = codes
+    if layout == "tile32":
+        # resident weights are repacked once into the tile32 layout (outside the timed region)
+        run_codes, _ = cuda.repack_tile32(codes, N_ROWS, K_COLS, GROUP, status=status)
+        cuda.check(status)
+    workspace = (torch.empty(cuda.dense_tc_workspace_bytes(m, K_COLS, GROUP, experts), dtype=torch.uint8,
+                             device=device) if engine == "tensor" else None)
+
+    def step():
+        cuda.dense(x, run_codes, books, N_ROWS, GROUP, layout=layout, out=y, status=status, engine=engine,
+                   workspace=workspace)
+
+    ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local)
+    cuda.check(status)
+    coded = experts * (CODE_BYTES + BOOK_BYTES)
+    kernel = ("k_dense_tc" if engine == "tensor" else
+              "k_dense_t32" if layout == "tile32" else ("k_dense_pair" if m == 1 else "k_dense_lut"))
+    algorithmic = experts * bytes_per_expert(m)
+    flops = 2.0 * experts * m * N_ROWS * K_COLS
+    achieved_hbm = algorithmic / (ms / 1e3) / 1e9
+    if engine == "tensor":
+        # the MMA does 2 x 16 K/G = 2 K multiply-adds per (row, X row) for g16: the bf16 hi and lo halves
+        mma_tflops = 2.0 * experts * (2 * ((min(m, 128) + 7) // 8 * 8)) * N_ROWS * (16 * K_COLS // GROUP)
+        mma_tflops *= (m + 127) // 128 / (ms / 1e3) / 1e12
+        roof = roofline("tensor", mma_tflops, kernel, flops, f"{kernel}_cfg2_m{m}",
+                        hbm_gbs=round(achieved_hbm, 1), dense_equivalent_tflops=round(flops / (ms / 1e3) / 1e12, 2),
+                        note="MMA TFLOP/s of the one-hot bf16 GEMM (hi and lo halves) against the cuBLAS bf16 peak")
+    else:
+        roof = roofline("hbm", achieved_hbm, kernel, algorithmic, f"{kernel}_cfg2_m{m}")
+    del x, y, workspace
+    if run_codes is not codes:
+        del run_codes
+    return {"ms": ms, "value": world * coded / (ms / 1e3) / 1e9, "coded": coded, "engine": engine,
+            "layout": layout, "kernel": kernel, "roofline": roof, "clocks": clocks,
+            "tflops_dense_equivalent": flops / (ms / 1e3) / 1e12}
+
+
+def compact(result: dict) -> dict:
+    """A secondary workload's entry: its metric, value, device time per
+    step, roofline and clock record."""
+    keep = ("metric", "value", "unit", "ms_per_step", "roofline", "clocks", "config")
+    return {k: result[k] for k in keep if k in result}
+
+
 def run_cfg2(args, world, rank, local):
     import torch
 
@@ -207,85 +291,132 @@ def run_cfg2(args, world, rank, local):
     torch.cuda.set_device(device)
     m = args.m
     experts = args.experts
-    codes, books, x, book = make_cfg2(torch, cuda, vq, experts, m, device)
-    y = torch.empty((experts, m, N_ROWS), dtype=torch.float32, device=device)
-    status = cuda.status_word(device)
-    layout = args.layout if args.layout != "auto" else ("canonical" if m == 1 else "tile32")
-    args.layout = layout
-    if layout == "tile32":
-        # resident weights are repacked once into the tile32 layout (outside the timed region)
-        codes_canonical = codes
-        codes, status = cuda.repack_tile32(codes_canonical, N_ROWS, K_COLS, GROUP, status=status)
-        cuda.check(status)
-
-    def step():
-        cuda.dense(x, codes, books, N_ROWS, GROUP, layout=layout, out=y, status=status)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    cuda.check(status)
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    torch.cuda.synchronize()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        torch.cuda.nvtx.range_push("timed")
-        start.record()
-        for _ in range(args.steps):
-            step()
-        stop.record()
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    ms = start.elapsed_time(stop)
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    cuda.check(status)
-    ms_step = ms / args.steps
-    coded = experts * (CODE_BYTES + BOOK_BYTES)
-    value = world * coded / (ms_step / 1e3) / 1e9
-    algorithmic = experts * bytes_per_expert(m)
-    peaks = measured_peaks()
-    peak = peaks.get("hbm_gbs")
-    achieved = algorithmic / (ms_step / 1e3) / 1e9
-    kernel = "k_dense_t32" if layout == "tile32" else ("k_dense_pair" if m == 1 else "k_dense_lut")
-    traffic_name = f"{kernel}_cfg2_m{m}"
-    traffic = profile_traffic(traffic_name)
+    codes, books, book = make_cfg2(torch, cuda, vq, experts, device)
+    rec = time_cfg2(args, torch, cuda, codes, books, m, device, world, local, args.engine, args.layout)
+    ms_step = rec["ms"]
+    args.layout = rec["layout"]
     result = {
         "metric": f"vq4 packed GEMV coded-weight GB/s (cfg2 W 11008x4096 g16, M={m}, grouped)",
-        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded N(0,0.02^2) weights, 16-value blocks L2-normalised; X ~ N(0,1))",
+        "value": round(rec["value"], 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02^2) weights, 16-value blocks L2-normalised; X ~ N(0,1))",
         "config": {"workload": f"cfg2-grouped-gemv-m{m}", "experts_per_gpu": experts, "M": m, "N": N_ROWS,
-                   "K": K_COLS, "group": GROUP, "coded_bytes_per_gpu_step": coded,
+                   "K": K_COLS, "group": GROUP, "coded_bytes_per_gpu_step": rec["coded"],
                    "l2": "inputs larger than L2 (codes of all experts exceed 126 MB per launch)",
-                   "weight_layout": layout,
+                   "weight_layout": rec["layout"], "engine": rec["engine"],
                    "parallelism": f"expert-sharded x{world}, no collective"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": peak if peak else 6650.0, "unit": "GB/s",
-                     "frac": round(achieved / (peak if peak else 6650.0), 4),
-                     "traffic": traffic, "peak_source": "measured" if peak else "fallback",
-                     "kernel": kernel, "algorithmic_bytes_per_launch": algorithmic},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
+        "roofline": rec["roofline"],
+        "gpu_launches": args.steps * (2 if rec["engine"] == "tensor" else 1),
+        "clocks": rec["clocks"],
     }
-    canonical = codes_canonical if layout == "tile32" else codes
+    x = make_cfg2_x(torch, experts, m, device)
     if rank == 0 and not args.no_e2e:
-        result["e2e"] = run_cfg2_e2e(args, torch, vq, canonical, books, x, book, local)
+        result["e2e"] = run_cfg2_e2e(args, torch, vq, codes, books, x, book, local)
     if rank == 0 and not args.no_cpu:
         sample = min(experts, 8)
         gbs, done, threads, elapsed = cpu_dense_sample(
-            canonical[:sample].cpu().numpy().view(np.uint32), books[:sample].cpu().numpy(), x[:sample].cpu().numpy(),
+            codes[:sample].cpu().numpy().view(np.uint32), books[:sample].cpu().numpy(), x[:sample].cpu().numpy(),
             args.cpu_budget)
         result["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                   "sample": f"{done} experts of the workload (decode + dot, float64 sums), "
                                             f"{elapsed:.1f} s"}
+    del x
+    if world == 1 and not args.no_secondary:
+        result["secondary"] = run_secondary(args, torch, cuda, codes, books, device, world, rank, local)
+    if world > 1 and not args.no_secondary:
+        result["sharded"] = run_sharded(args, torch, cuda, codes, books, device, world, rank, local)
     return result
+
+
+def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> dict:
+    """The partitions of the path across ranks (N > 1), beside the weak-scaling
+    headline:
+
+    * cfg2 split by W rows (output columns of Y): every rank holds rows
+      [r0, r1) of each of the same E experts, X is replicated; strong
+      scaling (the whole job is the E full products). Timed without and with
+      the NCCL all-gather of the Y shards, which lands in place in a
+      rank-major (world, E, M, rows) buffer.
+    * cfg4: the VQAdamW step of 8 experts per GPU (64 at 8 GPUs), experts
+      split across ranks, no collective."""
+    import copy
+
+    import torch.distributed as dist
+
+    from alelyon_compute_kit import parallel
+    experts, m = codes.shape[0], 1
+    ranges = parallel.row_ranges(N_ROWS, K_COLS, GROUP, world)
+    r0, r1 = ranges[rank]
+    width = max(b - a for a, b in ranges)
+    row_words = K_COLS // GROUP // 8
+    shard = codes.view(experts, N_ROWS, row_words)[:, r0:r1].contiguous().view(experts, -1)
+    x = make_cfg2_x(torch, experts, m, device)
+    y = torch.zeros((experts, m, r1 - r0), dtype=torch.float32, device=device)
+    send = y if r1 - r0 == width else torch.zeros((experts, m, width), dtype=torch.float32, device=device)
+    gathered = torch.empty((world, experts, m, width), dtype=torch.float32, device=device)
+    status = cuda.status_word(device)
+
+    def compute():
+        cuda.dense(x, shard, books, r1 - r0, GROUP, out=y, status=status)
+
+    def compute_gather():
+        compute()
+        if send is not y:  # a narrower last shard is padded to the common width
+            send[..., : r1 - r0] = y
+        dist.all_gather_into_tensor(gathered.view(-1), send.view(-1))
+
+    ms_c, clocks = _timed(torch, compute, args.steps, args.warmup, world, device, local, label="sharded")
+    ms_g, _ = _timed(torch, compute_gather, args.steps, args.warmup, world, device, local, label="sharded-gather")
+    cuda.check(status)
+    coded_total = experts * (CODE_BYTES + BOOK_BYTES)
+    out = {"cfg2-nsplit": {
+        "metric": "vq4 packed GEMV coded-weight GB/s, W rows split across ranks (cfg2, M=1, strong scaling)",
+        "unit": "GB/s", "experts": experts, "rows_per_rank": width, "scaling": "strong",
+        "ms_per_step_compute": round(ms_c, 4), "value_compute": round(coded_total / (ms_c / 1e3) / 1e9, 2),
+        "ms_per_step_with_allgather": round(ms_g, 4),
+        "value_with_allgather": round(coded_total / (ms_g / 1e3) / 1e9, 2),
+        "allgather_bytes_per_rank": send.numel() * 4, "allgather_share": round(max(0.0, ms_g - ms_c) / ms_g, 4),
+        "gather_layout": "rank-major (world, E, M, rows), in place", "clocks": clocks}}
+    del shard, x, y, send, gathered
+    torch.cuda.empty_cache()
+    sub = copy.copy(args)
+    sub.no_e2e = sub.no_cpu = True
+    bank = run_cfg4(sub, world, rank, local)
+    out["cfg4-bank"] = {"metric": bank["metric"], "value": bank["value"], "unit": bank["unit"],
+                        "experts_total": world * args.experts_cfg4, "ms_per_step": bank["ms_per_step"],
+                        "scaling": "weak", "clocks": bank["clocks"]}
+    return out
+
+
+def run_secondary(args, torch, cuda, codes, books, device, world, rank, local) -> dict:
+    """Every other workload of the configs, measured in the same run: cfg2
+    at M = 4, 16, 64 over the same experts; cfg3; the cfg4 VQAdamW step;
+    decode and encode of 2^30 values for each group and distribution."""
+    import copy
+    sec = {}
+    for m in (4, 16, 64):
+        rec = time_cfg2(args, torch, cuda, codes, books, m, device, world, local)
+        sec[f"cfg2-m{m}"] = {
+            "metric": f"vq4 packed GEMM coded-weight GB/s (cfg2, M={m})", "value": round(rec["value"], 2),
+            "unit": "GB/s", "ms_per_step": round(rec["ms"], 4), "engine": rec["engine"],
+            "weight_layout": rec["layout"], "dense_equivalent_tflops": round(rec["tflops_dense_equivalent"], 2),
+            "roofline": rec["roofline"], "clocks": rec["clocks"]}
+    del codes, books
+    torch.cuda.empty_cache()
+    sub = copy.copy(args)
+    sub.no_e2e = sub.no_cpu = True
+    sec["cfg3"] = compact(run_cfg3(sub, world, rank, local))
+    torch.cuda.empty_cache()
+    sec["cfg4"] = compact(run_cfg4(sub, world, rank, local))
+    torch.cuda.empty_cache()
+    for group in (8, 16, 32):
+        for dist in ("gauss", "heavy"):
+            sub.group, sub.dist = group, dist
+            for which, res in run_codec_both(sub, world, rank, local).items():
+                sec[f"{which}-g{group}-{dist}"] = compact(res)
+            torch.cuda.empty_cache()
+    return sec
 
 
 def run_cfg2_e2e(args, torch, vq, codes, books, x, book, local):
@@ -359,14 +490,11 @@ def _fit_from_device(vq, torch, values, group, sample_vectors=65536):
     return vq.fit_codebook(sample.cpu().numpy().reshape(-1), group=group, sample_vectors=sample_vectors)
 
 
-def run_codec(args, world, rank, local, which):
-    """cfg 5: encode or decode of 2^30 FP32 values (args.dist: gauss or heavy)."""
-    import torch
-
-    from alelyon_compute_kit import cuda, vq
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    group, n = args.group, args.values
+def make_codec_data(torch, vq, args, group, rank, device):
+    """cfg 5 inputs: 2^30 FP32 values (args.dist: block-normalised Gaussian,
+    or duplicate-heavy: 16 exact atoms, atom 0 at 85%), and the codebook
+    fitted on the CPU from a 65,536-vector sample."""
+    n = args.values
     gen = torch.Generator(device=device)
     gen.manual_seed(10 + rank)
     if args.dist == "heavy":
@@ -382,50 +510,71 @@ def run_codec(args, world, rank, local, which):
         blocks = x.view(-1, group)
         blocks /= blocks.norm(dim=1, keepdim=True)
     book = torch.from_numpy(_fit_from_device(vq, torch, x, group)).to(device)
+    return x, book
+
+
+def run_codec_both(args, world, rank, local, which=("encode", "decode")) -> dict:
+    """cfg 5: encode and decode of 2^30 FP32 values, one dataset (args.group,
+    args.dist); returns {which: result line}."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group, n = args.group, args.values
+    x, book = make_codec_data(torch, vq, args, group, rank, device)
     codes, status = cuda.encode(x, book, group)
     cuda.check(status)
-    if which == "encode":
-        fn = lambda: cuda.encode(x, book, group, out=codes, status=status)  # noqa: E731
-    else:
-        fn = lambda: cuda.decode(codes, book, n, group, out=x, status=status)  # noqa: E731
-    ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
-    cuda.check(status)
-    code_bytes = codes.numel() * 4
-    algorithmic = 4 * n + code_bytes + 64 * group
-    peak = measured_peaks().get("hbm_gbs") or 6650.0
-    achieved = algorithmic / (ms / 1e3) / 1e9
-    # x from torch is 16-byte aligned: encode runs the tensor-core kernel
-    kernel = "k_encode_tc" if which == "encode" else "k_decode"
-    result = {
-        "metric": f"vq4 {which} Gvalues/s (cfg5, 2^30 values, g{group}, {args.dist})",
-        "value": round(world * n / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": f"synthetic ({args.dist})",
-        "config": {"workload": f"cfg5-{which}-g{group}-{args.dist}", "values_per_gpu": n, "group": group,
-                   "l2": "inputs larger than L2", "parallelism": f"range-sharded x{world}, no collective"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"{kernel}_cfg5_g{group}"),
-                     "kernel": kernel, "algorithmic_bytes_per_launch": algorithmic},
-        # encode: the book-staging kernel and the encode kernel per step
-        "gpu_launches": args.steps * (2 if which == "encode" else 1), "clocks": clocks,
-    }
-    if rank == 0 and not args.no_cpu:
-        sys.path.insert(0, str(ROOT / "oracle"))
-        import vq_oracle_c as oc
-        m = 1 << 24
-        xs, cb, bk = x[:m].cpu().numpy(), codes[: m // group // 8].cpu().numpy().view(np.uint32), book.cpu().numpy()
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < args.cpu_budget:
-            if which == "encode":
-                oc.encode(xs, bk, group)
-            else:
-                oc.decode(cb, bk, m, group)
-            reps += 1
-        el = time.perf_counter() - t0
-        result["cpu_baseline"] = {"value": round(reps * m / el / 1e9, 4), "unit": "Gvalues/s", "cores": oc.threads(),
-                                  "kind": "port", "sample": f"{reps} x 2^24 values, {el:.1f} s"}
-    return result
+    out = torch.empty_like(x)
+    results = {}
+    for w in which:
+        if w == "encode":
+            fn = lambda: cuda.encode(x, book, group, out=codes, status=status)  # noqa: E731
+        else:
+            fn = lambda: cuda.decode(codes, book, n, group, out=out, status=status)  # noqa: E731
+        ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)
+        cuda.check(status)
+        code_bytes = codes.numel() * 4
+        algorithmic = 4 * n + code_bytes + 64 * group
+        achieved = algorithmic / (ms / 1e3) / 1e9
+        # x from torch is 16-byte aligned: encode runs the tensor-core kernel
+        kernel = "k_encode_tc" if w == "encode" else "k_decode"
+        result = {
+            "metric": f"vq4 {w} Gvalues/s (cfg5, 2^30 values, g{group}, {args.dist})",
+            "value": round(world * n / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": f"synthetic ({args.dist})",
+            "config": {"workload": f"cfg5-{w}-g{group}-{args.dist}", "values_per_gpu": n, "group": group,
+                       "l2": "inputs larger than L2", "parallelism": f"range-sharded x{world}, no collective"},
+            "roofline": roofline("hbm", achieved, kernel, algorithmic, f"{kernel}_cfg5_g{group}_{args.dist}"),
+            # encode: the book-staging kernel and the encode kernel per step
+            "gpu_launches": args.steps * (2 if w == "encode" else 1), "clocks": clocks,
+        }
+        if rank == 0 and not args.no_cpu:
+            sys.path.insert(0, str(ROOT / "oracle"))
+            import vq_oracle_c as oc
+            m = 1 << 24
+            xs, cb, bk = x[:m].cpu().numpy(), codes[: m // group // 8].cpu().numpy().view(np.uint32), book.cpu().numpy()
+            t0 = time.perf_counter()
+            reps = 0
+            while time.perf_counter() - t0 < args.cpu_budget:
+                if w == "encode":
+                    oc.encode(xs, bk, group)
+                else:
+                    oc.decode(cb, bk, m, group)
+                reps += 1
+            el = time.perf_counter() - t0
+            result["cpu_baseline"] = {"value": round(reps * m / el / 1e9, 4), "unit": "Gvalues/s",
+                                      "cores": oc.threads(), "kind": "port",
+                                      "sample": f"{reps} x 2^24 values, {el:.1f} s"}
+        results[w] = result
+    del x, out, codes
+    return results
+
+
+def run_codec(args, world, rank, local, which):
+    """cfg 5: encode or decode of 2^30 FP32 values (args.dist: gauss or heavy)."""
+    return run_codec_both(args, world, rank, local, (which,))[which]
 
 
 def run_cfg3(args, world, rank, local):
@@ -455,7 +604,6 @@ def run_cfg3(args, world, rank, local):
     flops = 2.0 * m * n * k
     lookups = m * n * (k // group)
     byts = xc.numel() * 4 + wc.numel() * 4 + 2 * 64 * group + 4 * m * n
-    peak = measured_peaks().get("hbm_gbs") or 6650.0
     return {
         "metric": "vq4 both-coded GEMM effective TFLOP/s (cfg3, 4096x4096 . (14336x4096)^T, g32)",
         "value": round(world * flops / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -463,9 +611,8 @@ def run_cfg3(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "cfg3-coded-gemm", "M": m, "N": n, "K": k, "group": group,
                    "lut_lookups_per_s": lookups / (ms / 1e3), "parallelism": f"replicated x{world}"},
-        "roofline": {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "k_coded_lut",
-                     "note": "the table lookups on the shared-memory pipe bound this kernel, not HBM"},
+        "roofline": roofline("hbm", byts / (ms / 1e3) / 1e9, "k_coded_lut", byts, "k_coded_lut_cfg3",
+                             note="the table lookups on the shared-memory pipe bound this kernel, not HBM"),
         "gpu_launches": args.steps, "clocks": clocks,
     }
 
@@ -523,7 +670,6 @@ def run_cfg4(args, world, rank, local):
     ms_encode, _ = _timed(torch, encode_pass, args.steps, args.warmup, world, device, local, label="encode-pass")
     cuda.check(status)
     byts = codes.numel() * 4 + out.numel() * 4
-    peak = measured_peaks().get("hbm_gbs") or 6650.0
     result = {
         "metric": "vq4 VQAdamW step Gvalues/s (cfg4, 3 x 4096x1024 g8 per expert: sample, device fit, re-encode)",
         "value": round(world * experts * count / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": world,
@@ -534,10 +680,9 @@ def run_cfg4(args, world, rank, local):
                    "parallelism": f"expert-sharded x{world}, no collective"},
         "encode_pass": {"ms": round(ms_encode, 4),
                         "gvalues_per_s": round(world * experts * count / (ms_encode / 1e3) / 1e9, 3)},
-        "roofline": {"bound": "hbm", "achieved": round(byts / (ms_encode / 1e3) / 1e9, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(byts / (ms_encode / 1e3) / 1e9 / peak, 4), "traffic": None,
-                     "kernel": "k_adamw_encode",
-                     "note": "compute-bound (three certified 16-entry searches per value); coded bytes only"},
+        "roofline": roofline("hbm", byts / (ms_encode / 1e3) / 1e9, "k_adamw_encode", byts,
+                             "k_adamw_encode_cfg4",
+                             note="compute-bound (three certified 16-entry searches per value); coded bytes only"),
         # per step: sample 1, fit 1 + 4 x 3, encode pass 2 per expert (book staging + pass)
         "gpu_launches": args.steps * (1 + 13 + 2 * experts), "clocks": clocks,
     }
@@ -633,9 +778,13 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the other workloads that the default cfg2 run measures beside the headline")
     ap.add_argument("--group", type=int, default=16)
     ap.add_argument("--layout", choices=("auto", "tile32", "canonical"), default="auto",
                     help="auto: canonical for M = 1 (the byte-table kernel), tile32 otherwise")
+    ap.add_argument("--engine", choices=("auto", "lut", "tensor"), default="auto",
+                    help="dense product kernels: tensor cores (M >= 8 by default) or lookup tables")
     ap.add_argument("--values", type=int, default=1 << 30)
     ap.add_argument("--dist", choices=("gauss", "heavy"), default="gauss")
     ap.add_argument("--experts-cfg4", type=int, default=8)

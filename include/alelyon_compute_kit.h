@@ -194,6 +194,8 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
 #define ACK_VQ2_REPACK_TILE32 23u /* canonical N x K images -> the tile32 layout op 16 reads */
 #define ACK_VQ2_ADAMW_FIT 24u    /* fit_codebook of W', M', V' on the device (warm start), bit for bit the CPU fit */
 #define ACK_VQ2_FIT 25u          /* fit_codebook of one tensor on the device, bit for bit the CPU function */
+#define ACK_VQ2_RESIDUAL 26u     /* harness residual: r = P - decode(T), r * s and the float64 sum of r^2 */
+#define ACK_VQ2_CLIP 27u         /* harness clip: float64 norm, g * fl32(min(1, max / (norm + 1e-6))) */
 
 /* Flags of ACK_VQ2_DENSE: bit 1 = W stored N x K (vectors along K); bit 2 =
  * W given in the tile32 layout (requires bit 1 and (K / group) % 32 == 0):
@@ -201,6 +203,11 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
  * row r at byte ((r / 32) * (K / group / 32) + c) * 512 + (r % 32) * 16. */
 #define ACK_VQ2_DENSE_NT 2u
 #define ACK_VQ2_DENSE_TILE32 4u
+/* bit 3: the tensor-core kernel (one-hot codes times the bf16 hi + lo
+ * projections of X on the entries); requires bit 1, the canonical layout
+ * and (K / group) % 32 == 0; in4 is its workspace, written:
+ * batch x 2 x roundup(min(M, 128), 8) x 16 K / group x 2 bytes. */
+#define ACK_VQ2_DENSE_TENSOR 8u
 
 uint32_t ack_vq2_schema(void);
 
@@ -233,9 +240,31 @@ int32_t ack_kernel_manifest(char *out, size_t len, size_t *needed);
  *   25 fit        values (count = m + aux2 << 32), warm book (flags bit 0),
  *                 u32 sample positions then 16 cold-start sample rows,
  *                 in4 = workspace (S x g x 4 + ceil16(S) + 160 bytes,
- *                 written); aux0 = S, aux1 = iterations -> book (16 x g) */
+ *                 written); aux0 = S, aux1 = iterations -> book (16 x g)
+ *   26 residual   prediction (m f32), target codes, target book, in4 =
+ *                 workspace ((1024 + 1) x 8 bytes, written, 8-byte aligned);
+ *                 aux0 = the FP32 bits of s -> r * s (m f32), sum r^2 (f64)
+ *   27 clip       gradient (m f32), in4 = workspace as 26; aux0/aux1 = the
+ *                 low/high words of the float64 max norm -> g * fl32(scale)
+ *                 (m f32), [norm, scale] (2 f64) */
 int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslots,
                 const uint8_t *plan, size_t plan_len);
+
+/* The grouped dense product (op 16) from and to host memory, pipelined: no
+ * counterpart in the reference (its products take and return device
+ * buffers one call at a time). `plan` is an op-16 plan for the whole batch;
+ * `codes` and `books` are device buffers holding the weights (canonical or
+ * tile32, as the flags say), `x` (batch x M x K f32) and `y` (batch x M x N
+ * f32) host memory. The experts run in `parts` contiguous ranges (0: the
+ * library chooses): part c's X is copied in on one stream while part c-1
+ * computes and part c-2's Y is copied out on a third, so the copies and the
+ * products overlap (host memory must be page-locked for the copies to be
+ * asynchronous). Returns when all of `y` is written; `*status_out` (not
+ * null) receives the status word of the whole product, read once. The
+ * device scratch (two parts of X and Y, and the tensor-core workspace when
+ * flag 8 is set) comes from the device's stream-ordered pool. */
+int32_t ack_vq2_dense_host(const AckDevice *dev, const uint8_t *plan, size_t plan_len, const AckBuffer *codes,
+                           const AckBuffer *books, const float *x, float *y, uint32_t parts, uint32_t *status_out);
 
 /* Device-pointer form of both entries, for callers whose data already lives
  * in device memory (a PyTorch tensor, an NCCL buffer): the same plan, the

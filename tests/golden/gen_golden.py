@@ -3,11 +3,13 @@
 Run this in a container where the reference checkout exists (it is not
 present on GPU machines, which only read the committed `.npz` fixtures):
 
-    python tests/golden/gen_golden.py /path/to/reference
+    python tests/golden/gen_golden.py /path/to/reference          # everything
+    python tests/golden/gen_golden.py /path/to/reference bank     # bank.npz only
 
 Every array below is produced by the reference's own CPU code
-(`src/alelyon_compute_kit/_kit/python/vq.py`): `fit_codebook`, `encode`,
-`VQArray.decode`, `VQArray.to_bytes`. Nothing here is restated; the
+(`src/alelyon_compute_kit/_kit/python/vq.py`: `fit_codebook`, `encode`,
+`VQArray.decode`, `VQArray.to_bytes`; `_kit/python/expert_bank.py`:
+`ExpertBank`). Nothing here is restated; the
 restatement under `oracle/` is checked against these files by
 `tests/test_oracle_golden.py`. Inputs are seeded synthetic data.
 """
@@ -36,7 +38,7 @@ def digest(array) -> str:
 def main(root: str) -> None:
     vq = load_reference(root)
 
-    # -- 256x256 N(0, 0.02^2), seed 7, group 16 --------
+    # -- the smoke workload: 256x256 N(0, 0.02^2), seed 7, group 16 --------
     w = (np.random.default_rng(7).standard_normal((256, 256)) * 0.02).astype(np.float32)
     book = vq.fit_codebook(w, group=16)
     image = vq.encode(w, book, group=16)
@@ -153,7 +155,51 @@ def main(root: str) -> None:
     print("golden fixtures written to", HERE)
 
 
+def load_reference_bank(root: str):
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, str(Path(root) / "src"))
+    from alelyon_compute_kit._kit.python import expert_bank  # noqa: E402
+    return expert_bank
+
+
+def bank(root: str) -> None:
+    """bank.npz: every file of a small expert bank written by the reference's
+    own `ExpertBank` (two initialized experts, one of them with a second,
+    updated generation), its `stats()` and each expert's pointer fields; the
+    tests open it with this library's bank and write the same experts anew."""
+    import json
+    import tempfile
+    eb = load_reference_bank(root)
+    vq = load_reference(root)
+    files = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = eb.BankConfig(2, 3, ((16, 8), (8, 24), (16, 8)), 8)
+        b = eb.ExpertBank.create(Path(tmp) / "bank", cfg)
+        b.initialize_expert(0, 1, seed=3, zero_optimizer_state=True)
+        b.initialize_expert(1, 2, seed=5)
+        state = b.read_expert_state(0, 1)
+        w = state.tensors[0]
+        moved = vq.VQArray(w.shape, w.group, w.codes[::-1].copy(), w.codebook * np.float32(0.5))
+        b.write_expert(0, 1, (moved,) + state.tensors[1:], updated_count=7, optimizer_step=2)
+        for path in sorted((Path(tmp) / "bank").iterdir()):
+            files["file:" + path.name] = np.frombuffer(path.read_bytes(), dtype=np.uint8)
+        files["stats"] = np.array(json.dumps(b.stats(), sort_keys=True))
+        # what a fresh bank's initialize_expert writes for the same identities
+        fresh = eb.ExpertBank.create(Path(tmp) / "fresh", cfg)
+        fresh.initialize_expert(0, 1, seed=3, zero_optimizer_state=True)
+        fresh.initialize_expert(1, 2, seed=5)
+        for le in ((0, 1), (1, 2)):
+            for i, t in enumerate(fresh.read_expert(*le)):
+                files[f"init:{le[0]}-{le[1]}-t{i}"] = np.frombuffer(t.to_bytes(), dtype=np.uint8)
+    np.savez_compressed(HERE / "bank.npz", **files)
+    print("bank fixture written to", HERE / "bank.npz")
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: gen_golden.py <reference checkout root>")
-    main(sys.argv[1])
+    if len(sys.argv) == 3 and sys.argv[2] == "bank":
+        bank(sys.argv[1])
+    elif len(sys.argv) == 2:
+        main(sys.argv[1])
+        bank(sys.argv[1])
+    else:
+        raise SystemExit("usage: gen_golden.py <reference checkout root> [bank]")

@@ -134,6 +134,30 @@ def test_vq2_refuses_before_device_lookup_and_reaches_closed_device():
     assert "is not open" in last_error()
 
 
+def test_pipelined_host_product_refuses_before_device_lookup():
+    """ack_vq2_dense_host: null pointers, a wrong plan size, a malformed or
+    non-dense plan refuse before any handle is looked up; a forged device
+    reaches the closed-device refusal."""
+    c = lib().cdll
+    fn = c.ack_vq2_dense_host
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+    x = (ctypes.c_float * 64)()
+    y = (ctypes.c_float * 64)()
+    st = ctypes.c_uint32()
+    args = lambda plan, n: (FORGED, plan, n, FORGED, FORGED, ctypes.addressof(x), ctypes.addressof(y), 0,  # noqa: E731
+                            ctypes.addressof(st))
+    dense = block([16, 1, 8, 8, 8, 16, 2, 0, 1, 0, 0, 0, 0, 0, 0, 0])
+    assert fn(FORGED, None, 64, FORGED, FORGED, ctypes.addressof(x), ctypes.addressof(y), 0,
+              ctypes.addressof(st)) == ack.ACK_ERR_NULL
+    assert fn(FORGED, dense, 64, FORGED, FORGED, None, ctypes.addressof(y), 0, ctypes.addressof(st)) == ack.ACK_ERR_NULL
+    assert fn(*args(dense, 32)) == ack.ACK_ERR_SIZE
+    assert fn(*args(block([16, 1, 8, 8, 12, 16, 2, 0, 1, 0, 0, 0, 0, 0, 0, 0]), 64)) == ack.ACK_ERR_SHAPE
+    assert last_error().endswith("vq2-unsupported-group")
+    assert fn(*args(block([21, 64, 1, 1, 8, 16, 0, 0, 1, 0, 0, 0, 0, 0, 0, 0]), 64)) == ack.ACK_ERR_UNSUPPORTED_OP
+    assert fn(*args(dense, 64)) == ack.ACK_ERR_CLOSED
+
+
 def _cuda_present() -> bool:
     try:
         import torch

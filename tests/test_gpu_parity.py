@@ -371,10 +371,50 @@ def test_harness_on_the_device_equals_the_host_arithmetic(tmp_path, device, fit)
     t = rng.standard_normal((8, 48)).astype(np.float32)
     dev_h = harness.VulkanExpertHarness(roots[0], device=device, fit=fit)
     host_h = harness.VulkanExpertHarness(roots[1], backend=HostShaderBackend())
-    for _ in range(2):
-        a = dev_h.train_step(x, t, expert=1, beta2=0.999)
-        b = host_h.train_step(x, t, expert=1, beta2=0.999)
-        assert a.loss == b.loss and a.gradient_norm_before_clip == b.gradient_norm_before_clip
-    for ta, tb in zip(roots[0].read_expert(0, 1), roots[1].read_expert(0, 1)):
-        assert ta.to_bytes() == tb.to_bytes()
+    # the device engine keeps the step in HBM; its float64 loss and norm are
+    # sums in another order than numpy's (relative 1e-12), the committed
+    # state is the host arithmetic's bit for bit; a clipped and an unclipped step
+    for max_norm in (1e-3, 10.0):
+        a = dev_h.train_step(x, t, expert=1, beta2=0.999, max_grad_norm=max_norm)
+        b = host_h.train_step(x, t, expert=1, beta2=0.999, max_grad_norm=max_norm)
+        assert abs(a.loss - b.loss) <= 1e-12 * abs(b.loss)
+        assert abs(a.gradient_norm_before_clip - b.gradient_norm_before_clip) <= 1e-12 * b.gradient_norm_before_clip
+        assert a.clipped == b.clipped and a.optimizer_step == b.optimizer_step and a.revision == b.revision
+        assert a.input_layout == b.input_layout and a.gradient_layout == b.gradient_layout
+        assert a.persistent_state_bytes == b.persistent_state_bytes
+        for ta, tb in zip(roots[0].read_expert(0, 1), roots[1].read_expert(0, 1)):
+            assert ta.to_bytes() == tb.to_bytes()
     np.testing.assert_array_equal(dev_h.forward(x, expert=1), host_h.forward(x, expert=1))
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_harness_residual_and_clip_ops(group):
+    """Ops 26 and 27 against numpy: the residual and its scaling bit for bit,
+    the float64 sums within 1e-12 relative, the clip's scale and output."""
+    import torch
+
+    from alelyon_compute_kit import cuda
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(60 + group)
+    for count in (1, group + 3, 100_003, 1 << 22):
+        book = rand_book(rng, group)
+        codes = o.pack(rng.integers(0, 16, (count + group - 1) // group))
+        pred = rng.standard_normal(count).astype(np.float32)
+        scale = np.float32(2.0 / count)
+        r, s, st = cuda.residual(torch.from_numpy(pred).to(dev), torch.from_numpy(codes.view(np.int32)).to(dev),
+                                 torch.from_numpy(book).to(dev), group, float(scale))
+        cuda.check(st)
+        want = pred - o.decode(codes, book, count, group)
+        np.testing.assert_array_equal(bits(r.cpu().numpy()), bits(want * scale))
+        ref = float(np.sum(np.square(want, dtype=np.float64)))
+        assert abs(float(s.item()) - ref) <= 1e-12 * ref
+        for max_norm in (1e-3, 1e9):
+            g = torch.from_numpy(want).to(dev)
+            out, stats, st = cuda.clip_norm(g, max_norm)
+            cuda.check(st)
+            norm = float(np.linalg.norm(want.astype(np.float64)))
+            got_norm, got_scale = (float(v) for v in stats.cpu().numpy())
+            assert abs(got_norm - norm) <= 1e-12 * norm
+            sc = min(1.0, max_norm / (got_norm + 1e-6))
+            assert got_scale == sc
+            np.testing.assert_array_equal(bits(out.cpu().numpy()), bits(want * np.float32(sc)))

@@ -109,3 +109,56 @@ def test_gain_scheduler_reserves_exploration():
     assert s.select(2) == (0, 3)
     with pytest.raises(expert_bank.ExpertBankError):
         s.observe(1, float("nan"), 0.0, 1.0, 1, 1)
+
+
+# ---- format compatibility with the reference's own bank (tests/golden/bank.npz) ----
+
+def _reference_bank(tmp_path, golden):
+    data = golden("bank")
+    root = tmp_path / "refbank"
+    root.mkdir()
+    for key in data.files:
+        if key.startswith("file:"):
+            (root / key[5:]).write_bytes(data[key].tobytes())
+    return root, data
+
+
+def test_a_bank_the_reference_wrote_opens_and_reads_here(tmp_path, golden):
+    root, data = _reference_bank(tmp_path, golden)
+    bank = expert_bank.ExpertBank.open(root)
+    assert bank.config == expert_bank.BankConfig(2, 3, ((16, 8), (8, 24), (16, 8)), 8)
+    assert bank.stats() == json.loads(str(data["stats"]))
+    state = bank.read_expert_state(0, 1)
+    assert (state.revision, state.optimizer_step, state.parameter_update_applications) == (2, 2, 7)
+    first = bank.read_expert_state(1, 2)
+    assert (first.revision, first.optimizer_step, first.parameter_update_applications) == (1, 0, 0)
+    for i, t in enumerate(first.tensors):
+        assert t.to_bytes() == data[f"init:1-2-t{i}"].tobytes()
+    # and this library commits a further generation the reference's layout accepts
+    receipt = bank.write_expert(1, 2, first.tensors, updated_count=3, optimizer_step=1)
+    assert receipt["revision"] == 2
+    assert expert_bank.ExpertBank.open(root).read_expert_state(1, 2).parameter_update_applications == 3
+
+
+def test_initialize_expert_writes_the_references_bytes(tmp_path, golden):
+    data = golden("bank")
+    bank = expert_bank.ExpertBank.create(tmp_path / "b", expert_bank.BankConfig(2, 3, ((16, 8), (8, 24), (16, 8)), 8))
+    bank.initialize_expert(0, 1, seed=3, zero_optimizer_state=True)
+    bank.initialize_expert(1, 2, seed=5)
+    for le in ((0, 1), (1, 2)):
+        for i, t in enumerate(bank.read_expert(*le)):
+            assert t.to_bytes() == data[f"init:{le[0]}-{le[1]}-t{i}"].tobytes(), (le, i)
+    ref_bank_json = data["file:bank.json"].tobytes()
+    assert (tmp_path / "b" / "bank.json").read_bytes() == ref_bank_json
+
+
+def test_bank_metadata_must_be_canonical(tmp_path, golden):
+    root, _ = _reference_bank(tmp_path, golden)
+    pointer = root / "expert-1-2.json"
+    text = pointer.read_bytes()
+    pointer.write_bytes(text.replace(b",", b", ", 1))
+    with pytest.raises(expert_bank.ExpertBankError, match="noncanonical"):
+        expert_bank.ExpertBank.open(root).read_expert(1, 2)
+    pointer.write_bytes(text[:-1] + b',"revision":1}')
+    with pytest.raises(expert_bank.ExpertBankError):
+        expert_bank.ExpertBank.open(root).read_expert(1, 2)

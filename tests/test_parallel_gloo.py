@@ -68,6 +68,18 @@ def _worker(rank, world, port, queue):
         y_local = torch.from_numpy(x @ shard.decode().T if shard else np.zeros((m, 0), np.float32))
         full_y = parallel.gather_columns(y_local, n, ranges).numpy()
         ok_gather = bool(np.allclose(full_y, x @ w.decode().T, rtol=1e-6, atol=1e-6))
+        # in place, rank-major: rank r's padded slice holds its columns
+        rm = parallel.gather_columns(y_local, n, ranges, layout="rank-major").numpy()
+        want = x @ w.decode().T
+        ok_gather &= rm.shape[0] == world and all(
+            np.allclose(rm[r][:, : b - a], want[:, a:b], rtol=1e-6, atol=1e-6) for r, (a, b) in enumerate(ranges))
+        # equal ranges: the one-copy column layout of (E, M, width) shards
+        even = [(r * 5, (r + 1) * 5) for r in range(world)]
+        y_even = torch.from_numpy(np.full((2, m, 5), rank, np.float32) + np.arange(5, dtype=np.float32))
+        full_even = parallel.gather_columns(y_even, 5 * world, even).numpy()
+        expect = np.concatenate([np.full((2, m, 5), r, np.float32) + np.arange(5, dtype=np.float32)
+                                 for r in range(world)], axis=-1)
+        ok_gather &= bool(np.array_equal(full_even, expect))
         queue.put((rank, ok_encode, ok_gather))
     finally:
         dist.destroy_process_group()

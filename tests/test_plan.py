@@ -157,6 +157,27 @@ def test_schema2_dense_and_coded_slot_sizes():
     assert probe(plan2(17, 4096, 14336, 4096, 32, flags=2))[0] == 0
 
 
+def test_schema2_tensor_core_dense_workspace():
+    """Op 16 with flag 8 (the tensor-core kernel): the workspace in in4 holds
+    bf16 hi and lo projections of one pass of at most 128 rows,
+    2 * roundup(rows, 8) x 16 K / G per expert; the flag needs W stored
+    N x K (bit 1), the canonical layout and (K / G) % 32 == 0."""
+    n, k, g, e = 11008, 4096, 16, 3
+    words = (n * k // g + 7) // 8
+    for m, rows in ((1, 8), (8, 8), (37, 40), (64, 64), (128, 128), (300, 128)):
+        assert required(plan2(16, m, n, k, g, flags=10, batch=e)) == [
+            e * m * k * 4, e * words * 4, e * 64 * g, 0, e * 2 * rows * 16 * (k // g) * 2, e * m * n * 4, 0, 4]
+    for flags, k2 in ((8, k), (14, k), (10, 16 * 33), (10, 16 * 32 + 3)):
+        assert refusal(plan2(16, 4, 64, k2, g, flags=flags))[1].endswith("vq2-unsupported-flags"), (flags, k2)
+    # the workspace is written: it may alias no other operand
+    ok = plan2(16, 8, 128, 512, 16, flags=10)
+    caps = [8 * 512 * 4, 128 * 512 // 16 // 2, 1024, 0, 2 * 8 * 16 * 32 * 2, 8 * 128 * 4, 0, 4]
+    assert validate_buffers(ok, caps, [1, 2, 3, 0, 4, 5, 0, 6]) == 0
+    assert validate_buffers(ok, caps, [1, 2, 3, 0, 1, 5, 0, 6]) != 0
+    caps[4] -= 1
+    assert validate_buffers(ok, caps, [1, 2, 3, 0, 4, 5, 0, 6]) != 0
+
+
 def test_schema2_adamw_and_large_slot_sizes():
     n, g, e, s = 4096 * 1024, 8, 8, 4096
     words = (n // g + 7) // 8
@@ -180,6 +201,25 @@ def test_schema2_adamw_and_large_slot_sizes():
         (big // 16 + 7) // 8 * 4, 1024, 0, 0, 0, big * 4, 0, 4]
 
 
+def test_schema2_harness_reductions():
+    """Ops 26 (residual and its float64 sum of squares) and 27 (norm and
+    clip): float64 partials and their total in in4, the float64 results in
+    out1; written in4 may alias nothing."""
+    n, g = 1000, 16
+    ws = (1024 + 1) * 8
+    assert required(plan2(26, n, 1, 1, g, aux0=0x3C000000)) == [
+        4 * n, ((n + g - 1) // g + 7) // 8 * 4, 64 * g, 0, ws, 4 * n, 8, 4]
+    assert required(plan2(27, n, 1, 1, 8, aux0=0, aux1=0x3FF00000)) == [4 * n, 0, 0, 0, ws, 4 * n, 16, 4]
+    for words, name in ((plan2(26, 0, 1, 1, g), "vq2-invalid-geometry"), (plan2(26, n, 1, 1, g, flags=1),
+                        "vq2-unsupported-flags"), (plan2(27, n, 1, 1, 8, aux2=1), "vq2-invalid-aux-word"),
+                        (plan2(27, n, 1, 1, 8, batch=2), "vq2-invalid-batch"), (plan2(28, n, 1, 1, 8),
+                        "vq2-operation-out-of-range")):
+        assert refusal(words)[1].endswith(name), name
+    caps = [4 * n, 0, 0, 0, ws, 4 * n, 16, 4]
+    assert validate_buffers(plan2(27, n, 1, 1, 8), caps, [1, 0, 0, 0, 2, 3, 4, 5]) == 0
+    assert validate_buffers(plan2(27, n, 1, 1, 8), caps, [1, 0, 0, 0, 1, 3, 4, 5]) != 0
+
+
 def test_schema2_refusals_are_named():
     cases = [
         (plan2(15, 1, 1, 1, 8), "vq2-operation-out-of-range"),
@@ -197,7 +237,7 @@ def test_schema2_refusals_are_named():
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=9, aux1=4), "vq2-invalid-aux-word"),
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=8, aux1=33), "vq2-invalid-aux-word"),
         (plan2(24, 64, 1, 1, 8, flags=1, aux0=8, aux1=4, batch=0), "vq2-invalid-batch"),
-        (plan2(26, 64, 1, 1, 8), "vq2-operation-out-of-range"),
+        (plan2(28, 64, 1, 1, 8), "vq2-operation-out-of-range"),
         (plan2(25, 64, 1, 1, 8, flags=2, aux0=8, aux1=4), "vq2-unsupported-flags"),
         (plan2(25, 64, 1, 1, 8, aux0=9, aux1=4), "vq2-invalid-aux-word"),
         (plan2(25, 64, 1, 1, 8, aux0=8, aux1=4, batch=2), "vq2-invalid-batch"),
