@@ -126,20 +126,22 @@ def repack_tile32(codes, n: int, k: int, group: int, *, out=None, status=None):
 
 
 # The dense product runs on the tensor cores from this many activation rows
-# (canonical layout, W stored n x k, (k / group) % 32 == 0). Each tcgen05.mma
-# there costs about the same whatever its N (2 x the rows of X), so below
-# this the shared-memory lookup-table kernels are faster (cfg2 measured: M=16
-# 4.3 ms LUT against 14.5 ms; M=64 16.9 ms LUT against 15.4 ms).
-DENSE_TC_MIN_ROWS = 64
+# (canonical layout, W stored n x k, (k / group) % 32 == 0). The tensor-core
+# kernel computes 64 rows of X per tile whatever M is, so its time is flat up
+# to 64 rows; the shared-memory lookup-table kernels grow with M (cfg2
+# measured: M=32 8.5 ms LUT against 8.9 ms; M=48 12.8 ms against 8.7 ms;
+# M=64 16.9 ms against 9.0 ms).
+DENSE_TC_MIN_ROWS = 40
 DENSE_TC_MAX_ROWS = 128   # rows of X per pass of the tensor-core kernel
 
 
 def dense_tc_workspace_bytes(m: int, k: int, group: int, batch: int) -> int:
     """Bytes of the tensor-core dense product's workspace: the projections of
     one pass of at most 128 rows of X on every codebook entry, as bf16 hi and
-    lo halves, (2 * roundup(rows, 8)) x (16 k / group) per expert."""
+    lo rows, 128 rows per 64-row tile of X, 16 k / group values each, per
+    expert."""
     rows = min(m, DENSE_TC_MAX_ROWS)
-    return batch * 2 * ((rows + 7) // 8 * 8) * 16 * (k // group) * 2
+    return batch * ((rows + 63) // 64) * 128 * 16 * (k // group) * 2
 
 
 def dense_engine(m: int, k: int, group: int, *, transpose_b: bool = True, layout: str = "canonical") -> str:

@@ -42,7 +42,7 @@ MAX_MATMUL_MACS = 1 << 28       # multiply-adds of one schema-1 product
 # schema-2 operations of ack_vq2 (include/alelyon_compute_kit.h)
 OP_DENSE, OP_CODED, OP_ADAMW_SAMPLE, OP_ADAMW_USAGE, OP_ADAMW_ENCODE, OP_ENCODE, OP_DECODE, OP_REPACK, OP_FIT, \
     OP_FIT_VALUES = range(16, 26)
-DENSE_TC_MIN_ROWS = 64   # rows of X from which the dense product runs on the tensor cores
+DENSE_TC_MIN_ROWS = 40   # rows of X from which the dense product runs on the tensor cores
 
 
 # ------------------------------------------------------------ argument checks ----
@@ -708,17 +708,19 @@ class VQDevice:
         kernel (one lookup per code byte); tile32 is faster for M >= 2."""
         return ResidentStack(self, stack, layout)
 
-    def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True, out: np.ndarray | None = None) -> np.ndarray:
+    def matmul_dense_grouped(self, xs, ws, *, transpose_b: bool = True, out: np.ndarray | None = None,
+                             parts: int = 0) -> np.ndarray:
         """E independent products in one launch: `xs` is (E, M, K) float32
         (or a sequence of (M, K)), `ws` a `VQStack` (or a sequence of
         VQArray) of E matrices of one shape and group, or a `ResidentStack`
         (then only X and Y cross the bus, into `out` when given: a
-        contiguous (E, M, N) float32 array, ideally in pinned memory).
+        contiguous (E, M, N) float32 array, ideally in pinned memory; the
+        copies and products overlap over `parts` ranges of the experts).
         Returns (E, M, N)."""
         if type(transpose_b) is not bool:
             raise ValueError("transpose flags must be boolean")
         if isinstance(ws, ResidentStack):
-            return ws.matmul(xs, transpose_b=transpose_b, out=out)
+            return ws.matmul(xs, transpose_b=transpose_b, out=out, parts=parts)
         stack = ws if isinstance(ws, VQStack) else VQStack.from_arrays(ws)
         if len(stack.shape) != 2:
             raise ValueError("vq matmul requires matrices")

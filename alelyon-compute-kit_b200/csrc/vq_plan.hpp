@@ -80,14 +80,13 @@ inline uint64_t tile32_bytes(uint64_t rows, uint64_t cols, uint32_t group) {
 inline uint64_t fit_workspace_stride(uint32_t samples) { return (uint64_t(samples) + 15) / 16 * 16 + 160; }
 
 // The tensor-core path of the dense product (op 16, flag 8) handles X rows in
-// chunks of at most kDenseTcMaxRows; each chunk's projections P (bf16 hi and
-// lo, 2 x roundup(rows, 8) rows of 16 K / G values per expert) live in the
-// caller's workspace (slot in4).
+// passes of at most kDenseTcMaxRows; a pass's projections P (bf16 hi and lo
+// rows interleaved, 128 rows per 64-row tile of X, 16 K / G values each, per
+// expert) live in the caller's workspace (slot in4).
 constexpr uint32_t kDenseTcMaxRows = 128;
-constexpr uint32_t dense_tc_padded_rows(uint32_t rows) { return (rows + 7) / 8 * 8; }
 inline uint64_t dense_tc_workspace_bytes(uint64_t m, uint64_t k, uint32_t group, uint64_t batch) {
-  const uint32_t mc = uint32_t(m < kDenseTcMaxRows ? m : kDenseTcMaxRows);
-  return batch * 2 * dense_tc_padded_rows(mc) * 16 * (k / group) * 2;
+  const uint64_t mc = m < kDenseTcMaxRows ? m : kDenseTcMaxRows;
+  return batch * ((mc + 63) / 64) * 128 * 16 * (k / group) * 2;
 }
 
 // The harness reductions (ops 26, 27) sum float64 partials of at most

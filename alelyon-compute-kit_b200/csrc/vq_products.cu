@@ -462,9 +462,34 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   uint32_t c = 0;
   prefetch(s0, 0);
   asm volatile("cp.async.commit_group;" ::: "memory");
+  uint32_t w[pair::kRows];
+  // one 32-row batch of code words: the rows of `unit`, of the expert whose
+  // (chunk) codes start at cbp and whose first unit is firstp
+  auto load_from = [&](const uint32_t* cbp, uint64_t firstp, uint64_t unit) {
+    const uint32_t n0 = uint32_t(unit - firstp) * pair::kRows;
+    const uint32_t off = n0 * row_words + lane;
+    if (n0 + pair::kRows <= N) {
+#pragma unroll
+      for (int r = 0; r < pair::kRows; ++r) w[r] = __ldcs(cbp + off + uint32_t(r) * row_words);
+    } else {
+#pragma unroll
+      for (int r = 0; r < pair::kRows; ++r) w[r] = n0 + r < N ? __ldcs(cbp + off + uint32_t(r) * row_words) : 0u;
+    }
+  };
+  bool preloaded = false;  // w already holds this warp's first batch of the current (segment, chunk)
   while (s0 < u1) {
     const uint64_t s1 = seg_end(s0);
     const uint32_t e = uint32_t(s0 / nb);
+    // codes of this (expert, chunk): a warp-uniform base, 32-bit lane offsets
+    const uint32_t* cb = codes + uint64_t(e) * words_per_expert + uint64_t(c) * 32u;
+    float* ye = Y + uint64_t(e) * N;
+    uint64_t u = s0 + warp;
+    const uint64_t first = uint64_t(e) * nb;  // units of this segment are one expert's
+    auto load = [&](uint64_t unit) { load_from(cb, first, unit); };
+    // the first batch's code words are in flight during the table build (or
+    // were issued during this warp's last batch of the previous segment)
+    if (!preloaded && u < s1) load(u);
+    preloaded = false;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // this chunk's x and book are in; Q is no longer read
     const float* xs = xbuf;
@@ -521,24 +546,6 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     }
     __syncthreads();
 
-    // codes of this (expert, chunk): a warp-uniform base, 32-bit lane offsets
-    const uint32_t* cb = codes + uint64_t(e) * words_per_expert + uint64_t(c) * 32u;
-    float* ye = Y + uint64_t(e) * N;
-    uint64_t u = s0 + warp;
-    uint32_t w[pair::kRows];
-    const uint64_t first = uint64_t(e) * nb;  // units of this segment are one expert's
-    auto load = [&](uint64_t unit) {
-      const uint32_t n0 = uint32_t(unit - first) * pair::kRows;
-      const uint32_t off = n0 * row_words + lane;
-      if (n0 + pair::kRows <= N) {
-#pragma unroll
-        for (int r = 0; r < pair::kRows; ++r) w[r] = __ldcs(cb + off + uint32_t(r) * row_words);
-      } else {
-#pragma unroll
-        for (int r = 0; r < pair::kRows; ++r) w[r] = n0 + r < N ? __ldcs(cb + off + uint32_t(r) * row_words) : 0u;
-      }
-    };
-    if (u < s1) load(u);
     for (; u < s1; u += pair::kWarps) {
       const uint32_t n0 = uint32_t(u - first) * pair::kRows;
       float v[pair::kRows];
@@ -551,7 +558,24 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         const float q3 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6735));
         v[r] = (q0 + q1) + (q2 + q3);
       }
-      if (u + pair::kWarps < s1) load(u + pair::kWarps);  // in flight during the folding
+      if (u + pair::kWarps < s1) {
+        load(u + pair::kWarps);  // in flight during the folding
+      } else {
+        // this warp's last batch here: the first batch of the next (segment,
+        // chunk) goes in flight now, through the fold, the barrier and the
+        // next table build
+        uint64_t ns = s0;
+        uint32_t nc = c + 1;
+        if (nc == chunks) {
+          nc = 0;
+          ns = s1;
+        }
+        if (ns < u1 && ns + warp < seg_end(ns)) {
+          const uint32_t en = uint32_t(ns / nb);
+          load_from(codes + uint64_t(en) * words_per_expert + uint64_t(nc) * 32u, uint64_t(en) * nb, ns + warp);
+          preloaded = true;
+        }
+      }
       // fold lanes: each step halves the rows a lane keeps; after five, lane l holds row l
 #pragma unroll
       for (int off = pair::kRows / 2; off; off >>= 1) {

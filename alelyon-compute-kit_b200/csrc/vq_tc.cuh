@@ -59,7 +59,15 @@ __device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
 }
 // Wait for the phase of parity `parity` to complete; false after ~2^22 polls
 // (each poll suspends for a hardware-chosen interval), never an endless spin.
+// A non-suspending probe first: a phase that completed earlier (the common
+// case for a stage filled ahead) returns without entering the suspend path.
 __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity) {
+  uint32_t done;
+  asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(done)
+               : "r"(smem_u32(b)), "r"(parity)
+               : "memory");
+  if (done) return true;
   for (uint32_t it = 0; it < (1u << 22); ++it) {
     uint32_t ok;
     asm volatile(

@@ -260,9 +260,10 @@ def time_cfg2(args, torch, cuda, codes, books, m, device, world, local, engine="
     flops = 2.0 * experts * m * N_ROWS * K_COLS
     achieved_hbm = algorithmic / (ms / 1e3) / 1e9
     if engine == "tensor":
-        # the MMA does 2 x 16 K/G = 2 K multiply-adds per (row, X row) for g16: the bf16 hi and lo halves
-        mma_tflops = 2.0 * experts * (2 * ((min(m, 128) + 7) // 8 * 8)) * N_ROWS * (16 * K_COLS // GROUP)
-        mma_tflops *= (m + 127) // 128 / (ms / 1e3) / 1e12
+        # the MMA runs 128 P rows (64 rows of X, bf16 hi and lo) per 64-row tile of X, each
+        # 16 K / G long, against every W row
+        mma_tflops = 2.0 * experts * 128 * ((m + 63) // 64) * N_ROWS * (16 * K_COLS // GROUP)
+        mma_tflops /= (ms / 1e3) * 1e12
         roof = roofline("tensor", mma_tflops, kernel, flops, f"{kernel}_cfg2_m{m}",
                         hbm_gbs=round(achieved_hbm, 1), dense_equivalent_tflops=round(flops / (ms / 1e3) / 1e12, 2),
                         note="MMA TFLOP/s of the one-hot bf16 GEMM (hi and lo halves) against the cuBLAS bf16 peak")
@@ -440,18 +441,39 @@ def run_cfg2_e2e(args, torch, vq, codes, books, x, book, local):
         with backend.resident(stack, layout=args.layout) as weights:
             del stack, host_codes
             for _ in range(3):
-                backend.matmul_dense_grouped(xs, weights, out=ys)
+                backend.matmul_dense_grouped(xs, weights, out=ys, parts=args.e2e_parts)
             steps = max(5, args.steps)
             t0 = time.perf_counter()
             for _ in range(steps):
-                backend.matmul_dense_grouped(xs, weights, out=ys)
+                backend.matmul_dense_grouped(xs, weights, out=ys, parts=args.e2e_parts)
             elapsed = (time.perf_counter() - t0) / steps
-    h2d = xs.nbytes + 4          # X and the cleared status word
+    # the copy ceiling of this host link: one plain pinned copy each way, timed alone
+    dev_x = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    dev_y = torch.empty(pin_y.shape, dtype=torch.float32, device=x.device)
+    link = {}
+    for name, dst, src in (("h2d", dev_x, pin_x), ("d2h", pin_y, dev_y)):
+        dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            dst.copy_(src, non_blocking=True)
+        z.record()
+        torch.cuda.synchronize()
+        link[name] = a.elapsed_time(z) / 5
+    del dev_x, dev_y
+    h2d = xs.nbytes              # X (the status word is cleared on the device)
     d2h = ys.nbytes + 4          # Y and the status word
     return {"value": round(experts * (CODE_BYTES + BOOK_BYTES) / elapsed / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(elapsed * 1e3, 3),
-            "api": "VQDevice.matmul_dense_grouped on a ResidentStack (C ABI ack_vq2; weights resident, "
-                   "X in and Y out through pinned host memory every step)"}
+            "copy_gbs": round((h2d + d2h) / elapsed / 1e9, 2),
+            "link": {"h2d_gbs": round(xs.nbytes / link["h2d"] / 1e6, 2),
+                     "d2h_gbs": round(ys.nbytes / link["d2h"] / 1e6, 2),
+                     "overlapped_bound_ms": round(max(link["h2d"], link["d2h"]), 3),
+                     "serial_copies_ms": round(link["h2d"] + link["d2h"], 3)},
+            "api": "VQDevice.matmul_dense_grouped on a ResidentStack (C ABI ack_vq2_dense_host: weights "
+                   "resident; X in, the product and Y out pipelined over parts of the experts on three "
+                   "streams; pinned host memory)"}
 
 
 def _timed(torch, fn, steps, warmup, world, device, local, label="timed"):
@@ -727,6 +749,72 @@ def run_cfg4_e2e(args, torch, vq, codes, books, experts, count, group, local):
             "host_fit_ms_per_step": round(timings["host"] * 1e3, 1)}
 
 
+def run_profile_cases(args, world, rank, local):
+    """Small cases of every measured kernel, each launched three times, for
+    ncu captures of per-launch DRAM traffic (`--workload profile`): decode and
+    encode of 2^28 values per group and distribution, the grouped product of
+    96 experts at M = 1, 4, 16, 64, cfg3 at its full size, and the fused
+    AdamW pass of 8 cfg4 experts. Prints one line per case; no timing."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    status = cuda.status_word(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    sub = __import__("copy").copy(args)
+    sub.values = 1 << 28
+    for group in (8, 16, 32):
+        for dist in ("gauss", "heavy"):
+            sub.dist = dist
+            x, book = make_codec_data(torch, vq, sub, group, rank, device)
+            codes, _ = cuda.encode(x, book, group, status=status)
+            out = torch.empty_like(x)
+            for _ in range(3):
+                cuda.encode(x, book, group, out=codes, status=status)
+            for _ in range(3):
+                cuda.decode(codes, book, x.numel(), group, out=out, status=status)
+            torch.cuda.synchronize()
+            print("profile case", f"cfg5-g{group}-{dist}", flush=True)
+            del x, codes, out
+    experts = 96
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (experts, CODE_BYTES // 4), generator=gen, device=device,
+                          dtype=torch.int32)
+    books = torch.randn((experts, 16, GROUP), generator=gen, device=device) * 0.25
+    for m in (1, 4, 16, 64):
+        x = torch.randn((experts, m, K_COLS), generator=gen, device=device)
+        engine = cuda.dense_engine(m, K_COLS, GROUP)
+        layout = "canonical" if (m == 1 or engine == "tensor") else "tile32"
+        run_codes = cuda.repack_tile32(codes, N_ROWS, K_COLS, GROUP, status=status)[0] if layout == "tile32" else codes
+        for _ in range(3):
+            cuda.dense(x, run_codes, books, N_ROWS, GROUP, layout=layout, engine=engine, status=status)
+        torch.cuda.synchronize()
+        print("profile case", f"cfg2-m{m}", engine, layout, flush=True)
+    del codes, books, x, run_codes
+    m, n, k, g = 4096, 14336, 4096, 32
+    xc = torch.randint(-2 ** 31, 2 ** 31 - 1, (m * k // g // 8,), generator=gen, device=device, dtype=torch.int32)
+    wc = torch.randint(-2 ** 31, 2 ** 31 - 1, (n * k // g // 8,), generator=gen, device=device, dtype=torch.int32)
+    xb, wb = torch.randn((16, g), device=device), torch.randn((16, g), device=device) * 0.02
+    for _ in range(3):
+        cuda.coded(xc, xb, wc, wb, m, n, k, g, flags=2, status=status)
+    torch.cuda.synchronize()
+    print("profile case cfg3", flush=True)
+    del xc, wc
+    e, count, g = 8, 4096 * 1024, 8
+    words = cuda.words_for(count, g)
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (e, 4, words), generator=gen, device=device, dtype=torch.int32)
+    books = torch.randn((e, 4, 16, g), generator=gen, device=device) * 0.01
+    books[:, 2] = books[:, 2].abs()
+    coefs = torch.from_numpy(np.tile(np.array([1e-3, 0.9, 0.999, 1e-8, 0.01, 0.19, 0.002], np.float32),
+                                     (e, 1))).to(device)
+    for _ in range(3):
+        cuda.adamw_encode(codes, books, coefs, books[:, :3].contiguous(), count, g, batch=e, status=status)
+    torch.cuda.synchronize()
+    print("profile case cfg4", flush=True)
+    return None
+
+
 def run_reference(args, world, rank):
     """The reference arm: the CPU restatement of the path (decode + dot
     product with all host threads) on a bounded sample of the workload."""
@@ -777,6 +865,8 @@ def main():
     ap.add_argument("--experts", type=int, default=768)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-parts", type=int, default=0,
+                    help="expert ranges of the pipelined host-memory product (0: the library's choice)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the other workloads that the default cfg2 run measures beside the headline")
@@ -802,6 +892,8 @@ def main():
         result = run_cfg3(args, world, rank, local)
     elif args.workload == "cfg4":
         result = run_cfg4(args, world, rank, local)
+    elif args.workload == "profile":
+        result = run_profile_cases(args, world, rank, local)
     else:
         raise SystemExit(f"unknown workload {args.workload!r}")
     if world > 1:

@@ -206,7 +206,7 @@ int32_t ack_vq(const AckDevice *dev, const AckBuffer *b0, const AckBuffer *b1, c
 /* bit 3: the tensor-core kernel (one-hot codes times the bf16 hi + lo
  * projections of X on the entries); requires bit 1, the canonical layout
  * and (K / group) % 32 == 0; in4 is its workspace, written:
- * batch x 2 x roundup(min(M, 128), 8) x 16 K / group x 2 bytes. */
+ * batch x ceil(min(M, 128) / 64) x 128 x 16 K / group x 2 bytes. */
 #define ACK_VQ2_DENSE_TENSOR 8u
 
 uint32_t ack_vq2_schema(void);

@@ -159,19 +159,19 @@ def test_schema2_dense_and_coded_slot_sizes():
 
 def test_schema2_tensor_core_dense_workspace():
     """Op 16 with flag 8 (the tensor-core kernel): the workspace in in4 holds
-    bf16 hi and lo projections of one pass of at most 128 rows,
-    2 * roundup(rows, 8) x 16 K / G per expert; the flag needs W stored
+    bf16 hi and lo projections of one pass of at most 128 rows of X, 128 rows
+    of 16 K / G values per 64-row tile, per expert; the flag needs W stored
     N x K (bit 1), the canonical layout and (K / G) % 32 == 0."""
     n, k, g, e = 11008, 4096, 16, 3
     words = (n * k // g + 7) // 8
-    for m, rows in ((1, 8), (8, 8), (37, 40), (64, 64), (128, 128), (300, 128)):
+    for m, tiles in ((1, 1), (8, 1), (37, 1), (64, 1), (65, 2), (128, 2), (300, 2)):
         assert required(plan2(16, m, n, k, g, flags=10, batch=e)) == [
-            e * m * k * 4, e * words * 4, e * 64 * g, 0, e * 2 * rows * 16 * (k // g) * 2, e * m * n * 4, 0, 4]
+            e * m * k * 4, e * words * 4, e * 64 * g, 0, e * tiles * 128 * 16 * (k // g) * 2, e * m * n * 4, 0, 4]
     for flags, k2 in ((8, k), (14, k), (10, 16 * 33), (10, 16 * 32 + 3)):
         assert refusal(plan2(16, 4, 64, k2, g, flags=flags))[1].endswith("vq2-unsupported-flags"), (flags, k2)
     # the workspace is written: it may alias no other operand
     ok = plan2(16, 8, 128, 512, 16, flags=10)
-    caps = [8 * 512 * 4, 128 * 512 // 16 // 2, 1024, 0, 2 * 8 * 16 * 32 * 2, 8 * 128 * 4, 0, 4]
+    caps = [8 * 512 * 4, 128 * 512 // 16 // 2, 1024, 0, 128 * 16 * 32 * 2, 8 * 128 * 4, 0, 4]
     assert validate_buffers(ok, caps, [1, 2, 3, 0, 4, 5, 0, 6]) == 0
     assert validate_buffers(ok, caps, [1, 2, 3, 0, 1, 5, 0, 6]) != 0
     caps[4] -= 1
