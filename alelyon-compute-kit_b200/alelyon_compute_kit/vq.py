@@ -375,7 +375,12 @@ class ResidentStack:
         if self.layout == "tile32" and not transpose_b:
             raise ValueError("the tile32 layout holds W stored N x K (transpose_b=True)")
         backend, device = self.backend, self.backend.device
-        x = _float_array(np.asarray(xs), "activations")
+        # finiteness is checked on the device (the kernels flag nonfinite
+        # products in the status word), not by a host pass over X
+        x = np.asarray(xs)
+        if x.dtype != np.float32:
+            raise ValueError("activations must contain finite float32 values")
+        x = np.ascontiguousarray(x)
         if x.ndim != 3 or x.shape[0] != self.count:
             raise ValueError("activations must be (count, M, K) with one matrix per coded weight")
         e, m, k = x.shape
@@ -403,6 +408,9 @@ class ResidentStack:
                     y.ctypes.data, int(parts), ctypes.byref(status))
             if rc != ack.ACK_OK:
                 raise ack._kit_error("vq2", rc, device._lib.last_error())
+        if status.value == 1:
+            raise ValueError("activations must contain finite float32 values (or the products overflowed): "
+                             "device status=1")
         if status.value:
             raise ack.AckError(f"vq device arithmetic refused: status={status.value}")
         return y

@@ -66,9 +66,14 @@ struct Device {
   cudaDeviceProp prop{};
   int inject_sync = 0;       // test-only: error reported by the next synchronisation
   bool inject_alloc = false; // test-only: the next allocation reports failure
-  // the copy streams and events of ack_vq2_dense_host, created on first use
+  // the copy streams, events and device scratch of ack_vq2_dense_host,
+  // created on first use; the scratch grows to the largest call's need and
+  // is kept until close (returning it to the driver on every call costs
+  // milliseconds of page mapping per call)
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   cudaEvent_t ev[7] = {};    // allocated, h_done[2], k_done[2], d_done[2]
+  void* scratch = nullptr;
+  uint64_t scratch_bytes = 0;
 };
 
 struct Registry {
@@ -360,6 +365,9 @@ ACK_EXPORT int32_t ack_close(AckDevice* handle) {
           if (st) cudaStreamDestroy(st);
         for (cudaEvent_t ev : dev->ev)
           if (ev) cudaEventDestroy(ev);
+        if (dev->scratch) cudaFree(dev->scratch);
+        dev->scratch = nullptr;
+        dev->scratch_bytes = 0;
       }
     }
     dev->closed = true;
@@ -718,6 +726,18 @@ cudaError_t pipeline_streams(Device& d) {
   return e;
 }
 
+// At least `bytes` of the device's pipeline scratch. Called with the device
+// lock held and its streams idle (every call ends with a stream sync).
+cudaError_t pipeline_scratch(Device& d, uint64_t bytes) {
+  if (d.scratch_bytes >= bytes) return cudaSuccess;
+  if (d.scratch) cudaFree(d.scratch);
+  d.scratch = nullptr;
+  d.scratch_bytes = 0;
+  cudaError_t e = cudaMalloc(&d.scratch, bytes);
+  if (e == cudaSuccess) d.scratch_bytes = bytes;
+  return e;
+}
+
 }  // namespace
 
 ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* plan, size_t plan_len,
@@ -762,7 +782,7 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   if (pe != ack::PlanError::None) return plan_refused(entry, pe, 2, slot);
   const uint32_t E = p.batch;
   const uint64_t M = p.m, N = p.n, K = p.k;
-  if (parts == 0) parts = uint32_t(std::min<uint64_t>(8, E));
+  if (parts == 0) parts = uint32_t(std::min<uint64_t>(16, E));  // measured best for cfg2 M = 1 (12-24 alike)
   parts = uint32_t(std::min<uint64_t>(parts, E));
   const uint32_t per = (E + parts - 1) / parts;
   const uint64_t x_part = uint64_t(per) * M * K * 4, y_part = uint64_t(per) * M * N * 4;
@@ -773,20 +793,26 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
   cudaStream_t cs = dev->stream, in = dev->copy_in, out = dev->copy_out;
   cudaEvent_t allocated = dev->ev[0], *h_done = dev->ev + 1, *k_done = dev->ev + 3, *d_done = dev->ev + 5;
+  // scratch: two buffers each of X, Y and (tensor-core path) workspace per part, and the status word
+  auto up = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+  const uint64_t need = 2 * (up(x_part) + up(y_part) + up(ws_part)) + 256;
+  e = pipeline_scratch(*dev, need);
+  if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
   void *xb[2] = {}, *yb[2] = {}, *wb[2] = {};
-  uint32_t* status = nullptr;
-  auto fail = [&](cudaError_t err) {
-    for (void* q : {xb[0], xb[1], yb[0], yb[1], wb[0], wb[1], static_cast<void*>(status)})
-      if (q) cudaFreeAsync(q, cs);
-    return cuda_fail(*dev, err, entry);
-  };
-  for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
-    e = cudaMallocAsync(&xb[b], x_part, cs);
-    if (e == cudaSuccess) e = cudaMallocAsync(&yb[b], y_part, cs);
-    if (e == cudaSuccess && ws_part) e = cudaMallocAsync(&wb[b], ws_part, cs);
+  {
+    char* at = static_cast<char*>(dev->scratch);
+    for (int b = 0; b < 2; ++b) {
+      xb[b] = at;
+      at += up(x_part);
+      yb[b] = at;
+      at += up(y_part);
+      wb[b] = ws_part ? at : nullptr;
+      at += up(ws_part);
+    }
   }
-  if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&status), 4, cs);
-  if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, 4, cs);
+  uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<char*>(dev->scratch) + need - 256);
+  auto fail = [&](cudaError_t err) { return cuda_fail(*dev, err, entry); };
+  e = cudaMemsetAsync(status, 0, 4, cs);
   if (e == cudaSuccess) e = cudaEventRecord(allocated, cs);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(in, allocated, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(out, allocated, 0);
@@ -819,14 +845,12 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
                                               cudaMemcpyDeviceToHost, out);
     if (e == cudaSuccess) e = cudaEventRecord(d_done[b], out);
   }
-  // the scratch is freed on the compute stream after the last copies out
+  // the status word is read on the compute stream after the last copies out
   if (e == cudaSuccess) e = cudaEventRecord(d_done[0], out);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, d_done[0], 0);
   uint32_t host_status = 0;
   if (e == cudaSuccess) e = cudaMemcpyAsync(&host_status, status, 4, cudaMemcpyDeviceToHost, cs);
   if (e != cudaSuccess) return fail(e);
-  for (void* q : {xb[0], xb[1], yb[0], yb[1], wb[0], wb[1], static_cast<void*>(status)})
-    if (q) cudaFreeAsync(q, cs);
   e = sync_stream(*dev);
   if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
   *status_out = host_status;

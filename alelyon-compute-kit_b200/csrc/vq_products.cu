@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_dense_lut(const float* __restri
     for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) bits |= finite32(sbook[i]) ? 0u : kNonfinite;
     flag_warp(status, bits);
   }
+  uint32_t ybits = 0;  // nonfinite outputs (from x, or overflow)
   const uint32_t nb = (r1 - r0 + kThreads - 1) / kThreads;
 
   for (uint32_t m0 = 0; m0 < M; m0 += MC) {
@@ -212,7 +213,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_dense_lut(const float* __restri
             if (m < int(mc)) {
               const float y = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
               float* dst = Yb + uint64_t(m0 + m) * N + row;
-              *dst = t0 ? *dst + y : y;
+              const float v = t0 ? *dst + y : y;
+              *dst = v;
+              ybits |= finite32(v) ? 0u : kNonfinite;  // a nonfinite partial sum stays nonfinite
             }
           }
         }
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_dense_lut(const float* __restri
       }
     }
   }
+  flag_warp(status, ybits);
 }
 
 // Repack E canonical N x K images (vectors along K) into the tile32 layout:
@@ -278,6 +282,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
   const bool x_vec = (reinterpret_cast<uintptr_t>(X) & 15u) == 0;
   const uint64_t u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint32_t ybits = 0;  // nonfinite outputs (from x, or overflow)
   for (uint64_t s0 = u0; s0 < u1;) {
     const uint32_t e = uint32_t(s0 / ntiles);
     const uint64_t s1 = min(u1, uint64_t(e + 1) * ntiles);
@@ -377,7 +382,9 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
               if (m < int(mc)) {
                 const float y = (acc[m][0].x + acc[m][0].y) + (acc[m][1].x + acc[m][1].y);
                 float* dst = Yb + uint64_t(m0 + m) * N + row;
-                *dst = t0 ? *dst + y : y;
+                const float v = t0 ? *dst + y : y;
+                *dst = v;
+                ybits |= finite32(v) ? 0u : kNonfinite;  // a nonfinite partial sum stays nonfinite
               }
             }
           }
@@ -386,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
     }
     s0 = s1;
   }
+  flag_warp(status, ybits);
 }
 
 // ------------------------------- dense X times coded W^T, M = 1: byte table --
@@ -477,6 +485,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     }
   };
   bool preloaded = false;  // w already holds this warp's first batch of the current (segment, chunk)
+  uint32_t ybits = 0;      // nonfinite outputs (from x, or overflow)
   while (s0 < u1) {
     const uint64_t s1 = seg_end(s0);
     const uint32_t e = uint32_t(s0 / nb);
@@ -589,7 +598,9 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       }
       if (n0 + lane < N) {  // lane l now holds row n0 + l
         float* y = ye + n0 + lane;
-        *y = c == 0 ? v[0] : *y + v[0];
+        const float nv = c == 0 ? v[0] : *y + v[0];
+        *y = nv;
+        ybits |= finite32(nv) ? 0u : kNonfinite;  // a nonfinite partial sum stays nonfinite
       }
     }
     // advance: the next chunk of this segment, or the next segment
@@ -598,6 +609,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       s0 = s1;
     }
   }
+  flag_warp(status, ybits);
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 

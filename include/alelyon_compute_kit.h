@@ -260,9 +260,11 @@ int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslo
  * computes and part c-2's Y is copied out on a third, so the copies and the
  * products overlap (host memory must be page-locked for the copies to be
  * asynchronous). Returns when all of `y` is written; `*status_out` (not
- * null) receives the status word of the whole product, read once. The
+ * null) receives the status word of the whole product, read once; bit 1
+ * there covers a nonfinite X or product (X is not scanned on the host). The
  * device scratch (two parts of X and Y, and the tensor-core workspace when
- * flag 8 is set) comes from the device's stream-ordered pool. */
+ * flag 8 is set) is allocated on first use, grows to the largest call's
+ * need and is kept by the device until ack_close. */
 int32_t ack_vq2_dense_host(const AckDevice *dev, const uint8_t *plan, size_t plan_len, const AckBuffer *codes,
                            const AckBuffer *books, const float *x, float *y, uint32_t parts, uint32_t *status_out);
 

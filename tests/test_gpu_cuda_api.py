@@ -121,3 +121,49 @@ def test_tile32_layout_is_bitwise_the_canonical_product(group):
         y64 = x[0].astype(np.float64) @ wd.T
         err = np.max(np.abs(y_t32[0].cpu().numpy() - y64) / (np.abs(x[0]).astype(np.float64) @ np.abs(wd).T))
         assert err <= 1e-5
+
+
+@pytest.mark.parametrize("m,engine,layout", [(1, "lut", "canonical"), (2, "lut", "canonical"),
+                                             (4, "lut", "tile32"), (16, "lut", "tile32"),
+                                             (64, "tensor", "canonical")])
+def test_dense_flags_nonfinite_activations(m, engine, layout):
+    """Every dense engine reports a NaN or infinity in X (or an overflowed
+    sum) in the status word, as the wire API refuses nonfinite input: the
+    byte-pair GEMV (M = 1, K a multiple of 256 g), the LUT kernels and the
+    tensor-core product. A finite X leaves the word clear."""
+    group, n, k, e = 16, 11008, 4096, 2   # M = 1: 688 row batches, enough for the byte-pair kernel
+    rng = np.random.default_rng(70 + m)
+    dev = torch.device("cuda:0")
+    codes = torch.from_numpy(o.pack(rng.integers(0, 16, e * n * k // group)).view(np.int32)).to(dev).view(e, -1)
+    books = torch.from_numpy(rng.standard_normal((e, 16, group)).astype(np.float32) * 0.05).to(dev)
+    run = codes if layout == "canonical" else cuda.repack_tile32(codes, n, k, group)[0]
+    ws = (torch.empty(cuda.dense_tc_workspace_bytes(m, k, group, e), dtype=torch.uint8, device=dev)
+          if engine == "tensor" else None)
+    x = torch.from_numpy(rng.standard_normal((e, m, k)).astype(np.float32)).to(dev)
+    _, status = cuda.dense(x, run, books, n, group, layout=layout, engine=engine, workspace=ws)
+    assert int(status.item()) == 0
+    for bad in (float("nan"), float("inf")):
+        xb = x.clone()
+        xb[e - 1, m - 1, k // 2 + 3] = bad
+        _, status = cuda.dense(xb, run, books, n, group, layout=layout, engine=engine, workspace=ws)
+        assert int(status.item()) & 1, (bad, m, engine)
+
+
+def test_resident_product_refuses_nonfinite_activations():
+    """The resident-weights product checks X on the device, not by a host
+    pass, and refuses a nonfinite X with the wire API's error type."""
+    from alelyon_compute_kit import vq
+    group, n, k, e = 16, 512, 4096, 2
+    rng = np.random.default_rng(9)
+    ws = [vq.VQArray((n, k), group, o.pack(rng.integers(0, 16, n * k // group)),
+                     rng.standard_normal((16, group)).astype(np.float32) * 0.05) for _ in range(e)]
+    x = rng.standard_normal((e, 1, k)).astype(np.float32)
+    with ack.Device() as d:
+        backend = vq.VQDevice(d)
+        with backend.resident(vq.VQStack.from_arrays(ws), layout="canonical") as weights:
+            backend.matmul_dense_grouped(x, weights)
+            x[1, 0, 7] = np.nan
+            with pytest.raises(ValueError, match="finite"):
+                backend.matmul_dense_grouped(x, weights)
+            with pytest.raises(ValueError, match="finite"):
+                backend.matmul_dense_grouped(x.astype(np.float64), weights)
