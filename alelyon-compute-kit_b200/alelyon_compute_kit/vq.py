@@ -361,7 +361,9 @@ class ResidentStack:
     def _check(status) -> None:
         flags = int(status.download(np.uint32)[0])
         if flags:
-            raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            names = [name for bit, name in ((1, "nonfinite"), (2, "layout"), (4, "optimizer"), (8, "stalled"))
+                     if flags & bit]
+            raise ack.AckError(f"vq device arithmetic refused: status={flags} ({', '.join(names) or 'unknown'})")
 
     def matmul(self, xs, *, transpose_b: bool = True, out: np.ndarray | None = None,
                parts: int = 0) -> np.ndarray:
@@ -498,7 +500,9 @@ class VQDevice:
         must not be used."""
         flags = int(status.download(np.uint32)[0])
         if flags:
-            raise ack.AckError(f"vq device arithmetic refused: status={flags}")
+            names = [name for bit, name in ((1, "nonfinite"), (2, "layout"), (4, "optimizer"), (8, "stalled"))
+                     if flags & bit]
+            raise ack.AckError(f"vq device arithmetic refused: status={flags} ({', '.join(names) or 'unknown'})")
 
     def _run(self, words, inputs, output_bytes: int, dtype):
         """One schema-1 `ack_vq` call on fresh device buffers: the inputs

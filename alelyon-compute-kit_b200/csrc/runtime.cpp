@@ -602,8 +602,12 @@ ACK_EXPORT int32_t ack_inject_fault(const AckDevice* handle, int32_t kind, int32
     dev->inject_sync = code;
   } else if (kind == 1) {
     dev->inject_alloc = true;
+  } else if (kind == 2 && (code == 1 || code == 2)) {
+    ack::set_encode_stall_test(uint32_t(code));
   } else {
-    set_error(format("ack_inject_fault: kind %d is not 0 (synchronisation, nonzero code) or 1 (allocation)", kind));
+    set_error(format("ack_inject_fault: kind %d is not 0 (synchronisation, nonzero code), 1 (allocation) or 2 "
+                     "(encode stall test, code 1 or 2)",
+                     kind));
     return ACK_ERR_SHAPE;
   }
   return ACK_OK;

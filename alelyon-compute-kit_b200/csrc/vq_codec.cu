@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -359,7 +360,7 @@ __device__ __noinline__ void refine_queue(const float* __restrict__ x, uint32_t*
 template <int G, int SLOT>
 __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm)
     k_encode_tc(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ x, uint64_t n,
-                uint32_t* __restrict__ codes, uint32_t* __restrict__ status) {
+                uint32_t* __restrict__ codes, uint32_t* __restrict__ status, uint32_t stall_test) {
   using Book = CBook<G, SLOT, 0>;
   using W = tc::Swz<G>;
   using K = tc::Cfg<G>;
@@ -421,14 +422,18 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
   bool ok = true;
+  // stall_test (host-injected, test only): 1 = the producer issues no load,
+  // 2 = the consumers take no accumulator; the pipeline waits then run out
+  // after kTestPolls, set kStalled, and the drains below still complete
+  const uint32_t lim = stall_test ? tc::kTestPolls : tc::kPolls;
 
   if (warp == 4 * C) {
     // producer: one TMA tensor load (two for 512-row tiles) per tile
     if (lane == 0) {
       uint32_t issued = 0;
-      for (uint32_t k = 0; k < T && ok; ++k) {
+      for (uint32_t k = 0; k < T && ok && stall_test != 1; ++k) {
         const uint32_t s = k % S;
-        if (k >= S && !(ok = tc::mb_wait(&sfree[s], ((k / S) - 1) & 1))) break;
+        if (k >= S && !(ok = tc::mb_wait(&sfree[s], ((k / S) - 1) & 1, lim))) break;
         ++issued;
         tc::mb_expect(&full[s], K::kTile);
         const int32_t row = int32_t((blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H);
@@ -452,8 +457,8 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       uint32_t committed = 0;
       for (uint32_t k = 0; k < T && ok; ++k) {
         const uint32_t s = k % S, q = k % C;
-        if (!(ok = tc::mb_wait(&full[s], (k / S) & 1))) break;
-        if (k >= C && !(ok = tc::mb_wait(&afree[q], ((k / C) - 1) & 1))) break;
+        if (!(ok = tc::mb_wait(&full[s], (k / S) & 1, lim))) break;
+        if (k >= C && !(ok = tc::mb_wait(&afree[q], ((k / C) - 1) & 1, lim))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
         for (int h = 0; h < H; ++h) {
@@ -489,11 +494,11 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     constexpr float kappa1 = 1.0f / 1024 + 1.0f / 2048 + float(G + 8) / 2097152.0f;
     constexpr float kappa_t = float(G + 9) / 2097152.0f;  // TIGHT: all but the x residual
     uint32_t qhead = 0, qtail = 0;
-    for (uint32_t k = q; k < T && ok; k += C) {
+    for (uint32_t k = q; k < T && ok && stall_test != 2; k += C) {
       const uint32_t s = k % S;
       // warp-uniform outcomes: tcgen05.ld below is .sync.aligned
-      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&full[s], (k / S) & 1)))) break;
-      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&done[q], (k / C) & 1)))) break;
+      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&full[s], (k / S) & 1, lim)))) break;
+      if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&done[q], (k / C) & 1, lim)))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll(G == 8 ? 2 : 1)
       for (int h = 0; h < H; ++h) {
@@ -924,6 +929,11 @@ bool encode_tensor_map(const float* x, uint64_t complete, CUtensorMap* map) {
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The host-injected stall test of the next k_encode_tc launch (test only,
+// armed through ack_inject_fault): 0 none, 1 or 2 as the kernel describes.
+std::atomic<uint32_t> g_encode_stall_test{0};
+uint32_t take_encode_stall_test() { return g_encode_stall_test.exchange(0); }
+
 template <int G>
 struct RunEncode {
   static cudaError_t run(const float* x, uint64_t n, const float* book, uint32_t* codes, uint32_t* status,
@@ -977,7 +987,9 @@ struct RunEncode {
     const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sm_count()) * K::kBlocksPerSm));
     BookSlot slot(s, book, 1, G);
     if (slot.error() != cudaSuccess) return slot.error();
-#define ACK_LAUNCH_ENCODE(S) k_encode_tc<G, S><<<grid, K::kThreads, K::kSmem, s>>>(map, x, n, codes, status)
+    const uint32_t stall_test = take_encode_stall_test();
+#define ACK_LAUNCH_ENCODE(S) \
+  k_encode_tc<G, S><<<grid, K::kThreads, K::kSmem, s>>>(map, x, n, codes, status, stall_test)
     ACK_SLOT_SWITCH(slot.index(), ACK_LAUNCH_ENCODE)
 #undef ACK_LAUNCH_ENCODE
     const cudaError_t e = cudaGetLastError();
@@ -1087,4 +1099,8 @@ cudaError_t launch_adamw_fused(const Plan& p, void* const* ptr, cudaStream_t s) 
   return by_group<RunAdamwFused>(p.group, p, ptr, s);
 }
 
+}  // namespace ack
+
+namespace ack {
+void set_encode_stall_test(uint32_t mode) { g_encode_stall_test.store(mode); }
 }  // namespace ack

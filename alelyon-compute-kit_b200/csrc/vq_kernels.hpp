@@ -21,4 +21,9 @@ constexpr uint32_t kStaticEncodeBooks = 64;
 cudaError_t encode_noalloc(const float* x, uint64_t n, uint32_t batch, const float* books, uint32_t group,
                            uint32_t* codes, uint32_t* status, cudaStream_t stream);
 
+// Test only (ack_inject_fault kind 2): arm a stall test for the next
+// tensor-core encode launch in this process (1: its producer issues no load;
+// 2: its consumers take no accumulator). Defined in vq_codec.cu.
+void set_encode_stall_test(uint32_t mode);
+
 }  // namespace ack

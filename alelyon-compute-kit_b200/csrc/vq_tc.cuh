@@ -57,18 +57,22 @@ __device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// Wait for the phase of parity `parity` to complete; false after ~2^22 polls
-// (each poll suspends for a hardware-chosen interval), never an endless spin.
-// A non-suspending probe first: a phase that completed earlier (the common
-// case for a stage filled ahead) returns without entering the suspend path.
-__device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity) {
+constexpr uint32_t kPolls = 1u << 22;       // the normal bound of a wait
+constexpr uint32_t kTestPolls = 1u << 10;   // pipeline waits under a host-injected stall test
+
+// Wait for the phase of parity `parity` to complete; false after `polls`
+// polls (each suspends for a hardware-chosen interval), never an endless
+// spin. A non-suspending probe first: a phase that completed earlier (the
+// common case for a stage filled ahead) returns without entering the
+// suspend path.
+__device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity, uint32_t polls = kPolls) {
   uint32_t done;
   asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                : "=r"(done)
                : "r"(smem_u32(b)), "r"(parity)
                : "memory");
   if (done) return true;
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
+  for (uint32_t it = 0; it < polls; ++it) {
     uint32_t ok;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"

@@ -1,6 +1,6 @@
 """Benchmark of the vq4 hot path on B200 (one JSON line on rank 0).
 
-Default workload (the metric's configuration): packed
+Default workload (cfg2, the configuration the headline metric is quoted on): packed
 GEMV with coded weights, W = 11008 x 4096 FP32 N(0, 0.02^2) with every
 16-value block L2-normalised, group 16, FP32 activations X of 1 x 4096 from
 N(0, 1). To exercise HBM rather than L2 or launch latency, one step is one
@@ -12,7 +12,7 @@ headline metric is coded-weight GB/s = (code bytes + codebook bytes) / time.
   e2e      the same metric through VQDevice.matmul_dense_grouped with host
            (pinned) buffers and device-resident weights: X is copied to the
            device and Y back every step
-  roofline the k_dense_lut launch against the measured HBM copy bandwidth
+  roofline the k_dense_pair launch against the measured HBM copy bandwidth
   cpu_baseline / --impl reference
            the CPU restatement (decode + dot product, all host threads) on a
            bounded sample of the same experts
@@ -22,7 +22,10 @@ operands coded, 4096 x 4096 times 14336 x 4096, g32), cfg4 (fused VQAdamW,
 8 experts of 3 x 4096 x 1024 g8 per GPU), encode / decode (2^30 values).
 
 Multi-GPU (torchrun): every rank runs its own E experts (expert sharding,
-no collective, weak scaling); the reported time is the max over ranks.
+no collective, weak scaling); the reported time is the max over ranks. The
+line's `sharded` object adds the row splits of cfg2 and cfg3 across ranks
+(strong scaling) without and with the NCCL all-gather of the output, and the
+cfg4 VQAdamW step at 8 experts per GPU.
 """
 from __future__ import annotations
 
@@ -339,6 +342,8 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
       scaling (the whole job is the E full products). Timed without and with
       the NCCL all-gather of the Y shards, which lands in place in a
       rank-major (world, E, M, rows) buffer.
+    * cfg3 split the same way (rows of the coded W, columns of C), timed
+      without and with the all-gather of C's column shards.
     * cfg4: the VQAdamW step of 8 experts per GPU (64 at 8 GPUs), experts
       split across ranks, no collective."""
     import copy
@@ -380,6 +385,42 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
         "allgather_bytes_per_rank": send.numel() * 4, "allgather_share": round(max(0.0, ms_g - ms_c) / ms_g, 4),
         "gather_layout": "rank-major (world, E, M, rows), in place", "clocks": clocks}}
     del shard, x, y, send, gathered
+    torch.cuda.empty_cache()
+    # cfg3: W rows (output columns of C) split across ranks, both operands coded
+    from alelyon_compute_kit import vq
+    xc, xb, wc, wb, m3, n3, k3, g3 = make_cfg3(torch, cuda, vq, device)
+    ranges3 = parallel.row_ranges(n3, k3, g3, world)
+    a3, b3 = ranges3[rank]
+    width3 = max(b - a for a, b in ranges3)
+    wshard = wc.view(n3, k3 // g3 // 8)[a3:b3].contiguous().view(-1)
+    del wc
+    y3 = torch.zeros((m3, b3 - a3), dtype=torch.float32, device=device)
+    send3 = y3 if b3 - a3 == width3 else torch.zeros((m3, width3), dtype=torch.float32, device=device)
+    gathered3 = torch.empty((world, m3, width3), dtype=torch.float32, device=device)
+
+    def compute3():
+        cuda.coded(xc, xb, wshard, wb, m3, b3 - a3, k3, g3, flags=2, out=y3, status=status)
+
+    def compute3_gather():
+        compute3()
+        if send3 is not y3:
+            send3[:, : b3 - a3] = y3
+        dist.all_gather_into_tensor(gathered3.view(-1), send3.view(-1))
+
+    ms3_c, clocks3 = _timed(torch, compute3, args.steps, args.warmup, world, device, local, label="sharded-cfg3")
+    ms3_g, _ = _timed(torch, compute3_gather, args.steps, args.warmup, world, device, local,
+                      label="sharded-cfg3-gather")
+    cuda.check(status)
+    flops3 = 2.0 * m3 * n3 * k3
+    out["cfg3-nsplit"] = {
+        "metric": "vq4 both-coded GEMM effective TFLOP/s, W rows split across ranks (cfg3, strong scaling)",
+        "unit": "TFLOP/s", "rows_per_rank": width3, "scaling": "strong",
+        "ms_per_step_compute": round(ms3_c, 4), "value_compute": round(flops3 / (ms3_c / 1e3) / 1e12, 2),
+        "ms_per_step_with_allgather": round(ms3_g, 4),
+        "value_with_allgather": round(flops3 / (ms3_g / 1e3) / 1e12, 2),
+        "allgather_bytes_per_rank": send3.numel() * 4, "allgather_share": round(max(0.0, ms3_g - ms3_c) / ms3_g, 4),
+        "gather_layout": "rank-major (world, M, rows), in place", "clocks": clocks3}
+    del xc, wshard, y3, send3, gathered3
     torch.cuda.empty_cache()
     sub = copy.copy(args)
     sub.no_e2e = sub.no_cpu = True
@@ -599,14 +640,10 @@ def run_codec(args, world, rank, local, which):
     return run_codec_both(args, world, rank, local, (which,))[which]
 
 
-def run_cfg3(args, world, rank, local):
-    """cfg 3: both operands coded, X 4096 x 4096 (g32, own book) times
-    W 14336 x 4096 (g32) transposed; the 16x16 codebook inner-product table."""
-    import torch
-
-    from alelyon_compute_kit import cuda, vq
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
+def make_cfg3(torch, cuda, vq, device):
+    """cfg 3 operands: X 4096 x 4096 ~ N(0, 1) and W 14336 x 4096 ~
+    N(0, 0.02^2), each encoded g32 with a book fitted on the CPU from a
+    4,096-vector sample. Returns (xc, xb, wc, wb, m, n, k, group)."""
     m, n, k, group = 4096, 14336, 4096, 32
     gen = torch.Generator(device=device)
     gen.manual_seed(8)
@@ -618,7 +655,19 @@ def run_cfg3(args, world, rank, local):
     xc, status = cuda.encode(x, xb, group)
     wc, _ = cuda.encode(w, wb, group, status=status)
     cuda.check(status)
-    del x, w
+    return xc, xb, wc, wb, m, n, k, group
+
+
+def run_cfg3(args, world, rank, local):
+    """cfg 3: both operands coded, X 4096 x 4096 (g32, own book) times
+    W 14336 x 4096 (g32) transposed; the 16x16 codebook inner-product table."""
+    import torch
+
+    from alelyon_compute_kit import cuda, vq
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    xc, xb, wc, wb, m, n, k, group = make_cfg3(torch, cuda, vq, device)
+    status = cuda.status_word(device)
     y = torch.empty((m, n), dtype=torch.float32, device=device)
     fn = lambda: cuda.coded(xc, xb, wc, wb, m, n, k, group, flags=2, out=y, status=status)  # noqa: E731
     ms, clocks = _timed(torch, fn, args.steps, args.warmup, world, device, local)

@@ -319,7 +319,13 @@ int32_t ack_vq_plan_validate_dispatch(const uint8_t *plan, size_t plan_len, cons
  * process environment has ACK_FAULT_INJECTION=1. kind 0: the next stream
  * synchronisation reports `code` (a cudaError_t) after the real wait ran;
  * kind 1: the next buffer allocation reports cudaErrorMemoryAllocation after
- * freeing what it allocated. Nothing is injected on the GPU. ---- */
+ * freeing what it allocated; kind 2: the next tensor-core encode launch (in
+ * this process) runs a stall test, code 1 its TMA producer issuing no load,
+ * code 2 its consumers taking no accumulator: the bounded waits that nothing
+ * will satisfy run out after a short bound, the kernel sets
+ * ACK_VQ_STATUS_STALLED, waits for its own loads and MMAs in flight and
+ * returns, and the context stays usable. No fault, trap or hang is caused on
+ * the GPU. ---- */
 int32_t ack_inject_fault(const AckDevice *dev, int32_t kind, int32_t code);
 
 #ifdef __cplusplus

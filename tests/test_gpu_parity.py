@@ -183,7 +183,7 @@ def test_dense_activation_product_within_tolerance(backend, group):
 
 
 def test_dense_matches_cfg2_shapes(backend):
-    """One BASELINE config-2 matrix (11008 x 4096, g16) for M in {1, 4, 16, 64}."""
+    """One cfg2 matrix (11008 x 4096, g16) for M in {1, 4, 16, 64}."""
     rng = np.random.default_rng(7)
     n, k, group = 11008, 4096, 16
     book = rand_book(rng, group, 0.25)

@@ -77,3 +77,34 @@ def test_device_choice_by_environment(monkeypatch):
     monkeypatch.setenv("ACK_DEVICE", "gpu:0")
     with ack.Device() as dev:
         assert "B200" in dev.name
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_injected_encode_stall_reports_and_the_context_stays_usable(monkeypatch, mode):
+    """A bounded wait that nothing will satisfy runs out on the GPU: the
+    host arms a stall test of the next tensor-core encode (1: its TMA
+    producer issues no load; 2: its consumers take no accumulator, so loads
+    and MMAs are in flight when the waits give up). The kernel sets the
+    stalled bit, drains its own work and returns; the host reads the bit,
+    and the next encode on the same device is bit-exact again."""
+    import vq_oracle_c as oc
+    monkeypatch.setenv("ACK_FAULT_INJECTION", "1")
+    group, n = 16, 1 << 22
+    rng = np.random.default_rng(40 + mode)
+    values = rng.standard_normal(n).astype(np.float32)
+    book = vq.fit_codebook(values, group=group)
+    with ack.Device() as dev:
+        backend = vq.VQDevice(dev)
+        assert dev._lib.cdll.ack_inject_fault(dev._handle, 2, mode) == ack.ACK_OK
+        with pytest.raises(ack.AckError, match="stalled"):
+            backend.encode(values, book, group=group)
+        again = backend.encode(values, book, group=group)
+        np.testing.assert_array_equal(again.codes, oc.encode(values, book, group))
+        assert dev.leaked_on_poison() == 0
+
+
+def test_stall_injection_refuses_unknown_codes(monkeypatch):
+    monkeypatch.setenv("ACK_FAULT_INJECTION", "1")
+    with ack.Device() as dev:
+        assert dev._lib.cdll.ack_inject_fault(dev._handle, 2, 3) == ack.ACK_ERR_SHAPE
+        assert "stall" in dev._lib.last_error()
