@@ -237,6 +237,16 @@ class _Lib:
         c.ack_inject_fault.argtypes = [vp, ctypes.c_int32, ctypes.c_int32]
         c.ack_kernel_manifest.restype = ctypes.c_int32
         c.ack_kernel_manifest.argtypes = [ctypes.c_char_p, sz, ctypes.POINTER(sz)]
+        u32, dp = ctypes.c_uint32, ctypes.POINTER(ctypes.c_double)
+        # the NF4 comparator (ffi.rs:7365 ack_nf4_decode, :8017 ack_gemv_nf4) and its device-pointer forms
+        c.ack_nf4_decode.restype = ctypes.c_int32
+        c.ack_nf4_decode.argtypes = [vp] * 9 + [u32] * 6 + [dp]
+        c.ack_gemv_nf4.restype = ctypes.c_int32
+        c.ack_gemv_nf4.argtypes = [vp] * 10 + [u32] * 9 + [dp]
+        c.ack_nf4_decode_launch.restype = ctypes.c_int32
+        c.ack_nf4_decode_launch.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)] + [u32] * 6 + [vp]
+        c.ack_gemv_nf4_launch.restype = ctypes.c_int32
+        c.ack_gemv_nf4_launch.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)] + [u32] * 9 + [vp]
 
     def last_error(self) -> str:
         buf = ctypes.create_string_buffer(1024)

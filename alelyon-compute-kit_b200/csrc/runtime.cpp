@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -858,6 +859,294 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   e = sync_stream(*dev);
   if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
   *status_out = host_status;
+  return ACK_OK;
+}
+
+// ------------------------------------------------------ the NF4 comparator --
+//
+// nf4-decode/v1 and nf4-gemv/v1 (ffi.rs:7365 ack_nf4_decode, :8017
+// ack_gemv_nf4; planners nf4_ops.rs:158-204 and :515-569): the same
+// arguments, refusal names and return codes; the work is enqueued on the
+// device's stream (ack_download waits for it), and `ms_out`, when given,
+// reads NaN (no per-call duration is measured), as the reference reports a
+// recorded dispatch.
+
+namespace {
+
+constexpr uint32_t kNf4Block = 64, kNf4NestedValues = 64 * 256, kNf4TableEntries = 16 + 256;
+
+struct Nf4Operand {
+  void* ptr;
+  uint64_t bytes;
+  uint64_t id;
+};
+
+uint64_t nf4_covered(uint64_t packed_bytes, uint64_t absmax_q_bytes, uint64_t absmax2_bytes) {
+  return std::min({8 * (packed_bytes / 4), 4 * (absmax_q_bytes / 4) * kNf4Block,
+                   (absmax2_bytes / 4) * kNf4NestedValues});
+}
+
+void no_duration(double* ms_out) {
+  if (ms_out) *ms_out = std::nan("");
+}
+
+// Admission of one decode (nf4_ops.rs:158-204 and ffi.rs:7435-7490); on
+// success fills `src` and returns ACK_OK.
+int32_t nf4_decode_admit(const Nf4Operand* op, uint32_t n, uint32_t members, uint32_t selected,
+                         uint32_t member_values, uint32_t src_base, uint32_t storage, ack::Nf4Source* src) {
+  // op: packed, absmax_q, absmax2, tables, starts, offsets, ids, out
+  const uint64_t covered = nf4_covered(op[0].bytes, op[1].bytes, op[2].bytes);
+  const char* refused = nullptr;
+  int32_t code = ACK_ERR_SHAPE;
+  const uint32_t mv = selected == 0 ? 0 : member_values;
+  if (n == 0) {
+    refused = "nf4-zero-values";
+  } else if (uint64_t(n) > (uint64_t(1) << 31)) {
+    refused = "nf4-value-limit-exceeded";
+    code = ACK_ERR_SIZE;
+  } else if (members == 0) {
+    refused = "nf4-members-out-of-range";
+  } else if (selected != 0 && (mv == 0 || mv % kNf4Block != 0 || uint64_t(selected) * mv != n)) {
+    refused = "nf4-selection-out-of-range";
+  } else if (src_base % kNf4NestedValues != 0 || uint64_t(src_base) >= covered) {
+    refused = "nf4-base-out-of-range";
+  } else if (selected == 0 && n > std::min<uint64_t>(covered - src_base, 0xffffffffull)) {
+    refused = "nf4-source-too-small";
+    code = ACK_ERR_SIZE;
+  }
+  if (refused) {
+    set_error(format("nf4-decode: %u values, %u member(s), %u selected, base %u, %llu covered: plan refused: %s", n,
+                     members, selected, src_base, (unsigned long long)covered, refused));
+    return code;
+  }
+  const uint64_t out_bytes = uint64_t(n) * (storage == 0 ? 4 : 2);
+  struct Role {
+    int slot;
+    uint64_t needed;
+    const char* name;
+  } roles[] = {{3, 4ull * kNf4TableEntries, "tables"}, {4, 8ull * members, "starts"}, {5, 4ull * members, "offsets"},
+               {6, 8ull * selected, "ids"}, {7, out_bytes, "output"}};
+  for (const Role& r : roles) {
+    if (r.slot == 6 && selected == 0) continue;
+    if (op[r.slot].bytes < r.needed) {
+      set_error(format("nf4-decode: %s of %llu bytes for %llu: plan refused: nf4-%s-too-small", r.name,
+                       (unsigned long long)op[r.slot].bytes, (unsigned long long)r.needed, r.name));
+      return ACK_ERR_SIZE;
+    }
+  }
+  for (int i = 0; i < 7; ++i) {
+    if (i == 6 && selected == 0) continue;
+    if (op[i].id == op[7].id) {
+      set_error("nf4-decode: plan refused: nf4-output-aliases-input");
+      return ACK_ERR_SHAPE;
+    }
+  }
+  *src = ack::Nf4Source{static_cast<const uint32_t*>(op[0].ptr), static_cast<const uint32_t*>(op[1].ptr),
+                        static_cast<const float*>(op[2].ptr), static_cast<const float*>(op[3].ptr),
+                        static_cast<const uint32_t*>(op[4].ptr), static_cast<const float*>(op[5].ptr), members,
+                        src_base, uint32_t(std::min<uint64_t>(covered - src_base, 0xffffffffull))};
+  return ACK_OK;
+}
+
+// Admission of one grouped GEMV (nf4_ops.rs:515-569 and ffi.rs:8080-8145).
+int32_t nf4_gemv_admit(const Nf4Operand* op, uint32_t rows, uint32_t max_rows, uint32_t n, uint32_t k,
+                       uint32_t lda, uint32_t groups, uint32_t members, uint32_t src_base, ack::Nf4Gemv* g) {
+  // op: a, packed, absmax_q, absmax2, tables, starts, offsets, groups_table, c
+  const uint64_t covered = nf4_covered(op[1].bytes, op[2].bytes, op[3].bytes);
+  const char* refused = nullptr;
+  int32_t code = ACK_ERR_SHAPE;
+  const uint32_t pitch = lda == 0 ? k : lda;
+  const uint64_t weight = uint64_t(n) * k, limit = 0xffffffffull;
+  if (rows == 0 || max_rows == 0 || n == 0 || k == 0) {
+    refused = "nf4-matmul-zero-extent";
+  } else if (groups == 0 || groups > 65535u) {
+    refused = "nf4-matmul-groups-out-of-range";
+  } else if (max_rows > rows) {
+    refused = "nf4-matmul-rows-out-of-range";
+  } else if (max_rows > 16u) {
+    refused = "nf4-gemv-rows-above-16";
+  } else if (k % 8u) {
+    refused = "nf4-matmul-row-not-whole-words";
+  } else if (pitch < k) {
+    refused = "nf4-matmul-pitch-below-width";
+  } else if (pitch % 8u) {
+    refused = "nf4-gemv-pitch-not-whole-words";
+  } else if (members == 0) {
+    refused = "nf4-members-out-of-range";
+  } else if (src_base % kNf4NestedValues != 0 || uint64_t(src_base) >= covered) {
+    refused = "nf4-base-out-of-range";
+  } else if (weight > covered - src_base) {
+    refused = "nf4-source-too-small";
+    code = ACK_ERR_SIZE;
+  } else if (uint64_t(rows - 1) * pitch + k > limit || uint64_t(rows) * n > limit || weight > limit) {
+    refused = "nf4-matmul-address-limit-exceeded";
+    code = ACK_ERR_SIZE;
+  }
+  if (refused) {
+    set_error(format("nf4-gemv: %u group(s), %u rows (largest %u) x %u x %u, base %u, %llu covered: plan refused: %s",
+                     groups, rows, max_rows, n, k, src_base, (unsigned long long)covered, refused));
+    return code;
+  }
+  const uint64_t a_elements = uint64_t(rows - 1) * pitch + k;
+  struct Role {
+    int slot;
+    uint64_t needed;
+    const char* name;
+  } roles[] = {{0, 2 * a_elements, "a"}, {4, 4ull * kNf4TableEntries, "tables"}, {5, 8ull * members, "starts"},
+               {6, 4ull * members, "offsets"}, {7, 12ull * groups, "groups"}, {8, 4ull * rows * n, "output"}};
+  for (const Role& r : roles)
+    if (op[r.slot].bytes < r.needed) {
+      set_error(format("nf4-gemv: %s of %llu bytes for %llu: plan refused: nf4-matmul-%s-too-small", r.name,
+                       (unsigned long long)op[r.slot].bytes, (unsigned long long)r.needed, r.name));
+      return ACK_ERR_SIZE;
+    }
+  for (int i = 0; i < 8; ++i)
+    if (op[i].id == op[8].id) {
+      set_error("nf4-gemv: plan refused: nf4-matmul-output-aliases-input");
+      return ACK_ERR_SHAPE;
+    }
+  const uint32_t src_limit = uint32_t(std::min<uint64_t>(covered - src_base, limit - src_base));
+  *g = ack::Nf4Gemv{static_cast<const uint4*>(op[0].ptr), static_cast<float*>(op[8].ptr),
+                    static_cast<const uint32_t*>(op[7].ptr), n, k, pitch, rows, groups,
+                    ack::Nf4Source{static_cast<const uint32_t*>(op[1].ptr), static_cast<const uint32_t*>(op[2].ptr),
+                                   static_cast<const float*>(op[3].ptr), static_cast<const float*>(op[4].ptr),
+                                   static_cast<const uint32_t*>(op[5].ptr), static_cast<const float*>(op[6].ptr),
+                                   members, src_base, src_limit}};
+  return ACK_OK;
+}
+
+// The handle entries' common part: resolve `count` handles (null allowed
+// where `optional` says so) against the locked device.
+int32_t nf4_resolve(Device& d, const AckBuffer* const* handles, int count, uint64_t optional_mask,
+                    Nf4Operand* out) {
+  for (int i = 0; i < count; ++i) {
+    if (!handles[i] && ((optional_mask >> i) & 1u)) {
+      out[i] = Nf4Operand{nullptr, 0, ~uint64_t(0) - uint64_t(i)};
+      continue;
+    }
+    BufferRec* b = nullptr;
+    const int32_t rc = buffer_of(d, handles[i], &b);
+    if (rc) return rc;
+    out[i] = Nf4Operand{b->ptr, b->bytes, b->id};
+  }
+  return ACK_OK;
+}
+
+}  // namespace
+
+ACK_EXPORT int32_t ack_nf4_decode(const AckDevice* handle, const AckBuffer* packed, const AckBuffer* absmax_q,
+                                  const AckBuffer* absmax2, const AckBuffer* tables, const AckBuffer* starts,
+                                  const AckBuffer* offsets, const AckBuffer* ids, const AckBuffer* out, uint32_t n,
+                                  uint32_t members, uint32_t selected, uint32_t member_values, uint32_t src_base,
+                                  uint32_t storage, double* ms_out) {
+  no_duration(ms_out);
+  if (storage > 2) {
+    set_error("nf4-decode: plan refused: nf4-storage-out-of-range");
+    return ACK_ERR_SHAPE;
+  }
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  if ((rc = refuse_poisoned(*dev, "nf4-decode"))) return rc;
+  const AckBuffer* hs[8] = {packed, absmax_q, absmax2, tables, starts, offsets, ids, out};
+  Nf4Operand op[8];
+  // the whole-source decode reads no ids
+  if ((rc = nf4_resolve(*dev, hs, 8, selected == 0 ? (1u << 6) : 0u, op))) return rc;
+  ack::Nf4Source src;
+  if ((rc = nf4_decode_admit(op, n, members, selected, member_values, src_base, storage, &src))) return rc;
+  DeviceScope scope(dev->ordinal);
+  const cudaError_t e = ack::nf4_decode(src, static_cast<const uint32_t*>(op[6].ptr), op[7].ptr, n, selected,
+                                        member_values, storage, dev->stream);
+  return e == cudaSuccess ? ACK_OK : cuda_fail(*dev, e, "nf4-decode");
+}
+
+ACK_EXPORT int32_t ack_gemv_nf4(const AckDevice* handle, const AckBuffer* a, const AckBuffer* packed,
+                                const AckBuffer* absmax_q, const AckBuffer* absmax2, const AckBuffer* tables,
+                                const AckBuffer* starts, const AckBuffer* offsets, const AckBuffer* groups_table,
+                                const AckBuffer* c, uint32_t rows, uint32_t max_rows, uint32_t n, uint32_t k,
+                                uint32_t lda, uint32_t groups, uint32_t members, uint32_t src_base, uint32_t elem,
+                                double* ms_out) {
+  no_duration(ms_out);
+  if (elem > 1) {
+    set_error("nf4-gemv: plan refused: nf4-matmul-elem-out-of-range");
+    return ACK_ERR_SHAPE;
+  }
+  std::shared_ptr<Device> dev;
+  int32_t rc = lookup(handle, &dev);
+  if (rc) return rc;
+  std::unique_lock<std::mutex> lk;
+  rc = acquire(*dev, &lk);
+  if (rc) return rc;
+  if ((rc = refuse_poisoned(*dev, "nf4-gemv"))) return rc;
+  const AckBuffer* hs[9] = {a, packed, absmax_q, absmax2, tables, starts, offsets, groups_table, c};
+  Nf4Operand op[9];
+  if ((rc = nf4_resolve(*dev, hs, 9, 0, op))) return rc;
+  ack::Nf4Gemv g;
+  if ((rc = nf4_gemv_admit(op, rows, max_rows, n, k, lda, groups, members, src_base, &g))) return rc;
+  DeviceScope scope(dev->ordinal);
+  const cudaError_t e = ack::nf4_gemv(g, max_rows, elem, dev->stream);
+  return e == cudaSuccess ? ACK_OK : cuda_fail(*dev, e, "nf4-gemv");
+}
+
+// Device-pointer forms (no counterpart in the reference) for callers whose
+// data is in device memory already (PyTorch tensors): the same admission;
+// `ptrs` / `bytes` in the handle entries' argument order, work enqueued on
+// `stream` on the current device. Operands are told apart by address.
+ACK_EXPORT int32_t ack_nf4_decode_launch(void* const* ptrs, const uint64_t* bytes, uint32_t n, uint32_t members,
+                                         uint32_t selected, uint32_t member_values, uint32_t src_base,
+                                         uint32_t storage, void* stream) {
+  if (!ptrs || !bytes) return ACK_ERR_NULL;
+  if (storage > 2) {
+    set_error("nf4-decode: plan refused: nf4-storage-out-of-range");
+    return ACK_ERR_SHAPE;
+  }
+  Nf4Operand op[8];
+  for (int i = 0; i < 8; ++i) {
+    if (!ptrs[i] && !(i == 6 && selected == 0)) {
+      set_error(format("nf4-decode: operand %d is null", i));
+      return ACK_ERR_NULL;
+    }
+    op[i] = Nf4Operand{ptrs[i], bytes[i], ptrs[i] ? uint64_t(reinterpret_cast<uintptr_t>(ptrs[i])) : ~uint64_t(0)};
+  }
+  ack::Nf4Source src;
+  const int32_t rc = nf4_decode_admit(op, n, members, selected, member_values, src_base, storage, &src);
+  if (rc) return rc;
+  const cudaError_t e = ack::nf4_decode(src, static_cast<const uint32_t*>(op[6].ptr), op[7].ptr, n, selected,
+                                        member_values, storage, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error(format("nf4-decode: %s", cudaGetErrorString(e)));
+    return ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_gemv_nf4_launch(void* const* ptrs, const uint64_t* bytes, uint32_t rows, uint32_t max_rows,
+                                       uint32_t n, uint32_t k, uint32_t lda, uint32_t groups, uint32_t members,
+                                       uint32_t src_base, uint32_t elem, void* stream) {
+  if (!ptrs || !bytes) return ACK_ERR_NULL;
+  if (elem > 1) {
+    set_error("nf4-gemv: plan refused: nf4-matmul-elem-out-of-range");
+    return ACK_ERR_SHAPE;
+  }
+  Nf4Operand op[9];
+  for (int i = 0; i < 9; ++i) {
+    if (!ptrs[i]) {
+      set_error(format("nf4-gemv: operand %d is null", i));
+      return ACK_ERR_NULL;
+    }
+    op[i] = Nf4Operand{ptrs[i], bytes[i], uint64_t(reinterpret_cast<uintptr_t>(ptrs[i]))};
+  }
+  ack::Nf4Gemv g;
+  const int32_t rc = nf4_gemv_admit(op, rows, max_rows, n, k, lda, groups, members, src_base, &g);
+  if (rc) return rc;
+  const cudaError_t e = ack::nf4_gemv(g, max_rows, elem, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error(format("nf4-gemv: %s", cudaGetErrorString(e)));
+    return ACK_ERR_VULKAN;
+  }
   return ACK_OK;
 }
 

@@ -26,4 +26,29 @@ cudaError_t encode_noalloc(const float* x, uint64_t n, uint32_t batch, const flo
 // 2: its consumers take no accumulator). Defined in vq_codec.cu.
 void set_encode_stall_test(uint32_t mode);
 
+// ---- NF4 comparator (vq_nf4.cu): nf4-decode/v1 and nf4-gemv/v1 ----
+// The stored source: packed indices (two a byte, the first value in the high
+// nibble), one absmax index byte a block of 64 values, one FP32 absmax2 a
+// nested block of 256 blocks, the 16 code values then the 256 map values,
+// int64 member starts (read as their low words) and one FP32 offset a member.
+struct Nf4Source {
+  const uint32_t* packed;
+  const uint32_t* absmax_q;
+  const float* absmax2;
+  const float* tables;
+  const uint32_t* starts;
+  const float* offsets;
+  uint32_t members, src_base, src_limit;
+};
+struct Nf4Gemv {
+  const uint4* A;          // rows x lda 16-bit words, read 8 at a time
+  float* C;                // rows x n
+  const uint32_t* table;   // groups x (first row, rows, weight base)
+  uint32_t n, k, lda, rows, groups;
+  Nf4Source src;
+};
+cudaError_t nf4_decode(const Nf4Source& src, const uint32_t* ids, void* out, uint32_t n, uint32_t selected,
+                       uint32_t member_values, uint32_t storage, cudaStream_t stream);
+cudaError_t nf4_gemv(const Nf4Gemv& g, uint32_t max_rows, uint32_t elem, cudaStream_t stream);
+
 }  // namespace ack

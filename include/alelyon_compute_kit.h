@@ -314,6 +314,41 @@ int32_t ack_vq_plan_validate_buffers(const uint8_t *plan, size_t plan_len,
                                      const uint64_t *capacities, const uint64_t *ids, size_t n);
 int32_t ack_vq_plan_validate_dispatch(const uint8_t *plan, size_t plan_len, const uint32_t limits[3]);
 
+/* ---- the NF4 comparator (the adjacent 4-bit format of the same kit, for
+ * comparison with vq4) ----
+ * nf4-decode/v1 and nf4-gemv/v1 with the reference's names, arguments,
+ * refusal names and codes (ffi.rs:7365 ack_nf4_decode, :8017 ack_gemv_nf4;
+ * planners nf4_ops.rs:158-204, :515-569; the law in kernels/nf4_decode.comp
+ * and nf4_gemv.comp). Buffers: packed (two indices a byte, high nibble
+ * first), absmax_q (a byte a block of 64 values), absmax2 (f32 a nested
+ * block of 256 blocks), tables (the 16 code values then the 256 map values,
+ * f32), starts (int64 a member), offsets (f32 a member), ids (int64 a
+ * selected member; unread and may be null when `selected` is 0), out.
+ * storage: 0 f32, 1 bf16, 2 fp16; elem: 0 bf16, 1 fp16. The work is enqueued
+ * on the device's stream; `ms_out`, when given, reads NaN. */
+int32_t ack_nf4_decode(const AckDevice *dev, const AckBuffer *packed, const AckBuffer *absmax_q,
+                       const AckBuffer *absmax2, const AckBuffer *tables, const AckBuffer *starts,
+                       const AckBuffer *offsets, const AckBuffer *ids, const AckBuffer *out, uint32_t n,
+                       uint32_t members, uint32_t selected, uint32_t member_values, uint32_t src_base,
+                       uint32_t storage, double *ms_out);
+/* C[first + m, :] = A[first + m, :] . W^T for each group (first row, rows,
+ * weight base: three u32 words) of `groups_table`; A is `rows` x `lda`
+ * 16-bit words (lda 0: K), C `rows` x `n` f32. */
+int32_t ack_gemv_nf4(const AckDevice *dev, const AckBuffer *a, const AckBuffer *packed, const AckBuffer *absmax_q,
+                     const AckBuffer *absmax2, const AckBuffer *tables, const AckBuffer *starts,
+                     const AckBuffer *offsets, const AckBuffer *groups_table, const AckBuffer *c, uint32_t rows,
+                     uint32_t max_rows, uint32_t n, uint32_t k, uint32_t lda, uint32_t groups, uint32_t members,
+                     uint32_t src_base, uint32_t elem, double *ms_out);
+/* Device-pointer forms (no counterpart in the reference): the operands of
+ * the entries above in the same order as CUDA device pointers with their
+ * byte sizes, enqueued on the cudaStream_t `stream` of the current device. */
+int32_t ack_nf4_decode_launch(void *const *ptrs, const uint64_t *bytes, uint32_t n, uint32_t members,
+                              uint32_t selected, uint32_t member_values, uint32_t src_base, uint32_t storage,
+                              void *stream);
+int32_t ack_gemv_nf4_launch(void *const *ptrs, const uint64_t *bytes, uint32_t rows, uint32_t max_rows, uint32_t n,
+                            uint32_t k, uint32_t lda, uint32_t groups, uint32_t members, uint32_t src_base,
+                            uint32_t elem, void *stream);
+
 /* ---- test-only host fault injection (the reference's `ack_inject_fault`,
  * ffi.rs:3449, behind its `fault-injection` feature). Refused unless the
  * process environment has ACK_FAULT_INJECTION=1. kind 0: the next stream
