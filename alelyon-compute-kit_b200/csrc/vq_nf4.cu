@@ -196,24 +196,55 @@ __global__ void __launch_bounds__(256) k_nf4_gemv(Nf4Gemv g) {
       const uint32_t first = member_of(g.src.starts, g.src.members, col_base);
       const bool one = first == member_of(g.src.starts, g.src.members, col_base + g.k - 1u);
       const float col_off = __ldg(g.src.offsets + first);
-      uint32_t key = 0xFFFFFFFFu;  // the bits of the absmax wtab holds (none yet: a NaN pattern)
+      uint32_t key = 0xFFFFFFFFu;  // the bits of the absmax wtab holds (none yet)
       bool have = false;
+      uint32_t cur_blk = 0xFFFFFFFFu;
+      float absmax = 0.f;
       for (uint32_t base = 0; base < words; base += 64u) {
+        // this thread's run of P consecutive words: one coalesced vector load
+        // when it is whole and 16-byte aligned
+        const uint32_t j0 = base + uint32_t(P) * q;
+        const uint32_t s0 = g.src.src_base + col_base + 8u * j0;
+        const uint32_t* wp = g.src.packed + (s0 >> 3);
+        uint32_t pw[P];
+        if constexpr (P >= 4) {
+          if (j0 + P <= words && (reinterpret_cast<uintptr_t>(wp) & 15u) == 0) {
+#pragma unroll
+            for (int v = 0; v < P / 4; ++v) {
+              const uint4 u = __ldg(reinterpret_cast<const uint4*>(wp) + v);
+              pw[4 * v] = u.x;
+              pw[4 * v + 1] = u.y;
+              pw[4 * v + 2] = u.z;
+              pw[4 * v + 3] = u.w;
+            }
+          } else {
+#pragma unroll
+            for (int r = 0; r < P; ++r) pw[r] = j0 + uint32_t(r) < words ? __ldg(wp + r) : 0u;
+          }
+        } else {
+          pw[0] = j0 < words ? __ldg(wp) : 0u;
+        }
 #pragma unroll
         for (int r = 0; r < P; ++r) {
-          const uint32_t j = base + uint32_t(P) * q + uint32_t(r);
+          const uint32_t j = j0 + uint32_t(r);
           if (j < words) {
-            const uint32_t v0 = col_base + 8u * j;
-            const uint32_t s = g.src.src_base + v0;
-            const uint32_t word = __ldg(g.src.packed + (s >> 3));
-            const float absmax = block_absmax(
-                g.src, map_s, s, one ? col_off : __ldg(g.src.offsets + member_of(g.src.starts, g.src.members, v0)));
-            if (!have || __float_as_uint(absmax) != key) {
+            const uint32_t s = s0 + 8u * uint32_t(r);
+            // the absmax only changes with its 64-value block (or, in a column
+            // that straddles members, with the member)
+            if (!one || (s >> 6) != cur_blk) {
+              absmax = block_absmax(g.src, map_s, s,
+                                    one ? col_off
+                                        : __ldg(g.src.offsets + member_of(g.src.starts, g.src.members,
+                                                                          col_base + 8u * j)));
+              cur_blk = s >> 6;
+              if (!have || __float_as_uint(absmax) != key) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) wtab[e][tid] = widen16<E>(to16<E>(__fmul_rn(code_s[e], absmax)));
-              key = __float_as_uint(absmax);
-              have = true;
+                for (int e = 0; e < 16; ++e) wtab[e][tid] = widen16<E>(to16<E>(__fmul_rn(code_s[e], absmax)));
+                key = __float_as_uint(absmax);
+                have = true;
+              }
             }
+            const uint32_t word = pw[r];
             float w[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {

@@ -431,6 +431,62 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
     return out
 
 
+def run_nf4(args, world, rank, local) -> dict:
+    """The NF4 comparator on the headline's shape: 768 experts of an
+    11008 x 4096 weight in bitsandbytes' NF4 stored form (random indices and
+    absmax bytes, absmax2 in [0.004, 0.2]), one bf16 row of activations each,
+    through nf4-gemv/v1 (bit for bit the reference's law). The law indexes
+    values in 32 bits, so a step is 12 calls of 64 experts. `value` is NF4
+    weight bytes (indices + absmax bytes + absmax2) per second, the same
+    quantity as the headline's coded-weight bytes."""
+    import torch
+
+    from alelyon_compute_kit import nf4
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    experts, chunk = args.experts, 64
+    per = N_ROWS * K_COLS
+    calls = (experts + chunk - 1) // chunk
+    experts = calls * chunk
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    packed = torch.randint(0, 256, (experts * per // 2,), generator=gen, dtype=torch.uint8, device=device)
+    absq = torch.randint(0, 256, (experts * per // 64,), generator=gen, dtype=torch.uint8, device=device)
+    absmax2 = 0.004 + torch.randint(0, 997, (experts * per // 16384,), generator=gen, device=device).float() * 2e-4
+    from statistics import NormalDist
+    nd = NormalDist()
+    code = sorted([nd.inv_cdf(q) for q in np.linspace(0.03, 0.97, 15)] + [0.0])
+    code = np.array(code) / max(abs(c) for c in code)
+    tables = torch.from_numpy(np.concatenate([code, (np.arange(256) - 127.5) / 128.0]).astype(np.float32)).to(device)
+    starts = torch.arange(chunk, dtype=torch.int64, device=device) * per
+    offsets = torch.zeros(chunk, dtype=torch.float32, device=device)
+    a16 = (torch.randn((experts, K_COLS), generator=gen, device=device)).to(torch.bfloat16).view(torch.int16)
+    table = torch.from_numpy(np.array([[i, 1, i * per] for i in range(chunk)], np.uint32).view(np.int32)).to(device)
+    out = torch.empty((calls, chunk, N_ROWS), dtype=torch.float32, device=device)
+    wb_per = per // 2 + per // 64 + 4 * (per // 16384)
+
+    def step():
+        for c in range(calls):
+            e0 = c * chunk
+            nf4.gemv(a16[e0: e0 + chunk], packed[e0 * per // 2: (e0 + chunk) * per // 2],
+                     absq[e0 * per // 64: (e0 + chunk) * per // 64],
+                     absmax2[e0 * per // 16384: (e0 + chunk) * per // 16384], tables, starts, offsets, table,
+                     rows=chunk, n=N_ROWS, k=K_COLS, elem="bf16", max_rows=1, out=out[c])
+
+    ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local, label="nf4")
+    weight = experts * wb_per
+    algorithmic = weight + experts * (2 * K_COLS + 4 * N_ROWS)
+    del packed, absq, absmax2, a16, out
+    return {"metric": "NF4 comparator GEMV weight GB/s (cfg2 shape, 11008x4096, M=1, 768 experts, bf16 A)",
+            "value": round(world * weight / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "config": {"workload": "nf4-gemv-cfg2-shape", "experts": experts, "calls_per_step": calls,
+                       "weight_bytes_per_expert": wb_per},
+            "roofline": roofline("hbm", algorithmic / (ms / 1e3) / 1e9, "k_nf4_gemv", algorithmic, None,
+                                 note="the law's per-value rounding of the weight to 16 bits makes it "
+                                      "instruction-bound before HBM"),
+            "clocks": clocks}
+
+
 def run_secondary(args, torch, cuda, codes, books, device, world, rank, local) -> dict:
     """Every other workload of the configs, measured in the same run: cfg2
     at M = 4, 16, 64 over the same experts; cfg3; the cfg4 VQAdamW step;
@@ -451,6 +507,8 @@ def run_secondary(args, torch, cuda, codes, books, device, world, rank, local) -
     sec["cfg3"] = compact(run_cfg3(sub, world, rank, local))
     torch.cuda.empty_cache()
     sec["cfg4"] = compact(run_cfg4(sub, world, rank, local))
+    torch.cuda.empty_cache()
+    sec["nf4-gemv"] = compact(run_nf4(sub, world, rank, local))
     torch.cuda.empty_cache()
     for group in (8, 16, 32):
         for dist in ("gauss", "heavy"):
@@ -937,6 +995,8 @@ def main():
         result = run_cfg2(args, world, rank, local)
     elif args.workload in ("encode", "decode"):
         result = run_codec(args, world, rank, local, args.workload)
+    elif args.workload == "nf4":
+        result = run_nf4(args, world, rank, local)
     elif args.workload == "cfg3":
         result = run_cfg3(args, world, rank, local)
     elif args.workload == "cfg4":
