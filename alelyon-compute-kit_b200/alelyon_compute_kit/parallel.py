@@ -14,6 +14,13 @@ ACK_DEVICE). The path shards three ways:
 
 Row results do not depend on how rows are split, so a sharded product is
 bitwise equal to the one-GPU product.
+
+`PeerSlots` replaces the all-gather of the M = 1 dense product by peer
+stores: every rank's byte-pair GEMV writes its Y shard into its slot of
+every rank's rank-major buffer (CUDA IPC mappings over NVLink, no multicast
+object), then a step flag is published to every rank and awaited (bounded).
+The result is the all-gathered buffer, bit for bit, without a separate
+collective after the product.
 """
 from __future__ import annotations
 
@@ -131,3 +138,128 @@ def coded_sharded(a_codes, a_book, b_codes, b_book, m: int, n_total: int, k: int
     if not gather:
         return y, status
     return gather_columns(y, n_total, ranges), status
+
+
+class _CudaBuffer:
+    """A device allocation of the library's, seen by PyTorch without a copy."""
+
+    def __init__(self, ptr: int, shape, device):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.device = device
+
+
+class PeerSlots:
+    """A rank-major (world, E, width) float32 buffer on every rank, each
+    rank's slot written by that rank's product straight into every other
+    rank's buffer, and one u32 step flag per (receiver, sender).
+
+    `dense(x, codes, books, n, group)` runs this rank's op-16 product (M = 1,
+    W stored n x K, the byte-pair kernel's shapes) with peer stores, then
+    publishes the step and waits (bounded; a wait that runs out sets the
+    stalled bit of `status`) until every rank has published it. After the
+    wait, `tensor()` holds every rank's rows. Slots are rewritten by the next
+    call on any rank: read them before the next call, or `torch.distributed`
+    barrier first. `close()` unmaps and frees (call it on every rank)."""
+
+    def __init__(self, experts: int, width: int, group=None, device=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import ack
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 8:
+            raise ack.AckError("peer slots hold at most 8 ranks")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.experts, self.width = experts, width
+        self.slot = experts * width * 4
+        self.flags_off = self.world * self.slot
+        self._lib = ack._lib()
+        c = self._lib.cdll
+        for name, args in (("ack_peer_alloc", [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+                           ("ack_peer_open", [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+                           ("ack_peer_close", [ctypes.c_void_p]), ("ack_peer_free", [ctypes.c_void_p]),
+                           ("ack_vq_dense_peers", [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                                   ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+                           ("ack_peer_signal", [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                                ctypes.c_void_p]),
+                           ("ack_peer_wait", [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                              ctypes.c_uint32, ctypes.c_void_p])):
+            getattr(c, name).argtypes = args
+            getattr(c, name).restype = ctypes.c_int32
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            rc = c.ack_peer_alloc(self.flags_off + 256, ctypes.byref(ptr), handle)
+        if rc != ack.ACK_OK:
+            raise ack._kit_error("peer-alloc", rc, self._lib.last_error())
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.base = [0] * self.world
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for r in range(self.world):
+                if r == self.rank:
+                    self.base[r] = ptr.value
+                    continue
+                peer = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                rc = c.ack_peer_open(h, ctypes.byref(peer))
+                if rc != ack.ACK_OK:
+                    raise ack._kit_error("peer-open", rc, self._lib.last_error())
+                self.base[r] = peer.value
+                self._opened.append(peer.value)
+        others = [self.base[r] + self.rank * self.slot for r in range(self.world) if r != self.rank]
+        self._peers = (ctypes.c_void_p * max(1, len(others)))(*others)
+        self._flags = (ctypes.c_void_p * self.world)(*[b + self.flags_off for b in self.base])
+        self._view = _CudaBuffer(ptr.value, (self.world, experts, width), self.device)
+        self._tensor = torch.as_tensor(self._view, device=self.device)
+        self.epoch = 0
+
+    def tensor(self):
+        """The rank-major (world, E, width) buffer (valid after `dense`)."""
+        return self._tensor
+
+    def dense(self, x, codes, books, n: int, group: int, status):
+        import ctypes
+
+        import torch
+
+        from . import ack, cuda
+        e, m, k = x.shape
+        if m != 1 or n != self.width or e != self.experts:
+            raise ack.AckError("peer slots hold (experts, width) rows of an M = 1 product")
+        out = self._tensor[self.rank].view(e, 1, n)
+        plan = cuda.plan2(cuda.OP_DENSE, 1, n, k, group, flags=2, batch=e)
+        ops = ack.AckVqOperands()
+        ops.size = ctypes.sizeof(ops)
+        ops.nslots = 8
+        for i, t in enumerate((x, codes, books, None, None, out, None, status)):
+            if t is not None:
+                ops.ptr[i] = t.data_ptr()
+                ops.bytes[i] = t.numel() * t.element_size()
+        c = self._lib.cdll
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        self.epoch += 1
+        rc = c.ack_vq_dense_peers(plan, len(plan), ctypes.byref(ops), self._peers, self.world - 1, stream)
+        if rc == ack.ACK_OK:
+            rc = c.ack_peer_signal(self._flags, self.world, self.rank, self.epoch, stream)
+        if rc == ack.ACK_OK:
+            rc = c.ack_peer_wait(ctypes.c_void_p(self.base[self.rank] + self.flags_off), self.world, self.epoch,
+                                 ctypes.c_void_p(status.data_ptr()), 0, stream)
+        if rc != ack.ACK_OK:
+            raise ack._kit_error("vq2-dense-peers", rc, self._lib.last_error())
+        return self._tensor
+
+    def close(self):
+        import torch
+        c = self._lib.cdll
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                c.ack_peer_close(p)
+            self._opened = []
+            if self.base[self.rank]:
+                c.ack_peer_free(self.base[self.rank])
+                self.base[self.rank] = 0

@@ -1150,7 +1150,108 @@ ACK_EXPORT int32_t ack_gemv_nf4_launch(void* const* ptrs, const uint64_t* bytes,
   return ACK_OK;
 }
 
+namespace {
+int32_t launch_ptrs(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops, void* stream,
+                    const ack::PeerY* peers);
+}  // namespace
+
 ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops, void* stream) {
+  return launch_ptrs(plan, plan_len, ops, stream, nullptr);
+}
+
+// ack_vq_launch's op-16 plan (M = 1, W stored N x K, canonical) whose outputs
+// are also written into `npeers` other ranks' output slots (`peers`: device
+// pointers valid here, e.g. CUDA IPC mappings), at Y's offsets.
+ACK_EXPORT int32_t ack_vq_dense_peers(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops,
+                                      float* const* peers, uint32_t npeers, void* stream) {
+  if (npeers > ack::kMaxPeers || (npeers && !peers)) {
+    set_error(format("vq2-dense-peers: %u peer slots (at most %u)", npeers, ack::kMaxPeers));
+    return ACK_ERR_SHAPE;
+  }
+  ack::PeerY py{};
+  for (uint32_t i = 0; i < npeers; ++i) {
+    if (!peers[i]) {
+      set_error(format("vq2-dense-peers: peer slot %u is null", i));
+      return ACK_ERR_NULL;
+    }
+    py.dst[i] = peers[i];
+  }
+  py.n = npeers;
+  return launch_ptrs(plan, plan_len, ops, stream, &py);
+}
+
+// Step flags of the peer-store products: publish this rank's epoch into every
+// rank's flag array, and wait (bounded) for every rank's epoch here.
+ACK_EXPORT int32_t ack_peer_signal(uint32_t* const* flags, uint32_t world, uint32_t rank, uint32_t epoch,
+                                   void* stream) {
+  if (!flags) return ACK_ERR_NULL;
+  const cudaError_t e = ack::peer_signal(flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error(format("peer-signal: %s", cudaGetErrorString(e)));
+    return e == cudaErrorInvalidValue ? ACK_ERR_SHAPE : ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_peer_wait(const uint32_t* flags, uint32_t world, uint32_t epoch, uint32_t* status,
+                                 uint32_t polls, void* stream) {
+  if (!flags || !status) return ACK_ERR_NULL;
+  const cudaError_t e = ack::peer_wait(flags, world, epoch, status, polls ? polls : (1u << 24),
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error(format("peer-wait: %s", cudaGetErrorString(e)));
+    return e == cudaErrorInvalidValue ? ACK_ERR_SHAPE : ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
+// Device memory another process can map (CUDA IPC, no multicast object):
+// allocate zeroed on the current device and write its 64-byte handle.
+ACK_EXPORT int32_t ack_peer_alloc(uint64_t bytes, void** ptr, uint8_t* handle) {
+  if (!ptr || !handle) return ACK_ERR_NULL;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    cudaGetLastError();
+    set_error(format("peer-alloc of %llu bytes: %s", (unsigned long long)bytes, cudaGetErrorString(e)));
+    return ACK_ERR_VULKAN;
+  }
+  static_assert(sizeof(h) == 64, "a CUDA IPC memory handle is 64 bytes");
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_peer_open(const uint8_t* handle, void** ptr) {
+  if (!ptr || !handle) return ACK_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error(format("peer-open: %s", cudaGetErrorString(e)));
+    return ACK_ERR_VULKAN;
+  }
+  return ACK_OK;
+}
+
+ACK_EXPORT int32_t ack_peer_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? ACK_OK : ACK_ERR_VULKAN;
+}
+
+ACK_EXPORT int32_t ack_peer_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? ACK_OK : ACK_ERR_VULKAN;
+}
+
+namespace {
+int32_t launch_ptrs(const uint8_t* plan, size_t plan_len, const AckVqOperands* ops, void* stream,
+                    const ack::PeerY* peers) {
   if (!plan || !ops) {
     set_error(!plan ? "vq: null plan" : "vq: null operands");
     return ACK_ERR_NULL;
@@ -1200,13 +1301,20 @@ ACK_EXPORT int32_t ack_vq_launch(const uint8_t* plan, size_t plan_len, const Ack
       }
     }
   }
-  cudaError_t ce = ack::launch(p, ptr, static_cast<cudaStream_t>(stream));
+  cudaError_t ce = peers ? ack::dense_peers(p, ptr, *peers, static_cast<cudaStream_t>(stream))
+                        : ack::launch(p, ptr, static_cast<cudaStream_t>(stream));
+  if (ce == cudaErrorNotSupported && peers) {
+    set_error(format("%s: the peer-store product takes op 16 with M = 1, W stored N x K, canonical codes, "
+                     "K a multiple of 256 g and enough rows for the byte-pair kernel", entry));
+    return ACK_ERR_UNSUPPORTED_OP;
+  }
   if (ce != cudaSuccess) {
     set_error(format("%s: launch: %s (%s)", entry, cudaGetErrorName(ce), cudaGetErrorString(ce)));
     return ACK_ERR_VULKAN;
   }
   return ACK_OK;
 }
+}  // namespace
 
 // ---------------------------------------------- encode without allocation --
 // For callers that may not allocate device memory themselves or through this

@@ -51,4 +51,24 @@ cudaError_t nf4_decode(const Nf4Source& src, const uint32_t* ids, void* out, uin
                        uint32_t member_values, uint32_t storage, cudaStream_t stream);
 cudaError_t nf4_gemv(const Nf4Gemv& g, uint32_t max_rows, uint32_t elem, cudaStream_t stream);
 
+// ---- Y shards written straight into peers' memory (vq_products.cu, vq_peer.cu) ----
+// Up to 7 other ranks' output slots (CUDA IPC mappings over NVLink); the
+// product writes each output to its own Y and to every peer slot at the same
+// offset, then fences at system scope before its blocks exit.
+constexpr uint32_t kMaxPeers = 7;
+struct PeerY {
+  float* dst[kMaxPeers];
+  uint32_t n;
+};
+// The byte-pair GEMV (op 16, M = 1, W stored N x K, canonical) with peer
+// stores; cudaErrorNotSupported for a plan the byte-pair kernel does not take.
+cudaError_t dense_peers(const Plan& p, void* const* ptr, const PeerY& peers, cudaStream_t stream);
+// Publish `epoch` into slot `rank` of every rank's flag array (release, system
+// scope), after the stream's earlier work.
+cudaError_t peer_signal(uint32_t* const* flags, uint32_t world, uint32_t rank, uint32_t epoch, cudaStream_t stream);
+// Wait (bounded: `polls` polls a flag) until every rank's flag here has
+// reached `epoch`; a wait that runs out sets the stalled status bit.
+cudaError_t peer_wait(const uint32_t* flags, uint32_t world, uint32_t epoch, uint32_t* status, uint32_t polls,
+                      cudaStream_t stream);
+
 }  // namespace ack

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "vq_common.cuh"
+#include "vq_kernels.hpp"
 
 namespace ack {
 namespace {
@@ -436,7 +437,7 @@ template <int G, bool ONE>  // ONE: K = 256 G, one chunk (32-word rows, a compil
 __global__ void __launch_bounds__(pair::kThreads, 1)
     k_dense_pair(const float* __restrict__ X, const uint32_t* __restrict__ codes, const float* __restrict__ books,
                  float* __restrict__ Y, uint32_t N, uint32_t K, uint32_t E, uint64_t words_per_expert,
-                 uint32_t* __restrict__ status) {
+                 uint32_t* __restrict__ status, const __grid_constant__ PeerY peers) {
   constexpr uint32_t kChunkX = 256u * G, kBook = 16u * G;
   extern __shared__ __align__(16) float pair_smem[];
   float* Q = pair_smem;
@@ -601,6 +602,8 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         const float nv = c == 0 ? v[0] : *y + v[0];
         *y = nv;
         ybits |= finite32(nv) ? 0u : kNonfinite;  // a nonfinite partial sum stays nonfinite
+        if (c + 1 == chunks)  // the finished value, into every peer's slot too (NVLink stores)
+          for (uint32_t i = 0; i < peers.n; ++i) peers.dst[i][uint64_t(e) * N + n0 + lane] = nv;
       }
     }
     // advance: the next chunk of this segment, or the next segment
@@ -610,6 +613,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     }
   }
   flag_warp(status, ybits);
+  if (peers.n) __threadfence_system();  // the peer stores are visible before the block exits
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
@@ -881,7 +885,8 @@ bool dense_pair_fits(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, const f
 
 template <int G>
 cudaError_t launch_dense_pair(const float* X, const uint32_t* codes, const float* books, float* Y, uint32_t N,
-                              uint32_t K, uint32_t batch, uint64_t words, uint32_t* status, cudaStream_t s) {
+                              uint32_t K, uint32_t batch, uint64_t words, uint32_t* status, cudaStream_t s,
+                              const PeerY& peers = PeerY{{}, 0}) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
@@ -896,10 +901,10 @@ cudaError_t launch_dense_pair(const float* X, const uint32_t* codes, const float
   const uint32_t grid = uint32_t(std::min<uint64_t>(units, uint64_t(sm_count())));
   if (K == 256u * G)
     k_dense_pair<G, true><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words,
-                                                                               status);
+                                                                               status, peers);
   else
     k_dense_pair<G, false><<<grid, pair::kThreads, pair::smem_bytes<G>(), s>>>(X, codes, books, Y, N, K, batch, words,
-                                                                                status);
+                                                                                status, peers);
   return cudaGetLastError();
 }
 
@@ -934,6 +939,20 @@ struct RunDense {
     dim3 grid((N + 63) / 64, (M + 63) / 64, p.batch);
     k_gemm_generic<G><<<grid, kThreads, 0, s>>>(A, B, Y, M, N, K, uint64_t(M) * K, words, status);
     return cudaGetLastError();
+  }
+};
+
+template <int G>
+struct RunDensePeers {
+  static cudaError_t run(const Plan& p, void* const* ptr, const PeerY& peers, cudaStream_t s) {
+    const float* X = static_cast<const float*>(ptr[0]);
+    const uint32_t* codes = static_cast<const uint32_t*>(ptr[1]);
+    const float* books = static_cast<const float*>(ptr[2]);
+    const uint32_t M = uint32_t(p.m), N = uint32_t(p.n), K = uint32_t(p.k);
+    if ((p.flags & ~2u) != 0 || !(p.flags & 2u) || !dense_pair_fits<G>(M, N, K, p.batch, X, books))
+      return cudaErrorNotSupported;
+    return launch_dense_pair<G>(X, codes, books, static_cast<float*>(ptr[5]), N, K, p.batch,
+                                packed_words(uint64_t(N) * K, G), static_cast<uint32_t*>(ptr[7]), s, peers);
   }
 };
 
@@ -986,4 +1005,16 @@ cudaError_t launch_repack(const Plan& p, void* const* ptr, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+}  // namespace ack
+
+namespace ack {
+cudaError_t dense_peers(const Plan& p, void* const* ptr, const PeerY& peers, cudaStream_t s) {
+  if (p.op != Op::Dense || peers.n > kMaxPeers) return cudaErrorNotSupported;
+  switch (p.group) {
+    case 8: return RunDensePeers<8>::run(p, ptr, peers, s);
+    case 16: return RunDensePeers<16>::run(p, ptr, peers, s);
+    case 32: return RunDensePeers<32>::run(p, ptr, peers, s);
+    default: return cudaErrorNotSupported;
+  }
+}
 }  // namespace ack

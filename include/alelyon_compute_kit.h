@@ -349,6 +349,29 @@ int32_t ack_gemv_nf4_launch(void *const *ptrs, const uint64_t *bytes, uint32_t r
                             uint32_t k, uint32_t lda, uint32_t groups, uint32_t members, uint32_t src_base,
                             uint32_t elem, void *stream);
 
+/* ---- peer stores between ranks (no counterpart in the reference: its kit
+ * has no multi-GPU layer). One process per GPU; each rank allocates a buffer
+ * others map through CUDA IPC (no multicast object), exchanges the 64-byte
+ * handles (e.g. over torch.distributed) and opens the others'. ---- */
+int32_t ack_peer_alloc(uint64_t bytes, void **ptr, uint8_t *handle64);   /* zeroed, current device */
+int32_t ack_peer_open(const uint8_t *handle64, void **ptr);
+int32_t ack_peer_close(void *ptr);
+int32_t ack_peer_free(void *ptr);
+/* ack_vq_launch's op-16 plan (M = 1, W stored N x K, canonical codes, the
+ * byte-pair kernel's shapes; ACK_ERR_UNSUPPORTED_OP otherwise) whose outputs
+ * are also stored into `npeers` (at most 7) other ranks' slots at Y's offsets;
+ * its blocks fence at system scope before they exit. */
+int32_t ack_vq_dense_peers(const uint8_t *plan, size_t plan_len, const AckVqOperands *ops, float *const *peers,
+                           uint32_t npeers, void *stream);
+/* After the stream's earlier work, store `epoch` (release, system scope) into
+ * slot `rank` of each of the `world` flag arrays (u32 per sender). */
+int32_t ack_peer_signal(uint32_t *const *flags, uint32_t world, uint32_t rank, uint32_t epoch, void *stream);
+/* Wait until each of this rank's `world` flags has reached `epoch` (epochs
+ * only grow), at most `polls` polls a flag (0: 2^24, about two seconds);
+ * a wait that runs out ORs ACK_VQ_STATUS_STALLED into `status`. */
+int32_t ack_peer_wait(const uint32_t *flags, uint32_t world, uint32_t epoch, uint32_t *status, uint32_t polls,
+                      void *stream);
+
 /* ---- test-only host fault injection (the reference's `ack_inject_fault`,
  * ffi.rs:3449, behind its `fault-injection` feature). Refused unless the
  * process environment has ACK_FAULT_INJECTION=1. kind 0: the next stream

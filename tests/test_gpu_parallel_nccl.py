@@ -1,7 +1,9 @@
 """Row-sharded products over NCCL on two GPUs: each rank runs the dense and
 the both-coded product on its rows of W and one all-gather assembles Y; the
 result must equal the one-GPU product bit for bit (the same kernels and the
-same per-row summation order). Skipped with fewer than two GPUs; the
+same per-row summation order). The M = 1 product with peer stores
+(`PeerSlots`: each rank's GEMV writes its rows into every rank's buffer over
+NVLink, then step flags) must equal the all-gathered rows bit for bit. Skipped with fewer than two GPUs; the
 sharding arithmetic itself is covered on CPU by the gloo tests."""
 import os
 import socket
@@ -62,7 +64,33 @@ def _worker(rank, world, port, out_dir):
         c, st = parallel.coded_sharded(a_codes, tbook, tcodes[w0:w1].contiguous(), tbook, m, n, k, group)
         cuda.check(st)
         same_coded = bool(torch.equal(c.view(torch.int32), cfull.view(torch.int32)))
-        Path(out_dir, f"rank{rank}").write_text(f"{int(same_dense)} {int(same_coded)}")
+        # M = 1 over many experts (the byte-pair kernel) with peer stores instead of the all-gather
+        e, n1, k1 = 64, 1024, 4096
+        pcodes = torch.from_numpy(o.pack(rng.integers(0, 16, e * n1 * k1 // group)).view(np.int32)).to(dev)
+        pcodes = pcodes.view(e, -1)
+        pbooks = tbook.unsqueeze(0).repeat(e, 1, 1).contiguous()
+        px = torch.from_numpy(rng.standard_normal((e, 1, k1)).astype(np.float32)).to(dev)
+        lo1, hi1 = parallel.row_ranges(n1, k1, group, world)[rank]
+        rw = k1 // group // 8
+        shard = pcodes.view(e, n1, rw)[:, lo1:hi1].contiguous().view(e, -1)
+        st = cuda.status_word(dev)
+        yl, _ = cuda.dense(px, shard, pbooks, hi1 - lo1, group, status=st)
+        gathered = torch.empty((world, e, hi1 - lo1), device=dev)
+        dist.all_gather_into_tensor(gathered.view(-1), yl.contiguous().view(-1))
+        slots = parallel.PeerSlots(e, hi1 - lo1)
+        try:
+            for _ in range(3):   # repeated steps: the flags move by epoch
+                got = slots.dense(px, shard, pbooks, hi1 - lo1, group, st)
+                torch.cuda.synchronize()
+                cuda.check(st)
+                same_peer = bool(torch.equal(got.view(torch.int32), gathered.view(torch.int32)))
+                dist.barrier()
+                if not same_peer:
+                    break
+        finally:
+            slots.close()
+            dist.barrier()
+        Path(out_dir, f"rank{rank}").write_text(f"{int(same_dense)} {int(same_coded)} {int(same_peer)}")
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -84,4 +112,4 @@ def test_row_sharded_products_over_nccl_equal_the_single_gpu_product(tmp_path):
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
-        assert (tmp_path / f"rank{r}").read_text() == "1 1"
+        assert (tmp_path / f"rank{r}").read_text() == "1 1 1"
