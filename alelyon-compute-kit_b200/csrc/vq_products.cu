@@ -474,17 +474,18 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   uint32_t w[pair::kRows];
   // one 32-row batch of code words: the rows of `unit`, of the expert whose
   // (chunk) codes start at cbp and whose first unit is firstp
-  auto load_from = [&](const uint32_t* cbp, uint64_t firstp, uint64_t unit) {
-    const uint32_t n0 = uint32_t(unit - firstp) * pair::kRows;
-    const uint32_t off = n0 * row_words + lane;
+  // one 32-row batch of code words: rows n0.. of an expert, `wp` this lane's
+  // word of row n0
+  auto load_rows = [&](const uint32_t* wp, uint32_t n0) {
     if (n0 + pair::kRows <= N) {
 #pragma unroll
-      for (int r = 0; r < pair::kRows; ++r) w[r] = __ldcs(cbp + off + uint32_t(r) * row_words);
+      for (int r = 0; r < pair::kRows; ++r) w[r] = __ldcs(wp + uint32_t(r) * row_words);
     } else {
 #pragma unroll
-      for (int r = 0; r < pair::kRows; ++r) w[r] = n0 + r < N ? __ldcs(cbp + off + uint32_t(r) * row_words) : 0u;
+      for (int r = 0; r < pair::kRows; ++r) w[r] = n0 + r < N ? __ldcs(wp + uint32_t(r) * row_words) : 0u;
     }
   };
+  constexpr uint32_t kStepRows = pair::kWarps * pair::kRows;  // rows between a warp's batches
   bool preloaded = false;  // w already holds this warp's first batch of the current (segment, chunk)
   uint32_t ybits = 0;      // nonfinite outputs (from x, or overflow)
   while (s0 < u1) {
@@ -493,12 +494,15 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     // codes of this (expert, chunk): a warp-uniform base, 32-bit lane offsets
     const uint32_t* cb = codes + uint64_t(e) * words_per_expert + uint64_t(c) * 32u;
     float* ye = Y + uint64_t(e) * N;
-    uint64_t u = s0 + warp;
     const uint64_t first = uint64_t(e) * nb;  // units of this segment are one expert's
-    auto load = [&](uint64_t unit) { load_from(cb, first, unit); };
+    // this warp's batches: rows n0, n0 + kStepRows, ... below nend, the lane's
+    // word pointer advanced with them
+    const uint32_t nend = uint32_t(s1 - first) * pair::kRows;
+    uint32_t n0 = uint32_t(s0 + warp - first) * pair::kRows;
+    const uint32_t* wp = cb + n0 * row_words + lane;
     // the first batch's code words are in flight during the table build (or
     // were issued during this warp's last batch of the previous segment)
-    if (!preloaded && u < s1) load(u);
+    if (!preloaded && n0 < nend) load_rows(wp, n0);
     preloaded = false;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // this chunk's x and book are in; Q is no longer read
@@ -556,8 +560,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     }
     __syncthreads();
 
-    for (; u < s1; u += pair::kWarps) {
-      const uint32_t n0 = uint32_t(u - first) * pair::kRows;
+    for (; n0 < nend; n0 += kStepRows, wp += kStepRows * row_words) {
       float v[pair::kRows];
 #pragma unroll
       for (int r = 0; r < pair::kRows; ++r) {
@@ -568,8 +571,8 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         const float q3 = *reinterpret_cast<const float*>(qb + __byte_perm(w[r], base, 0x6735));
         v[r] = (q0 + q1) + (q2 + q3);
       }
-      if (u + pair::kWarps < s1) {
-        load(u + pair::kWarps);  // in flight during the folding
+      if (n0 + kStepRows < nend) {
+        load_rows(wp + kStepRows * row_words, n0 + kStepRows);  // in flight during the folding
       } else {
         // this warp's last batch here: the first batch of the next (segment,
         // chunk) goes in flight now, through the fold, the barrier and the
@@ -582,7 +585,8 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         }
         if (ns < u1 && ns + warp < seg_end(ns)) {
           const uint32_t en = uint32_t(ns / nb);
-          load_from(codes + uint64_t(en) * words_per_expert + uint64_t(nc) * 32u, uint64_t(en) * nb, ns + warp);
+          const uint32_t nn0 = uint32_t(ns + warp - uint64_t(en) * nb) * pair::kRows;
+          load_rows(codes + uint64_t(en) * words_per_expert + uint64_t(nc) * 32u + nn0 * row_words + lane, nn0);
           preloaded = true;
         }
       }
@@ -599,10 +603,10 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       }
       if (n0 + lane < N) {  // lane l now holds row n0 + l
         float* y = ye + n0 + lane;
-        const float nv = c == 0 ? v[0] : *y + v[0];
+        const float nv = (ONE || c == 0) ? v[0] : *y + v[0];
         *y = nv;
         ybits |= finite32(nv) ? 0u : kNonfinite;  // a nonfinite partial sum stays nonfinite
-        if (c + 1 == chunks)  // the finished value, into every peer's slot too (NVLink stores)
+        if (ONE || c + 1 == chunks)  // the finished value, into every peer's slot too (NVLink stores)
           for (uint32_t i = 0; i < peers.n; ++i) peers.dst[i][uint64_t(e) * N + n0 + lane] = nv;
       }
     }
