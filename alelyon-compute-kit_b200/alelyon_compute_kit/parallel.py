@@ -189,27 +189,38 @@ class PeerSlots:
                                               ctypes.c_uint32, ctypes.c_void_p])):
             getattr(c, name).argtypes = args
             getattr(c, name).restype = ctypes.c_int32
+        # every rank reaches every collective below, and all give up together
+        # if any rank's allocation or mapping fails (no rank is left waiting)
         ptr, handle = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
         with torch.cuda.device(self.device):
             rc = c.ack_peer_alloc(self.flags_off + 256, ctypes.byref(ptr), handle)
-        if rc != ack.ACK_OK:
-            raise ack._kit_error("peer-alloc", rc, self._lib.last_error())
+        mine = bytes(handle) if rc == ack.ACK_OK else None
+        error = None if rc == ack.ACK_OK else self._lib.last_error()
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
+        dist.all_gather_object(handles, mine, group=group)
         self.base = [0] * self.world
         self._opened = []
-        with torch.cuda.device(self.device):
-            for r in range(self.world):
-                if r == self.rank:
-                    self.base[r] = ptr.value
-                    continue
-                peer = ctypes.c_void_p()
-                h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
-                rc = c.ack_peer_open(h, ctypes.byref(peer))
-                if rc != ack.ACK_OK:
-                    raise ack._kit_error("peer-open", rc, self._lib.last_error())
-                self.base[r] = peer.value
-                self._opened.append(peer.value)
+        if mine is not None:
+            self.base[self.rank] = ptr.value
+        if all(h is not None for h in handles):
+            with torch.cuda.device(self.device):
+                for r in range(self.world):
+                    if r == self.rank:
+                        continue
+                    peer = ctypes.c_void_p()
+                    h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                    if c.ack_peer_open(h, ctypes.byref(peer)) != ack.ACK_OK:
+                        error = error or self._lib.last_error()
+                        break
+                    self.base[r] = peer.value
+                    self._opened.append(peer.value)
+        else:
+            error = error or "a peer rank could not allocate its buffer"
+        ok = torch.tensor([0 if error else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise ack.AckError(f"peer slots unavailable: {error or 'another rank failed'}")
         others = [self.base[r] + self.rank * self.slot for r in range(self.world) if r != self.rank]
         self._peers = (ctypes.c_void_p * max(1, len(others)))(*others)
         self._flags = (ctypes.c_void_p * self.world)(*[b + self.flags_off for b in self.base])

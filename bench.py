@@ -376,16 +376,20 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
     ms_g, _ = _timed(torch, compute_gather, args.steps, args.warmup, world, device, local, label="sharded-gather")
     cuda.check(status)
     # the same gathered result by peer stores from the GEMV itself (equal shards only)
-    ms_p = None
+    ms_p, peer_error = None, None
     if r1 - r0 == width:
-        slots = parallel.PeerSlots(experts, width)
         try:
-            ms_p, _ = _timed(torch, lambda: slots.dense(x, shard, books, width, GROUP, status), args.steps,
-                             args.warmup, world, device, local, label="sharded-peer")
-            cuda.check(status)
-        finally:
-            slots.close()
-            dist.barrier()
+            slots = parallel.PeerSlots(experts, width)   # all ranks raise together if any cannot map
+        except Exception as exc:  # noqa: BLE001
+            slots, peer_error = None, str(exc)[:200]
+        if slots is not None:
+            try:
+                ms_p, _ = _timed(torch, lambda: slots.dense(x, shard, books, width, GROUP, status), args.steps,
+                                 args.warmup, world, device, local, label="sharded-peer")
+                cuda.check(status)
+            finally:
+                slots.close()
+                dist.barrier()
     coded_total = experts * (CODE_BYTES + BOOK_BYTES)
     out = {"cfg2-nsplit": {
         "metric": "vq4 packed GEMV coded-weight GB/s, W rows split across ranks (cfg2, M=1, strong scaling)",
@@ -395,6 +399,7 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
         "value_with_allgather": round(coded_total / (ms_g / 1e3) / 1e9, 2),
         "allgather_bytes_per_rank": send.numel() * 4, "allgather_share": round(max(0.0, ms_g - ms_c) / ms_g, 4),
         "ms_per_step_with_peer_stores": None if ms_p is None else round(ms_p, 4),
+        "peer_stores_error": peer_error,
         "value_with_peer_stores": None if ms_p is None else round(coded_total / (ms_p / 1e3) / 1e9, 2),
         "peer_stores": "the GEMV stores each output into every rank's rank-major buffer over NVLink (CUDA IPC), "
                        "then step flags; the same bytes as the all-gather, bit for bit",
