@@ -681,16 +681,17 @@ __global__ void __launch_bounds__(kThreads, 2) k_coded_lut(const uint32_t* __res
     for (int j = 0; j < RJ; ++j) bw[j] = __ldg(bcol[j] + tw);
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
-      const float* Lr[RI];
-#pragma unroll
-      for (int i = 0; i < RI; ++i) Lr[i] = L + (((aw[i] >> (4 * s)) & 15u) << 4);
+      // the A rows' table rows are warp-uniform: lane l holds entry l % 16 of
+      // each, and a lookup is a shuffle from the lane of B's code
       uint32_t b1[RJ];
 #pragma unroll
       for (int j = 0; j < RJ; ++j) b1[j] = (bw[j] >> (4 * s)) & 15u;
 #pragma unroll
-      for (int i = 0; i < RI; ++i)
+      for (int i = 0; i < RI; ++i) {
+        const float row = L[(((aw[i] >> (4 * s)) & 15u) << 4) + (lane & 15u)];
 #pragma unroll
-        for (int j = 0; j < RJ; ++j) acc[i][j] += Lr[i][b1[j]];
+        for (int j = 0; j < RJ; ++j) acc[i][j] += __shfl_sync(0xffffffffu, row, b1[j]);
+      }
     }
   }
   uint32_t bits = 0;
