@@ -493,7 +493,7 @@ def run_nf4(args, world, rank, local) -> dict:
                      absmax2[e0 * per // 16384: (e0 + chunk) * per // 16384], tables, starts, offsets, table,
                      rows=chunk, n=N_ROWS, k=K_COLS, elem="bf16", max_rows=1, out=out[c])
 
-    ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local, label="nf4")
+    ms, clocks = _timed(torch, step, args.steps, args.warmup, world, device, local)
     weight = experts * wb_per
     algorithmic = weight + experts * (2 * K_COLS + 4 * N_ROWS)
     del packed, absq, absmax2, a16, out
