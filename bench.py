@@ -383,10 +383,13 @@ def run_sharded(args, torch, cuda, codes, books, device, world, rank, local) -> 
         except Exception as exc:  # noqa: BLE001
             slots, peer_error = None, str(exc)[:200]
         if slots is not None:
+            pstatus = cuda.status_word(device)   # its own word: a stalled wait is reported, not fatal
             try:
-                ms_p, _ = _timed(torch, lambda: slots.dense(x, shard, books, width, GROUP, status), args.steps,
+                ms_p, _ = _timed(torch, lambda: slots.dense(x, shard, books, width, GROUP, pstatus), args.steps,
                                  args.warmup, world, device, local, label="sharded-peer")
-                cuda.check(status)
+                cuda.check(pstatus)
+            except Exception as exc:  # noqa: BLE001
+                ms_p, peer_error = None, str(exc)[:200]
             finally:
                 slots.close()
                 dist.barrier()
