@@ -790,7 +790,7 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   if (parts == 0) parts = uint32_t(std::min<uint64_t>(16, E));  // measured best for cfg2 M = 1 (12-24 alike)
   parts = uint32_t(std::min<uint64_t>(parts, E));
   const uint32_t per = (E + parts - 1) / parts;
-  const uint64_t x_part = uint64_t(per) * M * K * 4, y_part = uint64_t(per) * M * N * 4;
+
   const uint64_t w_bytes = bc->bytes / E, book_bytes = bb->bytes / E;
   const uint64_t ws_part = (p.flags & 8u) ? ack::dense_tc_workspace_bytes(M, K, p.group, per) : 0;
   DeviceScope scope(dev->ordinal);
@@ -798,23 +798,16 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
   cudaStream_t cs = dev->stream, in = dev->copy_in, out = dev->copy_out;
   cudaEvent_t allocated = dev->ev[0], *h_done = dev->ev + 1, *k_done = dev->ev + 3, *d_done = dev->ev + 5;
-  // scratch: two buffers each of X, Y and (tensor-core path) workspace per part, and the status word
+  // scratch: all of X and Y (so no part waits for another's buffer), two
+  // tensor-core workspaces (reused in stream order), the status word
   auto up = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
-  const uint64_t need = 2 * (up(x_part) + up(y_part) + up(ws_part)) + 256;
+  const uint64_t x_all = uint64_t(E) * M * K * 4, y_all = uint64_t(E) * M * N * 4;
+  const uint64_t need = up(x_all) + up(y_all) + 2 * up(ws_part) + 256;
   e = pipeline_scratch(*dev, need);
   if (e != cudaSuccess) return cuda_fail(*dev, e, entry);
-  void *xb[2] = {}, *yb[2] = {}, *wb[2] = {};
-  {
-    char* at = static_cast<char*>(dev->scratch);
-    for (int b = 0; b < 2; ++b) {
-      xb[b] = at;
-      at += up(x_part);
-      yb[b] = at;
-      at += up(y_part);
-      wb[b] = ws_part ? at : nullptr;
-      at += up(ws_part);
-    }
-  }
+  char* xd = static_cast<char*>(dev->scratch);
+  char* yd = xd + up(x_all);
+  void* wb[2] = {ws_part ? yd + up(y_all) : nullptr, ws_part ? yd + up(y_all) + up(ws_part) : nullptr};
   uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<char*>(dev->scratch) + need - 256);
   auto fail = [&](cudaError_t err) { return cuda_fail(*dev, err, entry); };
   e = cudaMemsetAsync(status, 0, 4, cs);
@@ -824,31 +817,28 @@ ACK_EXPORT int32_t ack_vq2_dense_host(const AckDevice* handle, const uint8_t* pl
   if (e != cudaSuccess) return fail(e);
   const char* xh = reinterpret_cast<const char*>(x);
   char* yh = reinterpret_cast<char*>(y);
+  // the copies in run back to back on their stream; part c's product waits
+  // only for its own X, its copy out only for its own product (each event is
+  // waited on right after it is recorded, so one event of each kind serves
+  // every part)
   for (uint32_t c = 0; c < parts && e == cudaSuccess; ++c) {
-    const uint32_t b = c & 1u, e0 = c * per, ec = std::min<uint32_t>(per, E - std::min<uint32_t>(E, e0));
+    const uint32_t e0 = c * per, ec = std::min<uint32_t>(per, E - std::min<uint32_t>(E, e0));
     if (!ec) break;
-    // in: part c's X once the product of part c - 2 no longer reads its buffer
-    if (c >= 2) e = cudaStreamWaitEvent(in, k_done[b], 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(xb[b], xh + uint64_t(e0) * M * K * 4, uint64_t(ec) * M * K * 4,
-                                              cudaMemcpyHostToDevice, in);
-    if (e == cudaSuccess) e = cudaEventRecord(h_done[b], in);
-    // compute: once part c's X is in and part c - 2's Y is out of the buffer
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, h_done[b], 0);
-    if (e == cudaSuccess && c >= 2) e = cudaStreamWaitEvent(cs, d_done[b], 0);
+    const uint64_t xo = uint64_t(e0) * M * K * 4, yo = uint64_t(e0) * M * N * 4;
+    e = cudaMemcpyAsync(xd + xo, xh + xo, uint64_t(ec) * M * K * 4, cudaMemcpyHostToDevice, in);
+    if (e == cudaSuccess) e = cudaEventRecord(h_done[0], in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, h_done[0], 0);
     if (e == cudaSuccess) {
       ack::Plan q = p;
       q.batch = ec;
-      void* ptr[ack::kSlots] = {xb[b], static_cast<char*>(bc->ptr) + uint64_t(e0) * w_bytes,
-                                static_cast<char*>(bb->ptr) + uint64_t(e0) * book_bytes, nullptr, wb[b], yb[b],
-                                nullptr, status};
+      void* ptr[ack::kSlots] = {xd + xo, static_cast<char*>(bc->ptr) + uint64_t(e0) * w_bytes,
+                                static_cast<char*>(bb->ptr) + uint64_t(e0) * book_bytes, nullptr, wb[c & 1u],
+                                yd + yo, nullptr, status};
       e = ack::launch(q, ptr, cs);
     }
-    if (e == cudaSuccess) e = cudaEventRecord(k_done[b], cs);
-    // out: part c's Y once its product is done
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(out, k_done[b], 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(yh + uint64_t(e0) * M * N * 4, yb[b], uint64_t(ec) * M * N * 4,
-                                              cudaMemcpyDeviceToHost, out);
-    if (e == cudaSuccess) e = cudaEventRecord(d_done[b], out);
+    if (e == cudaSuccess) e = cudaEventRecord(k_done[0], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(out, k_done[0], 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(yh + yo, yd + yo, uint64_t(ec) * M * N * 4, cudaMemcpyDeviceToHost, out);
   }
   // the status word is read on the compute stream after the last copies out
   if (e == cudaSuccess) e = cudaEventRecord(d_done[0], out);

@@ -256,15 +256,15 @@ int32_t ack_vq2(const AckDevice *dev, const AckBuffer *const *slots, size_t nslo
  * `codes` and `books` are device buffers holding the weights (canonical or
  * tile32, as the flags say), `x` (batch x M x K f32) and `y` (batch x M x N
  * f32) host memory. The experts run in `parts` contiguous ranges (0: the
- * library chooses): part c's X is copied in on one stream while part c-1
- * computes and part c-2's Y is copied out on a third, so the copies and the
- * products overlap (host memory must be page-locked for the copies to be
- * asynchronous). Returns when all of `y` is written; `*status_out` (not
+ * library chooses): the parts' X are copied in back to back on one stream,
+ * part c computes once its X is in and its Y is copied out on a third stream
+ * once computed, so the copies and the products overlap (host memory must be
+ * page-locked for the copies to be asynchronous). Returns when all of `y` is written; `*status_out` (not
  * null) receives the status word of the whole product, read once; bit 1
  * there covers a nonfinite X or product (X is not scanned on the host). The
- * device scratch (two parts of X and Y, and the tensor-core workspace when
- * flag 8 is set) is allocated on first use, grows to the largest call's
- * need and is kept by the device until ack_close. */
+ * device scratch (all of X and Y, and two tensor-core workspaces when flag 8
+ * is set) is allocated on first use, grows to the largest call's need and is
+ * kept by the device until ack_close. */
 int32_t ack_vq2_dense_host(const AckDevice *dev, const uint8_t *plan, size_t plan_len, const AckBuffer *codes,
                            const AckBuffer *books, const float *x, float *y, uint32_t parts, uint32_t *status_out);
 
