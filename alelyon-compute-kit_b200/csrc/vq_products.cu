@@ -422,13 +422,18 @@ constexpr uint32_t kQFloats = 128u * 256u;         // the byte table
 constexpr uint32_t kPFloats = 256u * 16u + 32u;    // P, one pad word per 8 groups
 __device__ __forceinline__ uint32_t p_index(uint32_t t, uint32_t c) { return t * 16u + c + (t >> 3); }
 
+// The book's 16 rows sit G + 4 floats apart in shared memory, so the 16
+// threads that each read one row as float4s hit 16 distinct bank quads.
+template <int G>
+constexpr uint32_t kBookStride = G + 4;
+
 // Table, P and one x-chunk buffer (the next chunk is prefetched into it once
 // P is built): 161 KB for g16, so the 164 KB shared-memory configuration
 // leaves ~92 KB of L1 for the code loads in flight (the largest carveout
 // measured 6% slower).
 template <int G>
 constexpr size_t smem_bytes() {
-  return (size_t(kQFloats) + kPFloats + 256 * G + 16 * G) * sizeof(float);
+  return (size_t(kQFloats) + kPFloats + 256 * G + 16 * kBookStride<G>) * sizeof(float);
 }
 
 }  // namespace pair
@@ -438,7 +443,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     k_dense_pair(const float* __restrict__ X, const uint32_t* __restrict__ codes, const float* __restrict__ books,
                  float* __restrict__ Y, uint32_t N, uint32_t K, uint32_t E, uint64_t words_per_expert,
                  uint32_t* __restrict__ status, const __grid_constant__ PeerY peers) {
-  constexpr uint32_t kChunkX = 256u * G, kBook = 16u * G;
+  constexpr uint32_t kChunkX = 256u * G, kBook = 16u * G, kBs = pair::kBookStride<G>;
   extern __shared__ __align__(16) float pair_smem[];
   float* Q = pair_smem;
   float* P = Q + pair::kQFloats;
@@ -460,9 +465,12 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     const float* xs = X + uint64_t(e) * K + uint64_t(c) * kChunkX;
     const float* bs = books + uint64_t(e) * kBook;
     for (uint32_t i = tid; i < (kChunkX + kBook) / 4; i += pair::kThreads) {
-      const float* src = i < kChunkX / 4 ? xs + 4 * i : bs + 4 * (i - kChunkX / 4);
+      // x pieces land contiguously; book piece q (row q / (G/4)) at the padded row stride
+      const uint32_t q = i - kChunkX / 4;
+      const float* src = i < kChunkX / 4 ? xs + 4 * i : bs + 4 * q;
+      float* d = i < kChunkX / 4 ? dst + 4 * i : dst + kChunkX + (q / (G / 4)) * kBs + 4 * (q % (G / 4));
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(dst + 4 * i))),
+                       __cvta_generic_to_shared(d))),
                    "l"(src)
                    : "memory");
     }
@@ -510,7 +518,8 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     const float* bk = xs + kChunkX;
     if (c == 0 && s0 % nb == 0) {  // the expert's first unit reports a nonfinite book
       uint32_t bits = 0;
-      for (uint32_t i = tid; i < kBook; i += pair::kThreads) bits |= finite32(bk[i]) ? 0u : kNonfinite;
+      for (uint32_t i = tid; i < kBook; i += pair::kThreads)
+        bits |= finite32(bk[(i / G) * kBs + i % G]) ? 0u : kNonfinite;
       flag_warp(status, bits);
     }
     {
@@ -518,7 +527,13 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       const uint32_t ce = tid & 15;
       float br[G];
 #pragma unroll
-      for (int j = 0; j < G; ++j) br[j] = bk[ce * G + j];
+      for (int j = 0; j < G; j += 4) {
+        const float4 b4 = *reinterpret_cast<const float4*>(bk + ce * kBs + j);
+        br[j] = b4.x;
+        br[j + 1] = b4.y;
+        br[j + 2] = b4.z;
+        br[j + 3] = b4.w;
+      }
       for (uint32_t t = tid >> 4; t < 256u; t += pair::kThreads / 16) {
         float a = 0.f;
 #pragma unroll
@@ -545,18 +560,23 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       if (ns < u1) prefetch(ns, nc);
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    // Q: a thread holds P[2p][0..15] and fills one high nibble; lane = slot i,
-    // so both the P loads and the Q stores are conflict-free
-    for (uint32_t task = tid; task < 128u * 16u; task += pair::kThreads) {
-      const uint32_t i = task & 31, j = (task >> 5) & 3, hi = task >> 7;
+    // Q: a thread holds P[2p][0..15] of one pair p = 4 i + j (lane = slot i)
+    // and fills four of its high nibbles, so both the P loads and the Q
+    // stores are conflict-free and P[2p] is read once
+    {
+      static_assert(pair::kThreads == 512, "four high nibbles per thread");
+      const uint32_t i = tid & 31, j = (tid >> 5) & 3, h0 = tid >> 7;
       const uint32_t p = 4 * i + j;
-      float lo[16];
+      float lo[16], hv[4];
 #pragma unroll
       for (int k = 0; k < 16; ++k) lo[k] = P[pair::p_index(2 * p, k)];
-      const float hv = P[pair::p_index(2 * p + 1, hi)];
-      float* q = Q + (j & 1u) * 32u + i + (j >> 1) * 16384u + hi * 16u * 64u;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) q[k * 64] = lo[k] + hv;
+      for (int h = 0; h < 4; ++h) hv[h] = P[pair::p_index(2 * p + 1, h0 + 4 * h)];
+      float* qp = Q + (j & 1u) * 32u + i + (j >> 1) * 16384u + h0 * 16u * 64u;
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+#pragma unroll
+        for (int k = 0; k < 16; ++k) qp[h * 4 * 16 * 64 + k * 64] = lo[k] + hv[h];
     }
     __syncthreads();
 
