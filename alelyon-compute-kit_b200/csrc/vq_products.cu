@@ -12,6 +12,7 @@
 
 #include "vq_common.cuh"
 #include "vq_kernels.hpp"
+#include "vq_tc.cuh"
 
 namespace ack {
 namespace {
@@ -412,7 +413,10 @@ __global__ void __launch_bounds__(kThreads, 3) k_dense_t32(const float* __restri
 //
 // One block of 16 warps per SM, persistent over (expert, 32-row batch)
 // units; the next unit range's x chunk and book are prefetched with
-// cp.async while the current one is looked up. Each row sums its 128 pair
+// cp.async (completion tracked by an mbarrier) while the current one is
+// looked up, and the warps that finish their lookups first build the next
+// P from them, so only the Q build stands between two segments' lookups
+// (two block barriers per segment). Each row sums its 128 pair
 // values per chunk in a fixed order (pairs, then a tree over lanes); chunks
 // add in order, so the result does not depend on the grid.
 namespace pair {
@@ -445,6 +449,8 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
                  uint32_t* __restrict__ status, const __grid_constant__ PeerY peers) {
   constexpr uint32_t kChunkX = 256u * G, kBook = 16u * G, kBs = pair::kBookStride<G>;
   extern __shared__ __align__(16) float pair_smem[];
+  __shared__ uint64_t xfull;  // phase k: the k-th prefetched x chunk and book have landed
+  __shared__ uint32_t ptask;  // the next P task of the build under way
   float* Q = pair_smem;
   float* P = Q + pair::kQFloats;
   float* xbuf = P + pair::kPFloats;  // x chunk, then the book
@@ -456,9 +462,17 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   if (u0 >= u1) return;
   // byte 0: 4 i (slots 0, 2) or 4 i + 128 (slots 1, 3); byte 2: 0 or 1 (x 64 KB)
   const uint32_t base = (lane * 4u) | ((lane * 4u + 128u) << 8) | (1u << 24);
+  if (tid == 0) {
+    tc::mb_init(&xfull, pair::kThreads);  // one cp.async arrival per thread per phase
+    ptask = 0;
+  }
+  __syncthreads();
 
   // the work list: (segment of one expert's units, chunk) in order
   auto seg_end = [&](uint64_t s) { return min(u1, (s / nb + 1) * nb); };
+  // every thread copies its share of the x chunk and book of (s, c) into
+  // xbuf and arrives on xfull when its copies have landed
+  uint32_t xph = 1;  // parity of the last phase prefetched
   auto prefetch = [&](uint64_t s, uint32_t c) {
     const uint32_t e = uint32_t(s / nb);
     float* dst = xbuf;
@@ -469,19 +483,64 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       const uint32_t q = i - kChunkX / 4;
       const float* src = i < kChunkX / 4 ? xs + 4 * i : bs + 4 * q;
       float* d = i < kChunkX / 4 ? dst + 4 * i : dst + kChunkX + (q / (G / 4)) * kBs + 4 * (q % (G / 4));
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(d))),
-                   "l"(src)
-                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(d)), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(&xfull)) : "memory");
+    xph ^= 1u;
+  };
+  uint32_t ybits = 0;  // nonfinite outputs (from x, or overflow)
+  // P[t][e] = x_t . c_e of the last prefetched (segment, chunk), in tasks of
+  // 8 groups that any warp takes once its lookups are done: the warps that
+  // finish a segment early build the next one's P while the rest look up.
+  // `first_unit`: the chunk opens an expert, whose nonfinite book is reported.
+  auto build_p = [&](bool first_unit) {
+    bool have_book = false;
+    float br[G];  // book row lane % 16
+    for (;;) {
+      uint32_t task = 0;
+      if (lane == 0) task = atomicAdd(&ptask, 1u);
+      task = __shfl_sync(0xffffffffu, task, 0);
+      if (task >= 256u / 8u) break;
+      if (!have_book) {
+        if (!tc::mb_wait(&xfull, xph) && lane == 0) atomicOr(status, kStalled);
+        const float* bk = xbuf + kChunkX + (lane & 15) * kBs;
+#pragma unroll
+        for (int j = 0; j < G; j += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(bk + j);
+          br[j] = b4.x;
+          br[j + 1] = b4.y;
+          br[j + 2] = b4.z;
+          br[j + 3] = b4.w;
+        }
+        if (first_unit) {
+          uint32_t bits = 0;
+#pragma unroll
+          for (int j = 0; j < G; ++j) bits |= finite32(br[j]) ? 0u : kNonfinite;
+          flag_warp(status, bits);
+        }
+        have_book = true;
+      }
+#pragma unroll
+      for (uint32_t it = 0; it < 4; ++it) {
+        const uint32_t t = task * 8u + 2u * it + (lane >> 4);
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < G; j += 4) {
+          const float4 x4 = *reinterpret_cast<const float4*>(xbuf + t * G + j);
+          a = fmaf(x4.x, br[j], a);
+          a = fmaf(x4.y, br[j + 1], a);
+          a = fmaf(x4.z, br[j + 2], a);
+          a = fmaf(x4.w, br[j + 3], a);
+        }
+        P[pair::p_index(t, lane & 15)] = a;
+      }
     }
   };
   uint64_t s0 = u0;
   uint32_t c = 0;
   prefetch(s0, 0);
-  asm volatile("cp.async.commit_group;" ::: "memory");
+  build_p(s0 % nb == 0);
   uint32_t w[pair::kRows];
-  // one 32-row batch of code words: the rows of `unit`, of the expert whose
-  // (chunk) codes start at cbp and whose first unit is firstp
   // one 32-row batch of code words: rows n0.. of an expert, `wp` this lane's
   // word of row n0
   auto load_rows = [&](const uint32_t* wp, uint32_t n0) {
@@ -495,10 +554,17 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   };
   constexpr uint32_t kStepRows = pair::kWarps * pair::kRows;  // rows between a warp's batches
   bool preloaded = false;  // w already holds this warp's first batch of the current (segment, chunk)
-  uint32_t ybits = 0;      // nonfinite outputs (from x, or overflow)
   while (s0 < u1) {
     const uint64_t s1 = seg_end(s0);
     const uint32_t e = uint32_t(s0 / nb);
+    // the next (segment, chunk)
+    uint64_t ns = s0;
+    uint32_t nc = c + 1;
+    if (nc == chunks) {
+      nc = 0;
+      ns = s1;
+    }
+    const bool more = ns < u1;
     // codes of this (expert, chunk): a warp-uniform base, 32-bit lane offsets
     const uint32_t* cb = codes + uint64_t(e) * words_per_expert + uint64_t(c) * 32u;
     float* ye = Y + uint64_t(e) * N;
@@ -512,54 +578,10 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     // were issued during this warp's last batch of the previous segment)
     if (!preloaded && n0 < nend) load_rows(wp, n0);
     preloaded = false;
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();  // this chunk's x and book are in; Q is no longer read
-    const float* xs = xbuf;
-    const float* bk = xs + kChunkX;
-    if (c == 0 && s0 % nb == 0) {  // the expert's first unit reports a nonfinite book
-      uint32_t bits = 0;
-      for (uint32_t i = tid; i < kBook; i += pair::kThreads)
-        bits |= finite32(bk[(i / G) * kBs + i % G]) ? 0u : kNonfinite;
-      flag_warp(status, bits);
-    }
-    {
-      // P[t][e]: thread owns entry tid % 16 (its book row in registers)
-      const uint32_t ce = tid & 15;
-      float br[G];
-#pragma unroll
-      for (int j = 0; j < G; j += 4) {
-        const float4 b4 = *reinterpret_cast<const float4*>(bk + ce * kBs + j);
-        br[j] = b4.x;
-        br[j + 1] = b4.y;
-        br[j + 2] = b4.z;
-        br[j + 3] = b4.w;
-      }
-      for (uint32_t t = tid >> 4; t < 256u; t += pair::kThreads / 16) {
-        float a = 0.f;
-#pragma unroll
-        for (int j = 0; j < G; j += 4) {
-          const float4 x4 = *reinterpret_cast<const float4*>(xs + t * G + j);
-          a = fmaf(x4.x, br[j], a);
-          a = fmaf(x4.y, br[j + 1], a);
-          a = fmaf(x4.z, br[j + 2], a);
-          a = fmaf(x4.w, br[j + 3], a);
-        }
-        P[pair::p_index(t, ce)] = a;
-      }
-    }
-    __syncthreads();
-    {
-      // x is read: the next (segment, chunk)'s x and book, in flight during
-      // the table build and the lookups
-      uint64_t ns = s0;
-      uint32_t nc = c + 1;
-      if (nc == chunks) {
-        nc = 0;
-        ns = s1;
-      }
-      if (ns < u1) prefetch(ns, nc);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
+    __syncthreads();  // P of this chunk is built: Q, x and the book are no longer read
+    if (tid == 0) ptask = 0;
+    // the next chunk's x and book, in flight during the table build and the lookups
+    if (more) prefetch(ns, nc);
     // Q: a thread holds P[2p][0..15] of one pair p = 4 i + j (lane = slot i)
     // and fills four of its high nibbles, so both the P loads and the Q
     // stores are conflict-free and P[2p] is read once
@@ -578,7 +600,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 16; ++k) qp[h * 4 * 16 * 64 + k * 64] = lo[k] + hv[h];
     }
-    __syncthreads();
+    __syncthreads();  // Q is built; P is free for the next chunk
 
     for (; n0 < nend; n0 += kStepRows, wp += kStepRows * row_words) {
       float v[pair::kRows];
@@ -593,22 +615,14 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
       }
       if (n0 + kStepRows < nend) {
         load_rows(wp + kStepRows * row_words, n0 + kStepRows);  // in flight during the folding
-      } else {
+      } else if (more && ns + warp < seg_end(ns)) {
         // this warp's last batch here: the first batch of the next (segment,
-        // chunk) goes in flight now, through the fold, the barrier and the
-        // next table build
-        uint64_t ns = s0;
-        uint32_t nc = c + 1;
-        if (nc == chunks) {
-          nc = 0;
-          ns = s1;
-        }
-        if (ns < u1 && ns + warp < seg_end(ns)) {
-          const uint32_t en = uint32_t(ns / nb);
-          const uint32_t nn0 = uint32_t(ns + warp - uint64_t(en) * nb) * pair::kRows;
-          load_rows(codes + uint64_t(en) * words_per_expert + uint64_t(nc) * 32u + nn0 * row_words + lane, nn0);
-          preloaded = true;
-        }
+        // chunk) goes in flight now, through the fold, the P build, the
+        // barrier and the next table build
+        const uint32_t en = uint32_t(ns / nb);
+        const uint32_t nn0 = uint32_t(ns + warp - uint64_t(en) * nb) * pair::kRows;
+        load_rows(codes + uint64_t(en) * words_per_expert + uint64_t(nc) * 32u + nn0 * row_words + lane, nn0);
+        preloaded = true;
       }
       // fold lanes: each step halves the rows a lane keeps; after five, lane l holds row l
 #pragma unroll
@@ -630,15 +644,14 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
           for (uint32_t i = 0; i < peers.n; ++i) peers.dst[i][uint64_t(e) * N + n0 + lane] = nv;
       }
     }
-    // advance: the next chunk of this segment, or the next segment
-    if (++c == chunks) {
-      c = 0;
-      s0 = s1;
-    }
+    // this warp's lookups are done: help build the next chunk's P
+    if (more) build_p(nc == 0 && ns % nb == 0);
+    c = nc;
+    s0 = ns;
   }
   flag_warp(status, ybits);
   if (peers.n) __threadfence_system();  // the peer stores are visible before the block exits
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ------------------------------------------ coded A times coded B^T (LUT) --
