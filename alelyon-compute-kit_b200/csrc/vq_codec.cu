@@ -500,119 +500,121 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&full[s], (k / S) & 1, lim)))) break;
       if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&done[q], (k / C) & 1, lim)))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll(G == 8 ? 2 : 1)
-      for (int h = 0; h < H; ++h) {
-        uint32_t r[K::kN];
-        const uint32_t taddr = tmem + ((wq * 32u) << 16) + (q * H + h) * K::kN;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(taddr));
-        if constexpr (K::TIGHT)
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-                "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-                "=r"(r[30]), "=r"(r[31])
-              : "r"(taddr + 16u));
-        // ||x||^2 in enc_vector's order, from the swizzled tile (conflict-free);
-        // TIGHT also ||x - trunc(x)||^2, x truncated to its top 19 bits: the
-        // tensor core's operand is that or the nearer tf32 neighbour, so this
-        // bounds its residual either way
-        const unsigned char* tile = ring + s * K::kTile + h * K::kSub;
-        float2 n2 = make_float2(0.f, 0.f), r2 = make_float2(0.f, 0.f);
+      // sub-tiles are read in pairs: both accumulators' loads are in flight
+      // under one wait, and the two certificates interleave
+      constexpr int HP = H >= 2 ? 2 : 1;
 #pragma unroll
-        for (int kc = 0; kc < kChunks; ++kc) {
-          const float4 t = *reinterpret_cast<const float4*>(tile + W::off(row, kc));
-          n2 = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2);
-          n2 = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2);
-          if constexpr (K::RESID) {
-            const float2 a = make_float2(t.x - __uint_as_float(__float_as_uint(t.x) & 0xFFFFE000u),
-                                         t.y - __uint_as_float(__float_as_uint(t.y) & 0xFFFFE000u));
-            const float2 b = make_float2(t.z - __uint_as_float(__float_as_uint(t.z) & 0xFFFFE000u),
-                                         t.w - __uint_as_float(__float_as_uint(t.w) & 0xFFFFE000u));
-            r2 = __ffma2_rn(a, a, r2);
-            r2 = __ffma2_rn(b, b, r2);
+      for (int h0 = 0; h0 < H; h0 += HP) {
+        uint32_t r[HP][K::kN];
+        float2 n2[HP], r2[HP];
+#pragma unroll
+        for (int hp = 0; hp < HP; ++hp) {
+          const uint32_t taddr = tmem + ((wq * 32u) << 16) + (q * H + h0 + hp) * K::kN;
+          tc::tmem_ld16(r[hp], taddr);
+          if constexpr (K::TIGHT) tc::tmem_ld16(r[hp] + 16, taddr + 16u);
+          // ||x||^2 in enc_vector's order, from the swizzled tile (conflict-free);
+          // TIGHT also ||x - trunc(x)||^2, x truncated to its top 19 bits: the
+          // tensor core's operand is that or the nearer tf32 neighbour, so this
+          // bounds its residual either way
+          const unsigned char* tile = ring + s * K::kTile + (h0 + hp) * K::kSub;
+          n2[hp] = r2[hp] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int kc = 0; kc < kChunks; ++kc) {
+            const float4 t = *reinterpret_cast<const float4*>(tile + W::off(row, kc));
+            n2[hp] = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2[hp]);
+            n2[hp] = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2[hp]);
+            if constexpr (K::RESID) {
+              const float2 a = make_float2(t.x - __uint_as_float(__float_as_uint(t.x) & 0xFFFFE000u),
+                                           t.y - __uint_as_float(__float_as_uint(t.y) & 0xFFFFE000u));
+              const float2 b = make_float2(t.z - __uint_as_float(__float_as_uint(t.z) & 0xFFFFE000u),
+                                           t.w - __uint_as_float(__float_as_uint(t.w) & 0xFFFFE000u));
+              r2[hp] = __ffma2_rn(a, a, r2[hp]);
+              r2[hp] = __ffma2_rn(b, b, r2[hp]);
+            }
           }
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if constexpr (K::TIGHT) {
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float2 t = __fadd2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])),
-                                        make_float2(__uint_as_float(r[16 + e]), __uint_as_float(r[17 + e])));
-            r[e] = __float_as_uint(t.x);
-            r[e + 1] = __float_as_uint(t.y);
+        for (int hp = 0; hp < HP; ++hp) {
+          const int h = h0 + hp;
+          if constexpr (K::TIGHT) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float2 t = __fadd2_rn(make_float2(__uint_as_float(r[hp][e]), __uint_as_float(r[hp][e + 1])),
+                                          make_float2(__uint_as_float(r[hp][16 + e]), __uint_as_float(r[hp][17 + e])));
+              r[hp][e] = __float_as_uint(t.x);
+              r[hp][e + 1] = __float_as_uint(t.y);
+            }
           }
-        }
-        const uint64_t vbase = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h * 128;
-        const uint64_t v = vbase + row;
-        uint32_t idx = 0, bits = 0, cand = 0;
-        bool defer = false;
-        if (v < complete) {
-          float f[16];
+          const uint64_t vbase = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h * 128;
+          const uint64_t v = vbase + row;
+          const float nx = n2[hp].x + n2[hp].y;
+          uint32_t idx = 0, bits = 0, cand = 0;
+          bool defer = false;
+          if (v < complete) {
+            float f[16];
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const float2 t = __ffma2_rn(make_float2(-2.f, -2.f),
-                                        make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1])),
-                                        Book::qpair(p));
-            f[2 * p] = t.x;
-            f[2 * p + 1] = t.y;
-          }
-          float lo[8];
+            for (int p = 0; p < 8; ++p) {
+              const float2 t = __ffma2_rn(make_float2(-2.f, -2.f),
+                                          make_float2(__uint_as_float(r[hp][2 * p]), __uint_as_float(r[hp][2 * p + 1])),
+                                          Book::qpair(p));
+              f[2 * p] = t.x;
+              f[2 * p + 1] = t.y;
+            }
+            float lo[8];
 #pragma unroll
-          for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
+            for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
 #pragma unroll
-          for (int w = 4; w; w >>= 1)
+            for (int w = 4; w; w >>= 1)
 #pragma unroll
-            for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
-          const float fb = lo[0];
-          float eps;
-          if constexpr (K::TIGHT && !K::RESID) {
-            // x truncated (2^-10) against the exactly represented book
-            eps = fmaf(1.0f / 1024 + kappa_t, n2.x + n2.y + Book::cmax2(), 0x1p-118f);
-          } else if constexpr (K::RESID) {
-            // 2 ||r|| max||c|| (rounded up, 2^-16 margin for the FP32 sum of
-            // squares) + the accumulation, book-remainder, rounding and
-            // flushed-subnormal terms
-            const float rc = __fsqrt_ru(__fmul_ru(r2.x + r2.y, Book::cmax2()));
-            eps = fmaf(2.0f + 0x1p-15f, rc, fmaf(kappa_t, n2.x + n2.y + Book::cmax2(), 0x1p-118f));
-          } else {
-            eps = fmaf(kappa1, n2.x + n2.y + Book::cmax2(), 0x1p-118f);
-          }
-          const float thr = fmaf(2.f, eps, fb);
+              for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
+            const float fb = lo[0];
+            float eps;
+            if constexpr (K::TIGHT && !K::RESID) {
+              // x truncated (2^-10) against the exactly represented book
+              eps = fmaf(1.0f / 1024 + kappa_t, nx + Book::cmax2(), 0x1p-118f);
+            } else if constexpr (K::RESID) {
+              // 2 ||r|| max||c|| (rounded up, 2^-16 margin for the FP32 sum of
+              // squares) + the accumulation, book-remainder, rounding and
+              // flushed-subnormal terms
+              const float rc = __fsqrt_ru(__fmul_ru(r2[hp].x + r2[hp].y, Book::cmax2()));
+              eps = fmaf(2.0f + 0x1p-15f, rc, fmaf(kappa_t, nx + Book::cmax2(), 0x1p-118f));
+            } else {
+              eps = fmaf(kappa1, nx + Book::cmax2(), 0x1p-118f);
+            }
+            const float thr = fmaf(2.f, eps, fb);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
-          cand &= Book::uniq();
-          const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
-          if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
-            idx = uint32_t(__ffs(cand) - 1);
-          } else if (clean && cand != 0u) {
-            defer = true;
-          } else {
+            for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
+            cand &= Book::uniq();
+            const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
+            if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
+              idx = uint32_t(__ffs(cand) - 1);
+            } else if (clean && cand != 0u) {
+              defer = true;
+            } else {
+              const float* src = x + v * G;
+              for (int j = 0; j < G; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+              idx = enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
+            }
+          } else if (v < vectors) {
+            // the partial last vector: its valid components only (vq.py:171-172)
+            const int valid = int(n - v * G);
             const float* src = x + v * G;
-            for (int j = 0; j < G; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
-            idx = enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
+            for (int j = 0; j < valid; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
+            idx = enc_exact_mem<G, Book>(src, valid, 0xffffu);
           }
-        } else if (v < vectors) {
-          // the partial last vector: its valid components only (vq.py:171-172)
-          const int valid = int(n - v * G);
-          const float* src = x + v * G;
-          for (int j = 0; j < valid; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
-          idx = enc_exact_mem<G, Book>(src, valid, 0xffffu);
+          const uint32_t dm = __ballot_sync(0xffffffffu, defer);
+          if (defer) {
+            const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
+            q_vec[warp][pos] = v;
+            q_cand[warp][pos] = cand;
+          }
+          qtail += __popc(dm);
+          const uint32_t w = pack_nibbles(idx);
+          const uint64_t word = (vbase + wq * 32) / 8 + lane / 8;
+          if ((lane & 7) == 0 && word < words) codes[word] = w;
+          flag_warp(status, bits);
         }
-        const uint32_t dm = __ballot_sync(0xffffffffu, defer);
-        if (defer) {
-          const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
-          q_vec[warp][pos] = v;
-          q_cand[warp][pos] = cand;
-        }
-        qtail += __popc(dm);
-        const uint32_t w = pack_nibbles(idx);
-        const uint64_t word = (vbase + wq * 32) / 8 + lane / 8;
-        if ((lane & 7) == 0 && word < words) codes[word] = w;
-        flag_warp(status, bits);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();

@@ -57,6 +57,16 @@ __device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
+// 16 consecutive TMEM columns of this warp's 32 lanes into r[0..15]
+// (tcgen05.ld 32x32b.x16; the values are valid after tcgen05.wait::ld).
+__device__ __forceinline__ void tmem_ld16(uint32_t* r, uint32_t taddr) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 constexpr uint32_t kPolls = 1u << 22;       // the normal bound of a wait
 constexpr uint32_t kTestPolls = 1u << 10;   // pipeline waits under a host-injected stall test
 
