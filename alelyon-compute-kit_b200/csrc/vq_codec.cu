@@ -284,7 +284,11 @@ struct Cfg {
   static constexpr uint32_t kSub = 128u * G * 4u, kTile = kSub * H;
   static constexpr uint32_t kBoxRows = H > 2 ? 256u : 128u * H;
   static constexpr uint32_t kCols = C * H * kN <= 32 ? 32u : (C * H * kN <= 64 ? 64u : 128u);
-  static constexpr uint32_t kCap = H == 1 ? 64u : (H == 2 ? 128u : 256u);  // >= 31 + 32 H: a tile never overflows it
+  // queue ring per warp: flushed whenever it holds more than kCap - 32 H, so
+  // one tile's deferrals always fit; on smooth data a scheduled flush (every
+  // kFlush of the quad's tiles) finds 50-70 entries
+  static constexpr uint32_t kCap = 256u;
+  static constexpr uint32_t kFlush = 32;
   // dynamic shared memory: 1024-byte alignment slack, the ring, the tf32
   // book tile (kN rows, at most 4 KB), the FP32 book and its 16 squared norms
   static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 4096 + 16 * G * 4 + 64;
@@ -296,7 +300,7 @@ struct Cfg {
 // survives; the index is OR-ed into the zero nibble the filter pass stored.
 template <int G, class Book, uint32_t kCap>
 __device__ __noinline__ void refine_queue(const float* __restrict__ x, uint32_t* __restrict__ codes,
-                                          const uint64_t* qv, const uint32_t* qc, uint32_t head, uint32_t count,
+                                          const uint32_t* qv, const uint32_t* qc, uint32_t head, uint32_t count,
                                           const float* sbk, const float* sq, uint32_t lane) {
   constexpr float kappa2 = float(G + 8) / 8388608.0f;
   __syncwarp();  // the nibble stores of the filter pass come first
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
   float* sq = sbk + 16 * G;                               // its 16 squared norms
   __shared__ __align__(8) uint64_t full[S], sfree[S], done[C], afree[C];
   __shared__ uint32_t tmem_base;
-  __shared__ uint64_t q_vec[4 * C][kCap];
+  __shared__ uint32_t q_vec[4 * C][kCap];  // vector indices (below 2^31 on this path)
   __shared__ uint32_t q_cand[4 * C][kCap];
   const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
   const uint64_t vectors = (n + G - 1) / G, complete = n / G, words = (vectors + 7) / 8;
@@ -494,6 +498,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     constexpr float kappa1 = 1.0f / 1024 + 1.0f / 2048 + float(G + 8) / 2097152.0f;
     constexpr float kappa_t = float(G + 9) / 2097152.0f;  // TIGHT: all but the x residual
     uint32_t qhead = 0, qtail = 0;
+    constexpr uint32_t kChunk = 32u;  // queued vectors refined together (one per lane)
     for (uint32_t k = q; k < T && ok && stall_test != 2; k += C) {
       const uint32_t s = k % S;
       // warp-uniform outcomes: tcgen05.ld below is .sync.aligned
@@ -606,7 +611,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           const uint32_t dm = __ballot_sync(0xffffffffu, defer);
           if (defer) {
             const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
-            q_vec[warp][pos] = v;
+            q_vec[warp][pos] = uint32_t(v);
             q_cand[warp][pos] = cand;
           }
           qtail += __popc(dm);
@@ -622,14 +627,23 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
         tc::mb_arrive(&afree[q]);
         tc::mb_arrive(&sfree[s]);
       }
-      // refine off the pipeline's critical path, 32 vectors at a time
-      while (qtail - qhead >= 32u) {
-        tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, 32u, sbk, sq, lane);
-        qhead += 32u;
+      // Refine off the pipeline's critical path, kChunk vectors at a time. The
+      // four warps of a quad flush at the same tiles (every kFlush of the
+      // quad's tiles), so their refinements overlap instead of holding the
+      // quad's stages one warp after another; a queue that might not hold
+      // the next tile's deferrals flushes at once.
+      const uint32_t taken = (k - q) / C + 1;  // tiles this quad has certified
+      if (taken % K::kFlush == 0 || qtail - qhead > kCap - 32u * H) {
+        while (qtail != qhead) {
+          const uint32_t cnt = min(kChunk, qtail - qhead);
+          tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, cnt, sbk, sq, lane);
+          qhead += cnt;
+        }
       }
     }
-    if (ok && qtail != qhead)
-      tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, qtail - qhead, sbk, sq, lane);
+    for (; ok && qtail != qhead; qhead += min(kChunk, qtail - qhead))
+      tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, min(kChunk, qtail - qhead), sbk,
+                                      sq, lane);
     if (!ok) atomicOr(status, kStalled);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
