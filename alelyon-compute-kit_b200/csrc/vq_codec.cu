@@ -290,70 +290,34 @@ struct Cfg {
   static constexpr uint32_t kCap = 256u;
   static constexpr uint32_t kFlush = 32;
   // dynamic shared memory: 1024-byte alignment slack, the ring, the tf32
-  // book tile (kN rows, at most 4 KB), the FP32 book and its 16 squared norms
-  static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 4096 + 16 * G * 4 + 64;
+  // book tile (kN rows, at most 4 KB)
+  static constexpr size_t kSmem = 1024 + size_t(S) * kTile + 4096;
 };
 
 // Deferred FP32 refinement of `count` (<= 32) queued vectors, one per lane,
-// ring positions head + lane: x read again from memory, the FP32 filter of
-// enc_vector over the tf32 candidates, the float64 pass if more than one
-// survives; the index is OR-ed into the zero nibble the filter pass stored.
+// ring positions head + lane: x read again from memory, then enc_vector (the
+// FP32 filter over all 16 entries with its bound, packed FMAs against the
+// constant-bank book, no divergence across lanes) and its float64 pass if
+// more than one entry survives; the index is OR-ed into the zero nibble the
+// filter pass stored.
 template <int G, class Book, uint32_t kCap>
 __device__ __noinline__ void refine_queue(const float* __restrict__ x, uint32_t* __restrict__ codes,
-                                          const uint32_t* qv, const uint32_t* qc, uint32_t head, uint32_t count,
-                                          const float* sbk, const float* sq, uint32_t lane) {
-  constexpr float kappa2 = float(G + 8) / 8388608.0f;
+                                          const uint32_t* qv, uint32_t head, uint32_t count, uint32_t lane) {
   __syncwarp();  // the nibble stores of the filter pass come first
   if (lane < count) {
-    const uint32_t i = (head + lane) & (kCap - 1);
-    const uint64_t v = qv[i];
-    const uint32_t cand = qc[i];
-    const float4* src = reinterpret_cast<const float4*>(x + v * G);
+    const uint64_t v = qv[(head + lane) & (kCap - 1)];
+    const float* src = x + v * G;
     float xr[G];
-    float2 n2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int kc = 0; kc < G / 4; ++kc) {
-      const float4 t = __ldg(src + kc);
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src) + kc);
       xr[4 * kc] = t.x;
       xr[4 * kc + 1] = t.y;
       xr[4 * kc + 2] = t.z;
       xr[4 * kc + 3] = t.w;
-      n2 = __ffma2_rn(make_float2(t.x, t.y), make_float2(t.x, t.y), n2);
-      n2 = __ffma2_rn(make_float2(t.z, t.w), make_float2(t.z, t.w), n2);
     }
-    const float scale = n2.x + n2.y + Book::cmax2();
-    const float inf = __int_as_float(0x7f800000);
-    float f[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) f[e] = inf;
-    float fb = inf;
-    for (uint32_t m = cand; m; m &= m - 1u) {
-      const int e = __ffs(m) - 1;
-      const float* ce = sbk + e * G;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-      for (int kc = 0; kc < G / 4; ++kc) {
-        const float4 c4 = *reinterpret_cast<const float4*>(ce + 4 * kc);
-        a0 = fmaf(xr[4 * kc], c4.x, a0);
-        a1 = fmaf(xr[4 * kc + 1], c4.y, a1);
-        a2 = fmaf(xr[4 * kc + 2], c4.z, a2);
-        a3 = fmaf(xr[4 * kc + 3], c4.w, a3);
-      }
-      const float fe = fmaf(-2.f, (a0 + a1) + (a2 + a3), sq[e]);
-      fb = fminf(fb, fe);
-#pragma unroll
-      for (int t = 0; t < 16; ++t) f[t] = t == e ? fe : f[t];
-    }
-    const float thr = fmaf(2.f, fmaf(kappa2, scale, 1e-37f), fb);
-    uint32_t c2 = 0;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) c2 |= uint32_t(f[e] <= thr) << e;
-    c2 &= cand;
-    uint32_t idx;
-    if (finite32(thr) && c2 != 0u && (c2 & (c2 - 1u)) == 0u)
-      idx = uint32_t(__ffs(c2) - 1);
-    else
-      idx = enc_exact_mem<G, Book>(x + v * G, G, finite32(thr) && c2 ? c2 : cand);
+    bool exact;
+    const uint32_t idx = enc_vector<G, Book, true>(xr, &exact, src);
     if (idx) atomicOr(codes + v / 8, idx << (4 * uint32_t(v % 8)));
   }
   __syncwarp();
@@ -374,12 +338,9 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem) + 1023) & ~uintptr_t(1023));
   unsigned char* ring = base;
   unsigned char* bmat = base + S * K::kTile;             // 16 tf32 book rows, swizzled
-  float* sbk = reinterpret_cast<float*>(bmat + 4096);    // the FP32 book, row-major
-  float* sq = sbk + 16 * G;                               // its 16 squared norms
   __shared__ __align__(8) uint64_t full[S], sfree[S], done[C], afree[C];
   __shared__ uint32_t tmem_base;
   __shared__ uint32_t q_vec[4 * C][kCap];  // vector indices (below 2^31 on this path)
-  __shared__ uint32_t q_cand[4 * C][kCap];
   const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
   const uint64_t vectors = (n + G - 1) / G, complete = n / G, words = (vectors + 7) / 8;
   const uint64_t tiles = (vectors + 128 * H - 1) / (128 * H);
@@ -416,10 +377,8 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       *reinterpret_cast<float4*>(bmat + W::off(16 + e, kc)) =
           make_float4(tc::tf32_rna(c[0] - hi[0]), tc::tf32_rna(c[1] - hi[1]), tc::tf32_rna(c[2] - hi[2]),
                       tc::tf32_rna(c[3] - hi[3]));
-    *reinterpret_cast<float4*>(sbk + e * G + kc * 4) = make_float4(c[0], c[1], c[2], c[3]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
   }
-  if (tid < 4) *reinterpret_cast<float4*>(sq + 4 * tid) = Book::metaq(int(tid));
   if (blockIdx.x == 0 && tid == 0 && Book::bad()) atomicOr(status, kNonfinite);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -612,7 +571,6 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           if (defer) {
             const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
             q_vec[warp][pos] = uint32_t(v);
-            q_cand[warp][pos] = cand;
           }
           qtail += __popc(dm);
           const uint32_t w = pack_nibbles(idx);
@@ -636,14 +594,13 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
       if (taken % K::kFlush == 0 || qtail - qhead > kCap - 32u * H) {
         while (qtail != qhead) {
           const uint32_t cnt = min(kChunk, qtail - qhead);
-          tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, cnt, sbk, sq, lane);
+          tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], qhead, cnt, lane);
           qhead += cnt;
         }
       }
     }
     for (; ok && qtail != qhead; qhead += min(kChunk, qtail - qhead))
-      tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], q_cand[warp], qhead, min(kChunk, qtail - qhead), sbk,
-                                      sq, lane);
+      tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], qhead, min(kChunk, qtail - qhead), lane);
     if (!ok) atomicOr(status, kStalled);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

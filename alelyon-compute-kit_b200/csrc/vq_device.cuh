@@ -182,7 +182,9 @@ __device__ __noinline__ uint32_t enc_exact_mem(const float* x, int valid, uint32
 // `src`, when not null, is where x lives in memory: the rare exact pass then
 // reads the vector from there, so the values need not stay in registers
 // after the filter.
-template <int G, class Book>
+// MEM: `src` is never null, so the register copy of x is never needed by the
+// exact pass and stays out of local memory.
+template <int G, class Book, bool MEM = false>
 __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], bool* certified, const float* src = nullptr) {
   // acc[p] = (x.c_2p, x.c_2p+1): one packed FMA per component and entry pair,
   // each lane rounded like fmaf, components in order
@@ -231,7 +233,7 @@ __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], bool* certif
     return uint32_t(__ffs(cand) - 1);
   }
   *certified = true;
-  if (src) return enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
+  if (MEM || src) return enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
   return enc_exact<G, Book>(x, G, clean ? cand : 0xffffu);
 }
 
