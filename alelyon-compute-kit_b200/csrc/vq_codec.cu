@@ -547,9 +547,26 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
               eps = fmaf(kappa1, nx + Book::cmax2(), 0x1p-118f);
             }
             const float thr = fmaf(2.f, eps, fb);
+            // f_e <= thr as the sign of thr - f_e (one packed FMA a pair; the
+            // sign of a rounded difference is exact, and a zero difference
+            // is +0), the 16 sign bits collected by funnel shifts in two
+            // chains of 8: bit e of `over` is set iff f_e > thr. A NaN f_e
+            // leaves `clean` false below, so its unspecified sign never counts.
+            {
+              uint32_t over_lo = 0, over_hi = 0;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
-            cand &= Book::uniq();
+              for (int p = 3; p >= 0; --p) {
+                const float2 d = __ffma2_rn(make_float2(f[2 * p], f[2 * p + 1]), make_float2(-1.f, -1.f),
+                                            make_float2(thr, thr));
+                over_lo = __funnelshift_l(__float_as_uint(d.y), over_lo, 1);
+                over_lo = __funnelshift_l(__float_as_uint(d.x), over_lo, 1);
+                const float2 u = __ffma2_rn(make_float2(f[2 * p + 8], f[2 * p + 9]), make_float2(-1.f, -1.f),
+                                            make_float2(thr, thr));
+                over_hi = __funnelshift_l(__float_as_uint(u.y), over_hi, 1);
+                over_hi = __funnelshift_l(__float_as_uint(u.x), over_hi, 1);
+              }
+              cand = ~((over_hi << 8) | over_lo) & Book::uniq();
+            }
             const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
             if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
               idx = uint32_t(__ffs(cand) - 1);
