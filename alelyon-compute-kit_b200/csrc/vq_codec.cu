@@ -498,9 +498,12 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           }
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        // the pair's certificates: all arithmetic first, in one branch-free
+        // block, so the two vectors' dependency chains interleave
+        uint32_t cand[HP];
+        bool clean[HP];
 #pragma unroll
         for (int hp = 0; hp < HP; ++hp) {
-          const int h = h0 + hp;
           if constexpr (K::TIGHT) {
 #pragma unroll
             for (int e = 0; e < 16; e += 2) {
@@ -510,91 +513,112 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
               r[hp][e + 1] = __float_as_uint(t.y);
             }
           }
-          const uint64_t vbase = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h * 128;
-          const uint64_t v = vbase + row;
           const float nx = n2[hp].x + n2[hp].y;
-          uint32_t idx = 0, bits = 0, cand = 0;
-          bool defer = false;
+          float f[16];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            const float2 t = __ffma2_rn(make_float2(-2.f, -2.f),
+                                        make_float2(__uint_as_float(r[hp][2 * p]), __uint_as_float(r[hp][2 * p + 1])),
+                                        Book::qpair(p));
+            f[2 * p] = t.x;
+            f[2 * p + 1] = t.y;
+          }
+          float lo[8];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
+#pragma unroll
+          for (int w = 4; w; w >>= 1)
+#pragma unroll
+            for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
+          const float fb = lo[0];
+          float eps;
+          if constexpr (K::TIGHT && !K::RESID) {
+            // x truncated (2^-10) against the exactly represented book
+            eps = fmaf(1.0f / 1024 + kappa_t, nx + Book::cmax2(), 0x1p-118f);
+          } else if constexpr (K::RESID) {
+            // 2 ||r|| max||c|| (rounded up, 2^-16 margin for the FP32 sum of
+            // squares) + the accumulation, book-remainder, rounding and
+            // flushed-subnormal terms
+            const float rc = __fsqrt_ru(__fmul_ru(r2[hp].x + r2[hp].y, Book::cmax2()));
+            eps = fmaf(2.0f + 0x1p-15f, rc, fmaf(kappa_t, nx + Book::cmax2(), 0x1p-118f));
+          } else {
+            eps = fmaf(kappa1, nx + Book::cmax2(), 0x1p-118f);
+          }
+          const float thr = fmaf(2.f, eps, fb);
+          // f_e <= thr as the sign of thr - f_e (one packed FMA a pair; the
+          // sign of a rounded difference is exact, and a zero difference
+          // is +0), the 16 sign bits collected by funnel shifts in two
+          // chains of 8: bit e of `over` is set iff f_e > thr. A NaN f_e
+          // leaves `clean` false, so its unspecified sign never counts.
+          uint32_t over_lo = 0, over_hi = 0;
+#pragma unroll
+          for (int p = 3; p >= 0; --p) {
+            const float2 d = __ffma2_rn(make_float2(f[2 * p], f[2 * p + 1]), make_float2(-1.f, -1.f),
+                                        make_float2(thr, thr));
+            over_lo = __funnelshift_l(__float_as_uint(d.y), over_lo, 1);
+            over_lo = __funnelshift_l(__float_as_uint(d.x), over_lo, 1);
+            const float2 u = __ffma2_rn(make_float2(f[2 * p + 8], f[2 * p + 9]), make_float2(-1.f, -1.f),
+                                        make_float2(thr, thr));
+            over_hi = __funnelshift_l(__float_as_uint(u.y), over_hi, 1);
+            over_hi = __funnelshift_l(__float_as_uint(u.x), over_hi, 1);
+          }
+          cand[hp] = ~((over_hi << 8) | over_lo) & Book::uniq();
+          clean[hp] = finite32(thr) && finite32(fb) && !Book::bad();
+        }
+        // then the outcomes: a single candidate is the answer; several are
+        // queued for the refinement; the rest (nonfinite input, the partial
+        // last vector) take the float64 pass now
+        uint32_t idx[HP], bits = 0;
+        bool defer[HP];
+        const uint64_t vbase0 = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h0 * 128;
+#pragma unroll
+        for (int hp = 0; hp < HP; ++hp) {
+          const uint64_t v = vbase0 + hp * 128 + row;
+          const uint32_t c = cand[hp];
+          idx[hp] = 0;
+          defer[hp] = false;
           if (v < complete) {
-            float f[16];
-#pragma unroll
-            for (int p = 0; p < 8; ++p) {
-              const float2 t = __ffma2_rn(make_float2(-2.f, -2.f),
-                                          make_float2(__uint_as_float(r[hp][2 * p]), __uint_as_float(r[hp][2 * p + 1])),
-                                          Book::qpair(p));
-              f[2 * p] = t.x;
-              f[2 * p + 1] = t.y;
-            }
-            float lo[8];
-#pragma unroll
-            for (int p = 0; p < 8; ++p) lo[p] = fminf(f[2 * p], f[2 * p + 1]);
-#pragma unroll
-            for (int w = 4; w; w >>= 1)
-#pragma unroll
-              for (int p = 0; p < w; ++p) lo[p] = fminf(lo[p], lo[p + w]);
-            const float fb = lo[0];
-            float eps;
-            if constexpr (K::TIGHT && !K::RESID) {
-              // x truncated (2^-10) against the exactly represented book
-              eps = fmaf(1.0f / 1024 + kappa_t, nx + Book::cmax2(), 0x1p-118f);
-            } else if constexpr (K::RESID) {
-              // 2 ||r|| max||c|| (rounded up, 2^-16 margin for the FP32 sum of
-              // squares) + the accumulation, book-remainder, rounding and
-              // flushed-subnormal terms
-              const float rc = __fsqrt_ru(__fmul_ru(r2[hp].x + r2[hp].y, Book::cmax2()));
-              eps = fmaf(2.0f + 0x1p-15f, rc, fmaf(kappa_t, nx + Book::cmax2(), 0x1p-118f));
-            } else {
-              eps = fmaf(kappa1, nx + Book::cmax2(), 0x1p-118f);
-            }
-            const float thr = fmaf(2.f, eps, fb);
-            // f_e <= thr as the sign of thr - f_e (one packed FMA a pair; the
-            // sign of a rounded difference is exact, and a zero difference
-            // is +0), the 16 sign bits collected by funnel shifts in two
-            // chains of 8: bit e of `over` is set iff f_e > thr. A NaN f_e
-            // leaves `clean` false below, so its unspecified sign never counts.
-            {
-              uint32_t over_lo = 0, over_hi = 0;
-#pragma unroll
-              for (int p = 3; p >= 0; --p) {
-                const float2 d = __ffma2_rn(make_float2(f[2 * p], f[2 * p + 1]), make_float2(-1.f, -1.f),
-                                            make_float2(thr, thr));
-                over_lo = __funnelshift_l(__float_as_uint(d.y), over_lo, 1);
-                over_lo = __funnelshift_l(__float_as_uint(d.x), over_lo, 1);
-                const float2 u = __ffma2_rn(make_float2(f[2 * p + 8], f[2 * p + 9]), make_float2(-1.f, -1.f),
-                                            make_float2(thr, thr));
-                over_hi = __funnelshift_l(__float_as_uint(u.y), over_hi, 1);
-                over_hi = __funnelshift_l(__float_as_uint(u.x), over_hi, 1);
-              }
-              cand = ~((over_hi << 8) | over_lo) & Book::uniq();
-            }
-            const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
-            if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
-              idx = uint32_t(__ffs(cand) - 1);
-            } else if (clean && cand != 0u) {
-              defer = true;
+            if (clean[hp] && c != 0u && (c & (c - 1u)) == 0u) {
+              idx[hp] = uint32_t(__ffs(c) - 1);
+            } else if (clean[hp] && c != 0u) {
+              defer[hp] = true;
             } else {
               const float* src = x + v * G;
               for (int j = 0; j < G; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
-              idx = enc_exact_mem<G, Book>(src, G, clean ? cand : 0xffffu);
+              idx[hp] = enc_exact_mem<G, Book>(src, G, clean[hp] ? c : 0xffffu);
             }
           } else if (v < vectors) {
             // the partial last vector: its valid components only (vq.py:171-172)
             const int valid = int(n - v * G);
             const float* src = x + v * G;
             for (int j = 0; j < valid; ++j) bits |= finite32(src[j]) ? 0u : kNonfinite;
-            idx = enc_exact_mem<G, Book>(src, valid, 0xffffu);
+            idx[hp] = enc_exact_mem<G, Book>(src, valid, 0xffffu);
           }
-          const uint32_t dm = __ballot_sync(0xffffffffu, defer);
-          if (defer) {
+        }
+#pragma unroll
+        for (int hp = 0; hp < HP; ++hp) {
+          const uint32_t dm = __ballot_sync(0xffffffffu, defer[hp]);
+          if (defer[hp]) {
             const uint32_t pos = (qtail + __popc(dm & ((1u << lane) - 1u))) & (kCap - 1);
-            q_vec[warp][pos] = uint32_t(v);
+            q_vec[warp][pos] = uint32_t(vbase0 + hp * 128 + row);
           }
           qtail += __popc(dm);
-          const uint32_t w = pack_nibbles(idx);
-          const uint64_t word = (vbase + wq * 32) / 8 + lane / 8;
-          if ((lane & 7) == 0 && word < words) codes[word] = w;
-          flag_warp(status, bits);
         }
+        // OR the nibbles of the 8 lanes that share a code word, both vectors'
+        // shuffles interleaved
+        uint32_t wd[HP];
+#pragma unroll
+        for (int hp = 0; hp < HP; ++hp) wd[hp] = idx[hp] << (4u * (lane & 7u));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+          for (int hp = 0; hp < HP; ++hp) wd[hp] |= __shfl_xor_sync(0xffffffffu, wd[hp], o);
+#pragma unroll
+        for (int hp = 0; hp < HP; ++hp) {
+          const uint64_t word = (vbase0 + hp * 128 + wq * 32) / 8 + lane / 8;
+          if ((lane & 7) == 0 && word < words) codes[word] = wd[hp];
+        }
+        flag_warp(status, bits);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
