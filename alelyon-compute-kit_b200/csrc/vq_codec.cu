@@ -498,6 +498,17 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           }
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (h0 + HP == H) {
+          // the tile's accumulator and stage are read (TMEM into registers,
+          // the norms from the tile): release both now, so the next load and
+          // MMA into them run while this warp certifies
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tc::mb_arrive(&afree[q]);
+            tc::mb_arrive(&sfree[s]);
+          }
+        }
         // the pair's certificates: all arithmetic first, in one branch-free
         // block, so the two vectors' dependency chains interleave
         uint32_t cand[HP];
@@ -619,12 +630,6 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           if ((lane & 7) == 0 && word < words) codes[word] = wd[hp];
         }
         flag_warp(status, bits);
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        tc::mb_arrive(&afree[q]);
-        tc::mb_arrive(&sfree[s]);
       }
       // Refine off the pipeline's critical path, kChunk vectors at a time. The
       // four warps of a quad flush at the same tiles (every kFlush of the
