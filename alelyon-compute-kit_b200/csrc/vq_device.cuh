@@ -223,10 +223,21 @@ __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], bool* certif
   constexpr float kappa = float(G + 8) * (1.0f / 8388608.0f);
   const float eps = fmaf(kappa, nx2 + Book::cmax2(), 1e-37f);
   const float thr = fmaf(2.f, eps, fb);
-  uint32_t cand = 0;
+  // f_e <= thr as the sign of thr - f_e (exact for a rounded difference; a
+  // zero difference is +0), gathered by funnel shifts: bit e of `over` is set
+  // iff f_e > thr. A NaN f_e leaves `clean` false, where the mask is unused.
+  uint32_t over_lo = 0, over_hi = 0;
 #pragma unroll
-  for (int e = 0; e < 16; ++e) cand |= uint32_t(f[e] <= thr) << e;
-  cand &= Book::uniq();
+  for (int p = 3; p >= 0; --p) {
+    const float2 d = __ffma2_rn(make_float2(f[2 * p], f[2 * p + 1]), make_float2(-1.f, -1.f), make_float2(thr, thr));
+    over_lo = __funnelshift_l(__float_as_uint(d.y), over_lo, 1);
+    over_lo = __funnelshift_l(__float_as_uint(d.x), over_lo, 1);
+    const float2 u =
+        __ffma2_rn(make_float2(f[2 * p + 8], f[2 * p + 9]), make_float2(-1.f, -1.f), make_float2(thr, thr));
+    over_hi = __funnelshift_l(__float_as_uint(u.y), over_hi, 1);
+    over_hi = __funnelshift_l(__float_as_uint(u.x), over_hi, 1);
+  }
+  const uint32_t cand = ~((over_hi << 8) | over_lo) & Book::uniq();
   const bool clean = finite32(thr) && finite32(fb) && !Book::bad();
   if (clean && cand != 0u && (cand & (cand - 1u)) == 0u) {
     *certified = false;
