@@ -458,8 +458,10 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     constexpr float kappa_t = float(G + 9) / 2097152.0f;  // TIGHT: all but the x residual
     uint32_t qhead = 0, qtail = 0;
     constexpr uint32_t kChunk = 32u;  // queued vectors refined together (one per lane)
+    uint32_t bits = 0;                // nonfinite inputs seen, flagged once when the warp is done
     for (uint32_t k = q; k < T && ok && stall_test != 2; k += C) {
       const uint32_t s = k % S;
+      const uint64_t vtile = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H;  // the tile's first vector
       // warp-uniform outcomes: tcgen05.ld below is .sync.aligned
       if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&full[s], (k / S) & 1, lim)))) break;
       if (!(ok = __all_sync(0xffffffffu, tc::mb_wait(&done[q], (k / C) & 1, lim)))) break;
@@ -579,9 +581,9 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
         // then the outcomes: a single candidate is the answer; several are
         // queued for the refinement; the rest (nonfinite input, the partial
         // last vector) take the float64 pass now
-        uint32_t idx[HP], bits = 0;
+        uint32_t idx[HP];
         bool defer[HP];
-        const uint64_t vbase0 = (blockIdx.x + uint64_t(k) * gridDim.x) * 128 * H + h0 * 128;
+        const uint64_t vbase0 = vtile + h0 * 128;
 #pragma unroll
         for (int hp = 0; hp < HP; ++hp) {
           const uint64_t v = vbase0 + hp * 128 + row;
@@ -629,7 +631,6 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           const uint64_t word = (vbase0 + hp * 128 + wq * 32) / 8 + lane / 8;
           if ((lane & 7) == 0 && word < words) codes[word] = wd[hp];
         }
-        flag_warp(status, bits);
       }
       // Refine off the pipeline's critical path, kChunk vectors at a time. The
       // four warps of a quad flush at the same tiles (every kFlush of the
@@ -647,6 +648,7 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
     }
     for (; ok && qtail != qhead; qhead += min(kChunk, qtail - qhead))
       tc::refine_queue<G, Book, kCap>(x, codes, q_vec[warp], qhead, min(kChunk, qtail - qhead), lane);
+    flag_warp(status, bits);
     if (!ok) atomicOr(status, kStalled);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
