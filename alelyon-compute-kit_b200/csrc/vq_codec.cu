@@ -249,10 +249,17 @@ __global__ void __launch_bounds__(kThreads, 3) k_encode_async(const float* __res
 // flushed subnormal products). The float64 winner lies in
 // {e : f'_e <= min f' + 2 eps1} minus duplicate rows; one entry left is the
 // answer. Otherwise (a few per cent of vectors on smooth data) the vector
-// joins its warp's queue and is refined later: the FP32 filter of enc_vector
-// (its bound kappa2 = (G + 8) 2^-23) over those candidates only, then the
-// float64 pass over what survives, the result OR-ed into the zero nibble the
-// first pass stored. Nonfinite input or books take the float64 pass at once.
+// joins its warp's queue and is refined later: enc_vector's FP32 filter over
+// all 16 entries (its bound kappa2 = (G + 8) 2^-23), then the float64 pass
+// over what survives, the result OR-ed into the zero nibble the first pass
+// stored. Nonfinite input or books take the float64 pass at once.
+//
+// Schedule. A consumer warp takes its quad's tiles in turn: it loads a pair
+// of sub-tiles' accumulators under one wait, releases the stage and the
+// accumulator once the tile's last loads have landed (so the next TMA load
+// and MMA run while it certifies), certifies the pair in one branch-free
+// block, then stores the code words. A quad's four warps flush their queues
+// at the same tiles.
 //
 // Group 32 tightens the bound (Cfg::TIGHT, Cfg::RESID): the book enters as
 // tf32 hi and lo halves (N = 32, summed), so only x is truncated, and that
