@@ -566,10 +566,11 @@ __global__ void __launch_bounds__(tc::Cfg<G>::kThreads, tc::Cfg<G>::kBlocksPerSm
           }
           const float thr = fmaf(2.f, eps, fb);
           // f_e <= thr as the sign of thr - f_e (one packed FMA a pair; the
-          // sign of a rounded difference is exact, and a zero difference
-          // is +0), the 16 sign bits collected by funnel shifts in two
-          // chains of 8: bit e of `over` is set iff f_e > thr. A NaN f_e
-          // leaves `clean` false, so its unspecified sign never counts.
+          // sign of a rounded difference is exact, and a zero difference is
+          // +0 since thr = fb + 2 eps with eps > 0 is never -0), the 16 sign
+          // bits collected by funnel shifts in two chains of 8: bit e of
+          // `over` is set iff f_e > thr. A NaN f_e leaves `clean` false, so
+          // its unspecified sign never counts.
           uint32_t over_lo = 0, over_hi = 0;
 #pragma unroll
           for (int p = 3; p >= 0; --p) {

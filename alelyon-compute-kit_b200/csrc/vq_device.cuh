@@ -224,7 +224,8 @@ __device__ __forceinline__ uint32_t enc_vector(const float (&x)[G], bool* certif
   const float eps = fmaf(kappa, nx2 + Book::cmax2(), 1e-37f);
   const float thr = fmaf(2.f, eps, fb);
   // f_e <= thr as the sign of thr - f_e (exact for a rounded difference; a
-  // zero difference is +0), gathered by funnel shifts: bit e of `over` is set
+  // zero difference is +0, since thr = fb + 2 eps with eps > 0 is never -0),
+  // gathered by funnel shifts: bit e of `over` is set
   // iff f_e > thr. A NaN f_e leaves `clean` false, where the mask is unused.
   uint32_t over_lo = 0, over_hi = 0;
 #pragma unroll
