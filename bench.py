@@ -17,15 +17,20 @@ headline metric is coded-weight GB/s = (code bytes + codebook bytes) / time.
            the CPU restatement (decode + dot product, all host threads) on a
            bounded sample of the same experts
 
-Other workloads (`--workload`): cfg2-m4/m16/m64 (same, M rows), cfg3 (both
+Other workloads: cfg2 at M rows (`--m 4/16/64`), and `--workload` cfg3 (both
 operands coded, 4096 x 4096 times 14336 x 4096, g32), cfg4 (fused VQAdamW,
-8 experts of 3 x 4096 x 1024 g8 per GPU), encode / decode (2^30 values).
+8 experts of 3 x 4096 x 1024 g8 per GPU), encode / decode (2^30 values,
+`--group`, `--dist`), nf4 (the NF4 comparator's GEMV on the cfg2 shape) and
+profile (small cases of every kernel, for ncu captures; no timing). The
+default run carries all of them in the line's `secondary` object.
 
 Multi-GPU (torchrun): every rank runs its own E experts (expert sharding,
 no collective, weak scaling); the reported time is the max over ranks. The
 line's `sharded` object adds the row splits of cfg2 and cfg3 across ranks
-(strong scaling) without and with the NCCL all-gather of the output, and the
-cfg4 VQAdamW step at 8 experts per GPU.
+(strong scaling) without and with the NCCL all-gather of the output, cfg2
+with the GEMV storing its outputs into every rank's buffer over NVLink (CUDA
+IPC peer stores) instead of the all-gather, and the cfg4 VQAdamW step at 8
+experts per GPU.
 """
 from __future__ import annotations
 
